@@ -1,0 +1,621 @@
+// dmoe_api.cu — host side of libdiffuse_moe: the C ABI of include/diffuse_moe.h.
+//
+// dmoe_create   validates the layer (src/diffuse-common.h:59-86,103-118 semantics), uploads the
+//               weights once (library-owned device memory; Q8_0 repacked losslessly into an
+//               int8 quant plane + fp32 scale plane so TMA can 128B-swizzle the quants), builds
+//               the TMA descriptors of every weight tensor.
+// dmoe_forward  enqueues the layer on one stream:
+//               router logits -> routing -> scan / token tiles -> gather -> gate/up GEMM ->
+//               down GEMM (src/diffuse-moe-graph.cpp:195-287).
+// No CPU fallback: a missing device or a failed launch is reported, never worked around.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/diffuse_moe.h"
+#include "dmoe_internal.h"
+
+using namespace dmoe;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+dmoe_status fail(dmoe_status st, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return st;
+}
+
+#define DMOE_CUDA(call)                                                                              \
+  do {                                                                                               \
+    cudaError_t e_ = (call);                                                                         \
+    if (e_ != cudaSuccess) return fail(DMOE_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled get_encode_tiled() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [outer][inner] of `dt` elements, row pitch `pitch_bytes`.
+dmoe_status make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (!enc) return fail(DMOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): inner=%llu outer=%llu pitch=%llu box=%u,%u",
+                (int)r, (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)pitch_bytes,
+                box_inner, box_outer);
+  return DMOE_OK;
+}
+
+bool type_supported(int32_t t) { return t == DMOE_TYPE_F16 || t == DMOE_TYPE_Q8_0 || t == DMOE_TYPE_Q4_K; }
+
+// A weight matrix family on the device: `nmat` matrices of rows x k, in the kernel layout.
+struct DevWeight {
+  int32_t type = -1;
+  int64_t rows = 0;  // total rows (all experts)
+  int64_t k = 0;
+  void* q = nullptr;      // F16 / Q4_K bytes as in GGUF; Q8_0 int8 quant plane [rows][k]
+  float* s = nullptr;     // Q8_0 fp32 scale plane [rows][k / 32]
+  CUtensorMap tm_q;
+  CUtensorMap tm_s;
+};
+
+dmoe_status upload_weight(DevWeight& w, int32_t type, const void* host, int64_t rows, int64_t k) {
+  w.type = type;
+  w.rows = rows;
+  w.k = k;
+  const size_t rs = row_size(type, k);
+  if (rs == 0) return fail(DMOE_ERR_UNSUPPORTED, "row of %lld values is not a whole number of type-%d blocks",
+                           (long long)k, type);
+  if (type == DMOE_TYPE_Q8_0) {
+    if (cudaMalloc(&w.q, (size_t)rows * k) != cudaSuccess) return fail(DMOE_ERR_OOM, "cudaMalloc q8_0 quants");
+    if (cudaMalloc(&w.s, (size_t)rows * (k / 32) * 4) != cudaSuccess) return fail(DMOE_ERR_OOM, "cudaMalloc scales");
+    // repack in chunks of rows: {f16 d; int8 q[32]} -> quant plane + fp32 scale plane (lossless)
+    const int64_t chunk = std::max<int64_t>(1, (64ll << 20) / (int64_t)rs);
+    std::vector<int8_t> qb;
+    std::vector<float> sb;
+    for (int64_t r0 = 0; r0 < rows; r0 += chunk) {
+      const int64_t nr = std::min(chunk, rows - r0);
+      qb.resize((size_t)nr * k);
+      sb.resize((size_t)nr * (k / 32));
+      const uint8_t* src = static_cast<const uint8_t*>(host) + (size_t)r0 * rs;
+      for (int64_t r = 0; r < nr; ++r)
+        for (int64_t b = 0; b < k / 32; ++b) {
+          const uint8_t* blk = src + (size_t)r * rs + b * 34;
+          sb[(size_t)r * (k / 32) + b] = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+          std::memcpy(&qb[(size_t)r * k + b * 32], blk + 2, 32);
+        }
+      DMOE_CUDA(cudaMemcpy(static_cast<int8_t*>(w.q) + (size_t)r0 * k, qb.data(), (size_t)nr * k,
+                           cudaMemcpyHostToDevice));
+      DMOE_CUDA(cudaMemcpy(w.s + (size_t)r0 * (k / 32), sb.data(), (size_t)nr * (k / 32) * 4, cudaMemcpyHostToDevice));
+    }
+    dmoe_status st = make_map(&w.tm_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, (uint64_t)k, (uint64_t)rows, (uint64_t)k,
+                              128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DMOE_OK) return st;
+    return make_map(&w.tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.s, (uint64_t)(k / 32), (uint64_t)rows,
+                    (uint64_t)(k / 32) * 4, 4, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (cudaMalloc(&w.q, (size_t)rows * rs) != cudaSuccess) return fail(DMOE_ERR_OOM, "cudaMalloc weights");
+  DMOE_CUDA(cudaMemcpy(w.q, host, (size_t)rows * rs, cudaMemcpyHostToDevice));
+  if (type == DMOE_TYPE_Q4_K)
+    return make_map(&w.tm_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, (uint64_t)rs, (uint64_t)rows, (uint64_t)rs, 144, 128,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  return make_map(&w.tm_q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w.q, (uint64_t)k, (uint64_t)rows, (uint64_t)k * 2, 64,
+                  128, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+void free_weight(DevWeight& w) {
+  if (w.q) cudaFree(w.q);
+  if (w.s) cudaFree(w.s);
+  w.q = nullptr;
+  w.s = nullptr;
+}
+
+template <class T>
+dmoe_status grow(T*& p, size_t& cap, size_t need) {
+  if (need <= cap && p) return DMOE_OK;
+  if (p) cudaFree(p);
+  p = nullptr;
+  cap = 0;
+  const size_t n = std::max<size_t>(need, 1);
+  if (cudaMalloc(reinterpret_cast<void**>(&p), n * sizeof(T)) != cudaSuccess)
+    return fail(DMOE_ERR_OOM, "cudaMalloc workspace (%zu bytes)", n * sizeof(T));
+  cap = n;
+  return DMOE_OK;
+}
+
+}  // namespace
+
+struct dmoe_layer {
+  // shapes / hyper-parameters
+  int64_t H = 0, I = 0, Is = 0, E = 0, K = 0, cap = 0, blk = 0;
+  float scale = 1.0f;
+  int32_t norm_topk = 1;
+  int32_t etype = 0, stype = 0;
+  bool has_shared = false, has_bias = false;
+  int device = 0, sms = 148;
+  cudaStream_t own_stream = nullptr;
+  // weights
+  float* wr = nullptr;
+  float* br = nullptr;
+  DevWeight gate, up, down, sgate, sup, sdown;
+  // workspace (grown, never shrunk)
+  float* parts = nullptr; size_t parts_cap = 0;
+  int32_t* idx = nullptr; size_t idx_cap = 0;
+  float* wts = nullptr; size_t wts_cap = 0;
+  uint8_t* allowed = nullptr; size_t allowed_cap = 0;
+  int32_t* ints = nullptr; size_t ints_cap = 0;  // counts[E] fill[E] off[E] n_tiles n_active
+  TokTile* tiles = nullptr; size_t tiles_cap = 0;
+  __half* xg = nullptr; size_t xg_cap = 0;
+  __half* hbuf = nullptr; size_t hbuf_cap = 0;
+  float* gu = nullptr; size_t gu_cap = 0;
+  int32_t* pair_tok = nullptr; size_t pair_tok_cap = 0;
+  float* pair_w = nullptr; size_t pair_w_cap = 0;
+  float* xdev = nullptr; size_t xdev_cap = 0;
+  float* odev = nullptr; size_t odev_cap = 0;
+  uint32_t* err = nullptr;
+  // statistics
+  dmoe_stats stats{};
+  int32_t* host_counters = nullptr;  // pinned: n_tiles, n_active
+  cudaEvent_t ev[6] = {};
+  bool profiled = false;
+  cudaStream_t last_stream = nullptr;
+};
+
+namespace {
+
+dmoe_status validate(const dmoe_layer_desc* d) {
+  if (!d) return fail(DMOE_ERR_INVALID_ARG, "null layer descriptor");
+  if (d->n_embd <= 0 || d->n_ff_exp <= 0 || d->n_expert <= 0 || d->n_expert_used <= 0 || d->n_ff_shexp < 0)
+    return fail(DMOE_ERR_INVALID_ARG, "non-positive layer dimension");
+  if (d->n_expert_used > 16 || d->n_expert_used > d->n_expert)
+    return fail(DMOE_ERR_INVALID_ARG, "n_expert_used must be <= min(16, n_expert)");
+  if (d->n_expert > 1024) return fail(DMOE_ERR_UNSUPPORTED, "n_expert > 1024");
+  if (d->expert_capacity < 0 || d->moe_block_size < 0) return fail(DMOE_ERR_INVALID_ARG, "negative capacity/block");
+  const int64_t tpb = d->moe_block_size > 1 ? std::max<int64_t>(d->moe_block_size, 32) : 32;
+  if ((2 * tpb * d->n_expert + d->n_expert) * 4 > 200 * 1024)
+    return fail(DMOE_ERR_UNSUPPORTED, "moe_block_size x n_expert too large for the routing kernel");
+  if (!type_supported(d->expert_type)) return fail(DMOE_ERR_UNSUPPORTED, "expert weight type %d", d->expert_type);
+  if (d->n_ff_shexp > 0 && !type_supported(d->shared_type))
+    return fail(DMOE_ERR_UNSUPPORTED, "shared weight type %d", d->shared_type);
+  if (!d->w_gate || !d->w_up || !d->w_down || !d->w_router) return fail(DMOE_ERR_INVALID_ARG, "null weight pointer");
+  if (d->n_ff_shexp > 0 && (!d->sw_gate || !d->sw_up || !d->sw_down))
+    return fail(DMOE_ERR_INVALID_ARG, "null shared-expert weight pointer");
+  auto kmul = [](int32_t t) { return t == DMOE_TYPE_Q4_K ? 256 : 128; };
+  const int64_t H = d->n_embd, I = d->n_ff_exp, Is = d->n_ff_shexp;
+  if (H % 128 || H % kmul(d->expert_type) || I % kmul(d->expert_type))
+    return fail(DMOE_ERR_UNSUPPORTED, "n_embd / n_ff_exp must be multiples of %d for type %d", kmul(d->expert_type),
+                d->expert_type);
+  if (Is > 0 && (H % kmul(d->shared_type) || Is % kmul(d->shared_type)))
+    return fail(DMOE_ERR_UNSUPPORTED, "n_ff_shexp must be a multiple of %d", kmul(d->shared_type));
+  return DMOE_OK;
+}
+
+int pick_nt(const dmoe_layer* L, int64_t n) {
+  const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < L->E && n % L->blk == 0;
+  const int64_t pairs = n * L->K;
+  int64_t active = std::min<int64_t>(L->E, pairs);
+  if (use_block) active = std::min<int64_t>(active, L->cap * (n / L->blk));
+  const double avg = active > 0 ? (double)pairs / (double)active : 0.0;
+  if (avg <= 24.0) return 32;
+  if (avg <= 80.0) return 64;
+  return 128;
+}
+
+// Smallest power-of-two split (<= 8) dividing every K-stage count that gives >= 4 waves.
+int pick_ksplit(int64_t tiles_est, int sms, std::initializer_list<int> kstages) {
+  int best = 1;
+  for (int s = 2; s <= 8; s *= 2) {
+    if (tiles_est * (best) >= 4LL * sms) break;
+    bool ok = true;
+    for (int ks : kstages) ok = ok && ks > 0 && ks % s == 0;
+    if (!ok) break;
+    best = s;
+  }
+  return best;
+}
+
+void fill_group(GemmGroup& g, const DevWeight& w, int32_t type, int64_t rows_per_exp, int64_t n_out_rows) {
+  g.n_mt = (int32_t)(n_out_rows / kMTile);
+  g.k_stages = (int32_t)(w.k / gemm_stage_k(type));
+  g.rows_per_exp = (int32_t)rows_per_exp;
+  g.present = 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t dmoe_abi_version(void) { return DMOE_ABI_VERSION; }
+
+size_t dmoe_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    const size_t n = std::min(len - 1, g_last_error.size());
+    std::memcpy(buf, g_last_error.data(), n);
+    buf[n] = 0;
+  }
+  return g_last_error.size();
+}
+
+dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmoe_layer** out) {
+  if (!out) return fail(DMOE_ERR_INVALID_ARG, "null output handle");
+  *out = nullptr;
+  dmoe_status st = validate(d);
+  if (st != DMOE_OK) return st;
+  if (dist && dist->world_size > 1)
+    return fail(DMOE_ERR_UNSUPPORTED, "expert parallelism (world_size %d) is not available in this build",
+                dist->world_size);
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    return fail(DMOE_ERR_NO_DEVICE, "no CUDA device (libdiffuse_moe has no CPU fallback)");
+  }
+  dmoe_layer* L = new dmoe_layer();
+  L->device = dist ? dist->device : 0;
+  if (L->device < 0 || L->device >= ndev) {
+    delete L;
+    return fail(DMOE_ERR_INVALID_ARG, "device %d out of range", dist ? dist->device : 0);
+  }
+  auto bail = [&](dmoe_status s) {
+    dmoe_destroy(L);
+    return s;
+  };
+  if (cudaSetDevice(L->device) != cudaSuccess) return bail(fail(DMOE_ERR_CUDA, "cudaSetDevice"));
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, L->device) != cudaSuccess) return bail(fail(DMOE_ERR_CUDA, "device props"));
+  if (prop.major != 10) return bail(fail(DMOE_ERR_UNSUPPORTED, "device sm_%d%d is not sm_100", prop.major, prop.minor));
+  L->sms = prop.multiProcessorCount;
+  L->H = d->n_embd;
+  L->I = d->n_ff_exp;
+  L->Is = d->n_ff_shexp;
+  L->E = d->n_expert;
+  L->K = d->n_expert_used;
+  L->cap = d->expert_capacity;
+  L->blk = d->moe_block_size;
+  L->scale = d->routed_scaling;
+  L->norm_topk = d->norm_topk_prob;
+  L->etype = d->expert_type;
+  L->stype = d->shared_type;
+  L->has_shared = d->n_ff_shexp > 0;
+  L->has_bias = d->b_router != nullptr;
+  if (cudaStreamCreateWithFlags(&L->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+    return bail(fail(DMOE_ERR_CUDA, "stream create"));
+  for (auto& e : L->ev)
+    if (cudaEventCreate(&e) != cudaSuccess) return bail(fail(DMOE_ERR_CUDA, "event create"));
+  if (cudaMalloc(&L->wr, (size_t)L->E * L->H * 4) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "router alloc"));
+  if (cudaMemcpy(L->wr, d->w_router, (size_t)L->E * L->H * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(fail(DMOE_ERR_CUDA, "router upload"));
+  if (L->has_bias) {
+    if (cudaMalloc(&L->br, (size_t)L->E * 4) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "bias alloc"));
+    if (cudaMemcpy(L->br, d->b_router, (size_t)L->E * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(fail(DMOE_ERR_CUDA, "bias upload"));
+  }
+  if ((st = upload_weight(L->gate, L->etype, d->w_gate, L->E * L->I, L->H)) != DMOE_OK) return bail(st);
+  if ((st = upload_weight(L->up, L->etype, d->w_up, L->E * L->I, L->H)) != DMOE_OK) return bail(st);
+  if ((st = upload_weight(L->down, L->etype, d->w_down, L->E * L->H, L->I)) != DMOE_OK) return bail(st);
+  if (L->has_shared) {
+    if ((st = upload_weight(L->sgate, L->stype, d->sw_gate, L->Is, L->H)) != DMOE_OK) return bail(st);
+    if ((st = upload_weight(L->sup, L->stype, d->sw_up, L->Is, L->H)) != DMOE_OK) return bail(st);
+    if ((st = upload_weight(L->sdown, L->stype, d->sw_down, L->H, L->Is)) != DMOE_OK) return bail(st);
+  }
+  if (cudaMalloc(&L->err, 64) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "err alloc"));
+  if (cudaMemset(L->err, 0, 64) != cudaSuccess) return bail(fail(DMOE_ERR_CUDA, "err memset"));
+  if (cudaMallocHost(&L->host_counters, 64) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "pinned alloc"));
+  std::memset(L->host_counters, 0, 64);
+  *out = L;
+  return DMOE_OK;
+}
+
+void dmoe_destroy(dmoe_layer* L) {
+  if (!L) return;
+  cudaSetDevice(L->device);
+  if (L->own_stream) cudaStreamSynchronize(L->own_stream);
+  if (L->last_stream) cudaStreamSynchronize(L->last_stream);
+  cudaFree(L->wr);
+  cudaFree(L->br);
+  for (DevWeight* w : {&L->gate, &L->up, &L->down, &L->sgate, &L->sup, &L->sdown}) free_weight(*w);
+  cudaFree(L->parts);
+  cudaFree(L->idx);
+  cudaFree(L->wts);
+  cudaFree(L->allowed);
+  cudaFree(L->ints);
+  cudaFree(L->tiles);
+  cudaFree(L->xg);
+  cudaFree(L->hbuf);
+  cudaFree(L->gu);
+  cudaFree(L->pair_tok);
+  cudaFree(L->pair_w);
+  cudaFree(L->xdev);
+  cudaFree(L->odev);
+  cudaFree(L->err);
+  if (L->host_counters) cudaFreeHost(L->host_counters);
+  for (auto& e : L->ev)
+    if (e) cudaEventDestroy(e);
+  if (L->own_stream) cudaStreamDestroy(L->own_stream);
+  delete L;
+}
+
+dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, const dmoe_route_out* route,
+                         void* stream, uint32_t flags) {
+  if (!L) return fail(DMOE_ERR_INVALID_ARG, "null layer");
+  if (n < 0 || (n > 0 && !x)) return fail(DMOE_ERR_INVALID_ARG, "bad input");
+  const bool route_only = flags & DMOE_F_ROUTE_ONLY;
+  const bool host = flags & DMOE_F_HOST_PTRS;
+  const bool prof = flags & DMOE_F_PROFILE;
+  if (!route_only && n > 0 && !out) return fail(DMOE_ERR_INVALID_ARG, "null output");
+  if (n * (1 + L->K) >= (1ll << 31)) return fail(DMOE_ERR_UNSUPPORTED, "too many tokens in one call");
+  DMOE_CUDA(cudaSetDevice(L->device));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : L->own_stream;
+  L->last_stream = st;
+  L->profiled = prof;
+  std::memset(&L->stats, 0, sizeof(L->stats));
+  if (n == 0) return DMOE_OK;
+
+  const int64_t H = L->H, E = L->E, K = L->K;
+  const int64_t rows = n * (1 + K);  // shared segment [0, n) + routed pairs
+  const int64_t Imax = std::max(L->I, L->Is);
+  const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;
+  const int nseg = (int)((H + kRouterSeg - 1) / kRouterSeg);
+  const int64_t rl_ctas = ((n + 31) / 32) * ((E + 63) / 64);
+  const int nparts = rl_ctas < 2LL * L->sms ? nseg : 1;
+  const int nt = pick_nt(L, n);
+
+  dmoe_status s;
+  size_t dummy_cap;
+  (void)dummy_cap;
+  if ((s = grow(L->parts, L->parts_cap, (size_t)nparts * n * E)) != DMOE_OK) return s;
+  if ((s = grow(L->idx, L->idx_cap, (size_t)n * K)) != DMOE_OK) return s;
+  if ((s = grow(L->wts, L->wts_cap, (size_t)n * K)) != DMOE_OK) return s;
+  if ((s = grow(L->ints, L->ints_cap, (size_t)3 * E + 8)) != DMOE_OK) return s;
+  if (use_block && (s = grow(L->allowed, L->allowed_cap, (size_t)(n / L->blk) * E)) != DMOE_OK) return s;
+  int32_t* counts = L->ints;
+  int32_t* fill = L->ints + E;
+  int32_t* off = L->ints + 2 * E;
+  int32_t* n_tiles = L->ints + 3 * E;
+  int32_t* n_active = n_tiles + 1;
+
+  const float* xd = x;
+  float* od = out;
+  if (host) {
+    if ((s = grow(L->xdev, L->xdev_cap, (size_t)n * H)) != DMOE_OK) return s;
+    DMOE_CUDA(cudaMemcpyAsync(L->xdev, x, (size_t)n * H * 4, cudaMemcpyHostToDevice, st));
+    xd = L->xdev;
+    if (!route_only) {
+      if ((s = grow(L->odev, L->odev_cap, (size_t)n * H)) != DMOE_OK) return s;
+      od = L->odev;
+    }
+  }
+  int kernels = 0;
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[0], st));
+
+  // ---- router (src/diffuse-moe-graph.cpp:203-262)
+  DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)E, st));
+  DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, nparts, st));
+  ++kernels;
+  RouteArgs ra{};
+  ra.part = L->parts;
+  ra.nparts = nparts;
+  ra.bias = L->br;
+  ra.n = n;
+  ra.e = (int)E;
+  ra.top_k = (int)K;
+  ra.cap = (int)L->cap;
+  ra.blk = (int)L->blk;
+  ra.use_block = use_block ? 1 : 0;
+  ra.norm_topk = L->norm_topk;
+  ra.scale = L->scale;
+  ra.idx = (route && route->idx && !host) ? route->idx : L->idx;
+  ra.w = (route && route->weights && !host) ? route->weights : L->wts;
+  ra.allowed = use_block ? ((route && route->allowed && !host) ? route->allowed : L->allowed) : nullptr;
+  ra.probs = nullptr;
+  ra.counts = counts;
+  DMOE_CUDA(launch_route(ra, st));
+  ++kernels;
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[1], st));
+
+  if (!route_only) {
+    // ---- dispatch: offsets, token tiles, gathered fp16 rows
+    if ((s = grow(L->tiles, L->tiles_cap, (size_t)(n * K / 32 + E + 2))) != DMOE_OK) return s;
+    if ((s = grow(L->xg, L->xg_cap, (size_t)rows * H)) != DMOE_OK) return s;
+    if ((s = grow(L->hbuf, L->hbuf_cap, (size_t)rows * Imax)) != DMOE_OK) return s;
+    if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows)) != DMOE_OK) return s;
+    if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
+    DMOE_CUDA(launch_scan_tiles(counts, (int)E, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
+    DMOE_CUDA(launch_gather(xd, n, (int)H, (int)K, ra.idx, ra.w, off, fill, L->xg, L->pair_tok, L->pair_w,
+                            L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, L->has_shared ? 1 : 0, st));
+    kernels += 2;
+    if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
+
+    // ---- gate/up GEMM (+ SwiGLU)
+    CUtensorMap tm_x, tm_h;
+    if ((s = make_map(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->xg, (uint64_t)H, (uint64_t)rows, (uint64_t)H * 2, 64,
+                      (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+      return s;
+    if ((s = make_map(&tm_h, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->hbuf, (uint64_t)Imax, (uint64_t)rows,
+                      (uint64_t)Imax * 2, 64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+      return s;
+    int64_t active_est = std::min<int64_t>(E, n * K);
+    if (use_block) active_est = std::min<int64_t>(active_est, L->cap * (n / L->blk));
+    const int64_t tt_est = active_est + (n * K) / nt;
+    const int64_t sh_tt = L->has_shared ? (n + nt - 1) / nt : 0;
+    const bool same_type = !L->has_shared || L->stype == L->etype;
+    const int gu_stage_r = gemm_stage_k(L->etype), gu_stage_s = gemm_stage_k(L->stype);
+    const int64_t gu_tiles = tt_est * (L->I / kMTile) + sh_tt * (L->Is / kMTile);
+    int ks_gu = pick_ksplit(gu_tiles, L->sms,
+                            {(int)(H / gu_stage_r), L->has_shared ? (int)(H / gu_stage_s) : (int)(H / gu_stage_r)});
+    if ((size_t)rows * 2 * Imax * 4 > (256ull << 20)) ks_gu = 1;
+    const int64_t dn_tiles = (tt_est + sh_tt) * (H / kMTile);
+    int ks_dn = pick_ksplit(dn_tiles, L->sms,
+                            {(int)(L->I / gu_stage_r), L->has_shared ? (int)(L->Is / gu_stage_s) : (int)(L->I / gu_stage_r)});
+    if (ks_gu > 1) {
+      if ((s = grow(L->gu, L->gu_cap, (size_t)rows * 2 * Imax)) != DMOE_OK) return s;
+      DMOE_CUDA(cudaMemsetAsync(L->gu, 0, (size_t)rows * 2 * Imax * 4, st));
+    }
+    GemmParams gp;
+    std::memset(&gp, 0, sizeof(gp));
+    gp.tm_b = tm_x;
+    gp.tiles = L->tiles;
+    gp.n_tiles = n_tiles;
+    gp.n_shared_tt = (int32_t)sh_tt;
+    gp.ksplit = ks_gu;
+    gp.n_tokens = n;
+    gp.hbuf = L->hbuf;
+    gp.h_ld = Imax;
+    gp.h_quad_swap = (L->stype == DMOE_TYPE_Q4_K ? 1 : 0) | (L->etype == DMOE_TYPE_Q4_K ? 2 : 0);
+    gp.gu_acc = ks_gu > 1 ? L->gu : nullptr;
+    gp.gu_half = Imax;
+    gp.err = L->err;
+    if (L->has_shared) {
+      gp.tm_w[0][0] = L->sgate.tm_q;
+      gp.tm_w[0][1] = L->sup.tm_q;
+      gp.tm_s[0][0] = L->sgate.tm_s;
+      gp.tm_s[0][1] = L->sup.tm_s;
+      fill_group(gp.grp[0], L->sgate, L->stype, L->Is, L->Is);
+    }
+    gp.tm_w[1][0] = L->gate.tm_q;
+    gp.tm_w[1][1] = L->up.tm_q;
+    gp.tm_s[1][0] = L->gate.tm_s;
+    gp.tm_s[1][1] = L->up.tm_s;
+    fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I);
+    const int grid = L->sms;
+    if (same_type) {
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, gp, grid, st));
+      ++kernels;
+    } else {
+      GemmParams g0 = gp, g1 = gp;
+      g0.grp[1].present = 0;
+      g1.grp[0].present = 0;
+      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, g0, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, g1, grid, st));
+      kernels += 2;
+    }
+    if (ks_gu > 1) {
+      DMOE_CUDA(launch_swiglu_finish(L->gu, Imax, rows, n, (int)L->Is, (int)L->I, L->hbuf, Imax,
+                                     L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, st));
+      ++kernels;
+    }
+    if (prof) DMOE_CUDA(cudaEventRecord(L->ev[3], st));
+
+    // ---- down GEMM (+ gate weights, slot sum, shared expert)
+    DMOE_CUDA(cudaMemsetAsync(od, 0, (size_t)n * H * 4, st));
+    GemmParams dp = gp;
+    dp.tm_b = tm_h;
+    dp.ksplit = ks_dn;
+    dp.gu_acc = nullptr;
+    dp.out = od;
+    dp.out_ld = H;
+    dp.pair_tok = L->pair_tok;
+    dp.pair_w = L->pair_w;
+    std::memset(&dp.grp, 0, sizeof(dp.grp));
+    if (L->has_shared) {
+      dp.tm_w[0][0] = L->sdown.tm_q;
+      dp.tm_s[0][0] = L->sdown.tm_s;
+      fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H);
+    }
+    dp.tm_w[1][0] = L->down.tm_q;
+    dp.tm_s[1][0] = L->down.tm_s;
+    fill_group(dp.grp[1], L->down, L->etype, L->H, L->H);
+    if (same_type) {
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, dp, grid, st));
+      ++kernels;
+    } else {
+      GemmParams d0 = dp, d1 = dp;
+      d0.grp[1].present = 0;
+      d1.grp[0].present = 0;
+      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, d0, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, d1, grid, st));
+      kernels += 2;
+    }
+    if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));
+    L->stats.token_tile = nt;
+    L->stats.ksplit_gateup = ks_gu;
+    L->stats.ksplit_down = ks_dn;
+    DMOE_CUDA(cudaMemcpyAsync(L->host_counters, n_tiles, 8, cudaMemcpyDeviceToHost, st));
+  }
+  L->stats.router_parts = nparts;
+  L->stats.kernels = kernels;
+  L->stats.used_block_routing = use_block ? 1 : 0;
+
+  if (host) {
+    if (!route_only) DMOE_CUDA(cudaMemcpyAsync(out, od, (size_t)n * H * 4, cudaMemcpyDeviceToHost, st));
+    if (route) {
+      if (route->idx) DMOE_CUDA(cudaMemcpyAsync(route->idx, ra.idx, (size_t)n * K * 4, cudaMemcpyDeviceToHost, st));
+      if (route->weights)
+        DMOE_CUDA(cudaMemcpyAsync(route->weights, ra.w, (size_t)n * K * 4, cudaMemcpyDeviceToHost, st));
+      if (route->allowed && use_block)
+        DMOE_CUDA(cudaMemcpyAsync(route->allowed, ra.allowed, (size_t)(n / L->blk) * E, cudaMemcpyDeviceToHost, st));
+    }
+    return dmoe_sync(L);
+  }
+  return DMOE_OK;
+}
+
+dmoe_status dmoe_sync(dmoe_layer* L) {
+  if (!L) return fail(DMOE_ERR_INVALID_ARG, "null layer");
+  DMOE_CUDA(cudaSetDevice(L->device));
+  cudaStream_t st = L->last_stream ? L->last_stream : L->own_stream;
+  DMOE_CUDA(cudaStreamSynchronize(st));
+  uint32_t e = 0;
+  DMOE_CUDA(cudaMemcpy(&e, L->err, 4, cudaMemcpyDeviceToHost));
+  L->stats.n_routed_tiles = L->host_counters[0];
+  L->stats.n_active = L->host_counters[1];
+  if (L->profiled) {
+    float a = 0, b = 0, c = 0, d = 0;
+    cudaEventElapsedTime(&a, L->ev[0], L->ev[1]);
+    if (L->stats.token_tile) {
+      cudaEventElapsedTime(&b, L->ev[1], L->ev[2]);
+      cudaEventElapsedTime(&c, L->ev[2], L->ev[3]);
+      cudaEventElapsedTime(&d, L->ev[3], L->ev[4]);
+    }
+    L->stats.ms_router = a;
+    L->stats.ms_dispatch = b;
+    L->stats.ms_gateup = c;
+    L->stats.ms_down = d;
+    L->stats.ms_total = a + b + c + d;
+  }
+  if (e) {
+    cudaMemset(L->err, 0, 4);
+    return fail(DMOE_ERR_TIMEOUT, "device wait timed out (error bits 0x%x); the kernel gave up", e);
+  }
+  return DMOE_OK;
+}
+
+dmoe_status dmoe_get_stats(const dmoe_layer* L, dmoe_stats* s) {
+  if (!L || !s) return fail(DMOE_ERR_INVALID_ARG, "null argument");
+  *s = L->stats;
+  return DMOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,98 @@
+// dmoe_internal.h — device-side parameter blocks shared by the host library and the kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace dmoe {
+
+// ggml_type ids of the formats on this path (ggml.h enum ggml_type)
+enum WType : int { WT_F32 = 0, WT_F16 = 1, WT_Q8_0 = 8, WT_Q4_K = 12 };
+
+// The GEMM kernel's two epilogues.
+enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1 };
+
+constexpr int kRouterSeg = 256;  // canonical router segment length (fma chain per segment)
+constexpr int kMTile = 128;      // weight rows per MMA tile (tcgen05 M)
+
+// One token tile of one routed expert: rows [row0, row0 + nrows) of the gathered activation
+// buffer all belong to `expert`.
+struct TokTile {
+  int32_t expert;
+  int32_t row0;
+  int32_t nrows;
+  int32_t pad;
+};
+
+// A weight family processed by one GEMM launch. Group 0 is the shared expert (token rows
+// [0, n_tokens) in natural order, weight 1), group 1 the routed experts (token tiles from the
+// device tile list). Every flattened tile index maps to (group, token tile, m-tile, k-split).
+struct GemmGroup {
+  int32_t n_mt;          // output m-tiles per expert (rows_out / 128)
+  int32_t k_stages;      // K / STAGE_K
+  int32_t rows_per_exp;  // weight rows per expert in the tensor map (row coordinate stride)
+  int32_t present;       // 0 if this group has no work
+};
+
+struct GemmParams {
+  CUtensorMap tm_w[2][2];  // [group][matrix] quant / f16 tiles
+  CUtensorMap tm_s[2][2];  // [group][matrix] q8_0 scale tiles (fp32, repacked)
+  CUtensorMap tm_b;        // fp16 activations [rows][K] (xg for gate/up, hbuf for down)
+  GemmGroup grp[2];
+  const TokTile* tiles;        // routed token tiles (device)
+  const int32_t* n_tiles;      // number of routed token tiles (device)
+  int32_t n_shared_tt;         // shared-expert token tiles (host-known: ceil(N / NT))
+  int32_t ksplit;              // split-K factor
+  int64_t n_tokens;
+  // gate/up epilogue
+  __half* hbuf;
+  int64_t h_ld;
+  int32_t h_quad_swap;  // bit g: group g's down matrix is q4_K, write its h with the quad swap
+  float* gu_acc;        // split-K partial accumulators [rows][2 * gu_half], or null
+  int64_t gu_half;
+  // down epilogue
+  float* out;
+  int64_t out_ld;
+  const int32_t* pair_tok;
+  const float* pair_w;
+  uint32_t* err;
+};
+
+// Router: one routing block per CTA (src/diffuse-moe-graph.cpp:203-262).
+struct RouteArgs {
+  const float* part;   // [nparts][n][e] logit partials (segment partials, or the full logits)
+  int nparts;
+  const float* bias;   // [e] or null
+  int64_t n;
+  int e, top_k, cap, blk;
+  int use_block;       // block routing switch, evaluated on the host (:215-216)
+  int norm_topk;
+  float scale;
+  int32_t* idx;        // [n][top_k]
+  float* w;            // [n][top_k]
+  uint8_t* allowed;    // [n / blk][e] or null
+  float* probs;        // [n][e] or null
+  int32_t* counts;     // [e] per-expert pair counts (atomics; zeroed by the caller)
+};
+
+cudaError_t launch_router(const float* x, const float* wr, float* part, int64_t n, int h, int e, int nparts,
+                          cudaStream_t st);
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
+cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, int32_t* off, int32_t* fill,
+                              TokTile* tiles, int32_t* n_tiles, int32_t* n_active, cudaStream_t st);
+cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
+                          const int32_t* off, int32_t* fill, __half* xg, int32_t* pair_tok, float* pair_w,
+                          int swap_shared, int swap_routed, int with_shared, cudaStream_t st);
+cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows, int64_t n, int is, int iw,
+                                 __half* hbuf, int64_t h_ld, int swap_shared, int swap_routed, cudaStream_t st);
+cudaError_t launch_moe_gemm(int wtype, int mode, int nt, const GemmParams& p, int grid, cudaStream_t st);
+int gemm_stage_k(int wtype);
+
+// host-side codecs (quant.cpp)
+uint16_t f32_to_f16_bits(float f);
+float f16_bits_to_f32(uint16_t h);
+size_t row_size(int32_t type, int64_t k);
+
+}  // namespace dmoe

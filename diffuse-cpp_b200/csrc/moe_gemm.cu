@@ -1,0 +1,523 @@
+// moe_gemm.cu — grouped expert GEMMs of the block-routed MoE layer on sm_100a tensor cores.
+//
+// Replaces the three ggml_mul_mat_id calls, the SwiGLU, the gating multiply, the slot sum and
+// the shared expert of the reference layer (src/diffuse-moe-graph.cpp:264-286) with two
+// launches of one persistent kernel template:
+//
+//   MODE_GATEUP: h[row][i] = silu(Wg_e[i] . x_row) * (Wu_e[i] . x_row)   -> fp16 hbuf
+//   MODE_DOWN:   out[tok][o] += w_row * (Wd_e[o] . h_row)                  -> fp32 out (red.add)
+//
+// "Swap-AB" orientation: weights are the MMA's M side (128 rows per tile), the tokens of one
+// expert the N side (NT per tile), K runs along the GGUF rows, so quantised weights stream
+// through TMA in their native block layout.
+//
+// Warp roles (320 threads, one CTA per SM, persistent over a device-side tile list):
+//   warp 0      TMA producer: weight tiles (raw GGUF bytes / fp16) + activation tiles -> smem ring
+//   warp 1      TMEM allocator + MMA issuer (tcgen05.mma kind::f16, fp32 accumulators in TMEM)
+//   warps 2..9  two dequant warpgroups: q4_K / q8_0 tile -> fp16 in registers -> tcgen05.st into
+//               TMEM (the A operand of the TS-form MMA, no shared-memory round trip), then the
+//               tile epilogue (tcgen05.ld of the accumulators, SwiGLU / weighted scatter-add).
+// F16 weights skip the dequant: TMA lands them 128B-swizzled and the SS-form MMA reads smem.
+//
+// q4_K K-order: a q4_K 32-bit word of quants holds bytes b0..b3 of weights (k, k+1, k+2, k+3)
+// (low nibbles) and (k+32 .. k+35) (high nibbles). The masks 0x000F000F / (>>8) extract the
+// pairs (k, k+2) and (k+1, k+3) with one LOP3 each, so the MMA's K order inside every aligned
+// quad is (0, 2, 1, 3). The activations for a q4_K matrix are written with the same quad swap
+// (gather kernel for x, gate/up epilogue for h); the dot products are unchanged.
+#include "dmoe_internal.h"
+#include "sm100.cuh"
+
+namespace dmoe {
+
+template <int WT, int MODE, int NT>
+struct GemmCfg {
+  static constexpr bool QUANT = (WT != WT_F16);
+  static constexpr int MATS = (MODE == MODE_GATEUP) ? 2 : 1;
+  static constexpr int STAGE_K = (WT == WT_Q4_K) ? 256 : 128;
+  static constexpr int KB_PER_STAGE = STAGE_K / 128;
+  static constexpr int B_BYTES = STAGE_K * NT * 2;
+  // per matrix per stage: q4_K 128 rows x one 144 B super-block; q8_0 128 x 128 int8 (SW128)
+  // + 128 x 4 fp32 scales; f16 two SW128 boxes of 128 x 64.
+  static constexpr int W_BYTES = (WT == WT_Q4_K) ? 128 * 144 : (WT == WT_Q8_0) ? (128 * 128 + 128 * 16) : (128 * 128 * 2);
+  static constexpr int STAGE_BYTES = B_BYTES + MATS * W_BYTES;
+  static constexpr int SMEM_BUDGET = 227 * 1024 - 2048;
+  static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+  static constexpr int ACC_COLS = MATS * NT;
+  static constexpr int A_COLS = MATS * 64;
+  static constexpr int NA_RAW = QUANT ? (512 - ACC_COLS) / A_COLS : 0;
+  static constexpr int NA = NA_RAW > 4 ? 4 : NA_RAW;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int THREADS = 320;
+  static constexpr int EMPTY_COUNT = QUANT ? 1 + 4 * (KB_PER_STAGE >= 2 ? 2 : 1) : 1;
+  static_assert(STAGES >= 2, "smem ring needs two stages");
+  static_assert(!QUANT || NA >= 2, "TMEM A ring needs two buffers");
+  static_assert(B_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1024-B aligned stage parts");
+  static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "tcgen05 M=128 needs N % 16 == 0");
+};
+
+struct TileInfo {
+  int group, expert, row0, nrows, mt, k0, k1;
+};
+
+__device__ __forceinline__ int tiles_total(const GemmParams& p) {
+  int n0 = p.grp[0].present ? p.n_shared_tt * p.grp[0].n_mt * p.ksplit : 0;
+  int n1 = p.grp[1].present ? (*p.n_tiles) * p.grp[1].n_mt * p.ksplit : 0;
+  return n0 + n1;
+}
+
+template <int NT>
+__device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
+  TileInfo ti;
+  const int n0 = p.grp[0].present ? p.n_shared_tt * p.grp[0].n_mt * p.ksplit : 0;
+  int per_tt, r;
+  if (t < n0) {
+    ti.group = 0;
+    per_tt = p.grp[0].n_mt * p.ksplit;
+    const int tt = t / per_tt;
+    r = t - tt * per_tt;
+    ti.expert = 0;
+    ti.row0 = tt * NT;
+    const int64_t left = p.n_tokens - (int64_t)ti.row0;
+    ti.nrows = left < NT ? (int)left : NT;
+  } else {
+    t -= n0;
+    ti.group = 1;
+    per_tt = p.grp[1].n_mt * p.ksplit;
+    const int tt = t / per_tt;
+    r = t - tt * per_tt;
+    const TokTile tk = p.tiles[tt];
+    ti.expert = tk.expert;
+    ti.row0 = tk.row0;
+    ti.nrows = tk.nrows;
+  }
+  ti.mt = r / p.ksplit;
+  const int ks = r - ti.mt * p.ksplit;
+  const int ksz = p.grp[ti.group].k_stages / p.ksplit;
+  ti.k0 = ks * ksz;
+  ti.k1 = ti.k0 + ksz;
+  return ti;
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
+  return d;
+}
+__device__ __forceinline__ __half2 as_h2(uint32_t u) {
+  __half2 h;
+  memcpy(&h, &u, 4);
+  return h;
+}
+__device__ __forceinline__ uint32_t as_u32(__half2 h) {
+  uint32_t u;
+  memcpy(&u, &h, 4);
+  return u;
+}
+
+// Bounded mbarrier wait that also gives up when another role of this CTA has aborted.
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t errbit,
+                                          volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > DMOE_WAIT_NS) {
+      atomicOr(err, errbit);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// dequantisation of one 128-K block of one weight row into 64 TMEM columns (fp16 pairs)
+// ------------------------------------------------------------------------------------------
+// q4_K: `rowp` points at the row's 144-byte super-block in smem; kb selects K half 0/1.
+__device__ __forceinline__ void dequant_q4k_kblock(const uint8_t* rowp, int kb, uint32_t taddr) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(rowp);
+  const __half2 dd = as_h2(__byte_perm(hdr.x, 0, 0x1010));    // {d, d}
+  const __half2 dmn = as_h2(__byte_perm(hdr.x, 0, 0x3232));   // {dmin, dmin}
+  uint32_t scw, mw;
+  if (kb == 0) {
+    scw = hdr.y & 0x3F3F3F3Fu;
+    mw = hdr.z & 0x3F3F3F3Fu;
+  } else {
+    scw = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    mw = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+  }
+  const __half2 k1024 = __float2half2_rn(1024.0f);
+  // 6-bit ints -> fp16 exactly (magic 1024), then one rounding of d*sc / dmin*m
+  const __half2 sc01 = __hsub2(as_h2(__byte_perm(scw, 0x64646464u, 0x5140)), k1024);
+  const __half2 sc23 = __hsub2(as_h2(__byte_perm(scw, 0x64646464u, 0x5342)), k1024);
+  const __half2 mn01 = __hsub2(as_h2(__byte_perm(mw, 0x64646464u, 0x5140)), k1024);
+  const __half2 mn23 = __hsub2(as_h2(__byte_perm(mw, 0x64646464u, 0x5342)), k1024);
+  const __half2 dq01 = __hmul2(sc01, dd), dq23 = __hmul2(sc23, dd);
+  const __half2 nm01 = __hneg2(__hmul2(mn01, dmn)), nm23 = __hneg2(__hmul2(mn23, dmn));
+#pragma unroll
+  for (int gl = 0; gl < 2; ++gl) {
+    // sub-blocks 2 gl (low nibbles) and 2 gl + 1 (high nibbles) of this K half
+    const __half2 dlo = gl == 0 ? __low2half2(dq01) : __low2half2(dq23);
+    const __half2 dhi = gl == 0 ? __high2half2(dq01) : __high2half2(dq23);
+    const __half2 mlo = gl == 0 ? __low2half2(nm01) : __low2half2(nm23);
+    const __half2 mhi = gl == 0 ? __high2half2(nm01) : __high2half2(nm23);
+    const uint4* qp = reinterpret_cast<const uint4*>(rowp + 16 + 32 * (2 * kb + gl));
+    const uint4 qa = qp[0], qb = qp[1];
+    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    uint32_t lo[16], hi[16];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t q = qw[w];
+      const uint32_t v02 = lop3_and_or(q, 0x000F000Fu, 0x64006400u);
+      const uint32_t v13 = lop3_and_or(q >> 8, 0x000F000Fu, 0x64006400u);
+      const uint32_t h02 = lop3_and_or(q >> 4, 0x000F000Fu, 0x64006400u);
+      const uint32_t h13 = lop3_and_or(q >> 12, 0x000F000Fu, 0x64006400u);
+      lo[2 * w] = as_u32(__hfma2(__hsub2(as_h2(v02), k1024), dlo, mlo));
+      lo[2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(v13), k1024), dlo, mlo));
+      hi[2 * w] = as_u32(__hfma2(__hsub2(as_h2(h02), k1024), dhi, mhi));
+      hi[2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(h13), k1024), dhi, mhi));
+    }
+    tmem_st16(taddr + 32 * gl, lo);
+    tmem_st16(taddr + 32 * gl + 16, hi);
+  }
+}
+
+// q8_0 (repacked): `qtile` = 128 x 128 int8 tile (128B-swizzled), `stile` = 128 x 4 fp32 scales.
+__device__ __forceinline__ void dequant_q80_kblock(const uint8_t* qtile, const uint8_t* stile, int row,
+                                                   uint32_t taddr) {
+  const float4 sc = *reinterpret_cast<const float4*>(stile + row * 16);
+  const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
+  const __half2 k1152 = __float2half2_rn(1152.0f);
+  const uint8_t* rp = qtile + row * 128;
+#pragma unroll
+  for (int blk = 0; blk < 4; ++blk) {
+    const __half2 d2 = __float2half2_rn(scv[blk]);
+    uint32_t r[16];
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 2 * blk + cc;
+      const uint4 qv = *reinterpret_cast<const uint4*>(rp + ((c ^ (row & 7)) << 4));
+      const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const uint32_t xq = qw[w] ^ 0x80808080u;
+        const uint32_t v0 = __byte_perm(xq, 0x64646464u, 0x5140);
+        const uint32_t v1 = __byte_perm(xq, 0x64646464u, 0x5342);
+        r[8 * cc + 2 * w] = as_u32(__hmul2(__hsub2(as_h2(v0), k1152), d2));
+        r[8 * cc + 2 * w + 1] = as_u32(__hmul2(__hsub2(as_h2(v1), k1152), d2));
+      }
+    }
+    tmem_st16(taddr + 16 * blk, r);
+  }
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+
+__device__ __forceinline__ int quad_swap(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
+
+template <int WT, int MODE, int NT>
+__global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant__ GemmParams p) {
+  using C = GemmCfg<WT, MODE, NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* afull = empty + C::STAGES;
+  uint64_t* aempty = afull + 4;
+  uint64_t* accfull = aempty + 4;
+  uint64_t* accempty = accfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], C::EMPTY_COUNT);
+    }
+    for (int a = 0; a < 4; ++a) {
+      mbar_init(&afull[a], 4);
+      mbar_init(&aempty[a], 1);
+    }
+    mbar_init(accfull, 1);
+    mbar_init(accempty, 8);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int g = 0; g < 2; ++g) {
+      if (!p.grp[g].present) continue;
+      tma_prefetch_desc(&p.tm_w[g][0]);
+      if (C::MATS > 1) tma_prefetch_desc(&p.tm_w[g][1]);
+    }
+    tma_prefetch_desc(&p.tm_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const int total = tiles_total(p);
+
+  auto stage_ptr = [&](int s) -> uint8_t* { return smem + s * C::STAGE_BYTES; };
+  auto wtile_ptr = [&](int s, int m) -> uint8_t* { return smem + s * C::STAGE_BYTES + C::B_BYTES + m * C::W_BYTES; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      uint32_t stage_seq = 0;
+      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+        const TileInfo ti = decode_tile<NT>(p, t);
+        const int wrow = ti.expert * p.grp[ti.group].rows_per_exp + ti.mt * kMTile;
+        for (int kc = ti.k0; kc < ti.k1; ++kc) {
+          const int s = stage_seq % C::STAGES;
+          const uint32_t ph = (stage_seq / C::STAGES) & 1u;
+          if (!role_wait(&empty[s], ph ^ 1u, p.err, ERRBIT_TIMEOUT_EMPTY, abort_flag)) break;
+          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+#pragma unroll
+          for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
+            tma_load_2d(stage_ptr(s) + bx * NT * 128, &p.tm_b, kc * C::STAGE_K + bx * 64, ti.row0, &full[s]);
+#pragma unroll
+          for (int m = 0; m < C::MATS; ++m) {
+            uint8_t* wt = wtile_ptr(s, m);
+            if constexpr (WT == WT_Q4_K) {
+              tma_load_2d_hint(wt, &p.tm_w[ti.group][m], kc * 144, wrow, &full[s], pol_w);
+            } else if constexpr (WT == WT_Q8_0) {
+              tma_load_2d_hint(wt, &p.tm_w[ti.group][m], kc * 128, wrow, &full[s], pol_w);
+              tma_load_2d_hint(wt + 128 * 128, &p.tm_s[ti.group][m], kc * 4, wrow, &full[s], pol_w);
+            } else {
+              tma_load_2d_hint(wt, &p.tm_w[ti.group][m], kc * 128, wrow, &full[s], pol_w);
+              tma_load_2d_hint(wt + 128 * 128, &p.tm_w[ti.group][m], kc * 128 + 64, wrow, &full[s], pol_w);
+            }
+          }
+          ++stage_seq;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, NT);
+      uint32_t stage_seq = 0, tile_seq = 0;
+      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+        const TileInfo ti = decode_tile<NT>(p, t);
+        if (!role_wait(accempty, (tile_seq & 1u) ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) break;
+        tc_fence_after();
+        bool first = true;
+        bool ok = true;
+        for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
+          const int s = stage_seq % C::STAGES;
+          const uint32_t ph = (stage_seq / C::STAGES) & 1u;
+          if (!role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t bbase = smem_u32(stage_ptr(s));
+#pragma unroll
+          for (int kb = 0; kb < C::KB_PER_STAGE; ++kb) {
+            uint32_t abuf = 0;
+            int a = 0;
+            if constexpr (C::QUANT) {
+              const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
+              a = kbs % C::NA;
+              const uint32_t u = kbs / C::NA;
+              if (!role_wait(&afull[a], u & 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+              abuf = tbase + C::ACC_COLS + a * C::A_COLS;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint64_t bdesc = sdesc_sw128(bbase + (kb * 2 + j / 4) * (NT * 128) + (j % 4) * 32, 1024);
+#pragma unroll
+              for (int m = 0; m < C::MATS; ++m) {
+                const uint32_t dcol = tbase + m * NT;
+                if constexpr (C::QUANT) {
+                  mma_f16_ts(dcol, abuf + m * 64 + 8 * j, bdesc, idesc, first ? 0u : 1u);
+                } else {
+                  const uint32_t wb = smem_u32(wtile_ptr(s, m));
+                  const uint64_t adesc = sdesc_sw128(wb + (j / 4) * (128 * 128) + (j % 4) * 32, 1024);
+                  mma_f16_ss(dcol, adesc, bdesc, idesc, first ? 0u : 1u);
+                }
+              }
+              first = false;
+            }
+            if constexpr (C::QUANT) mma_commit(&aempty[a]);
+          }
+          mma_commit(&empty[s]);
+          ++stage_seq;
+        }
+        if (!ok) break;
+        mma_commit(accfull);
+        ++tile_seq;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ dequant + epilogue
+    const int wg = (warp - 2) >> 2;          // 0 or 1
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;     // weight row inside the 128-row tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint32_t stage_seq = 0, tile_seq = 0;
+    for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+      const TileInfo ti = decode_tile<NT>(p, t);
+      bool ok = true;
+      if constexpr (C::QUANT) {
+        for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
+          const int s = stage_seq % C::STAGES;
+          const uint32_t ph = (stage_seq / C::STAGES) & 1u;
+          const bool reads = (C::KB_PER_STAGE >= 2) || ((stage_seq & 1u) == (uint32_t)wg);
+          if (reads) {
+            if (!role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
+#pragma unroll
+            for (int kb = 0; kb < C::KB_PER_STAGE; ++kb) {
+              const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
+              if ((kbs & 1u) != (uint32_t)wg) continue;
+              const int a = kbs % C::NA;
+              const uint32_t u = kbs / C::NA;
+              if (!role_wait(&aempty[a], (u & 1u) ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t abuf = tbase + lane_off + C::ACC_COLS + a * C::A_COLS;
+#pragma unroll
+              for (int m = 0; m < C::MATS; ++m) {
+                const uint8_t* wt = wtile_ptr(s, m);
+                if constexpr (WT == WT_Q4_K) {
+                  dequant_q4k_kblock(wt + row * 144, kb, abuf + m * 64);
+                } else {
+                  dequant_q80_kblock(wt, wt + 128 * 128, row, abuf + m * 64);
+                }
+              }
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&afull[a]);
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+          }
+          ++stage_seq;
+        }
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------------- epilogue
+      if (!role_wait(accfull, tile_seq & 1u, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
+      tc_fence_after();
+      const int o = ti.mt * kMTile + row;  // output feature (gate/up: i, down: o)
+#pragma unroll 1
+      for (int c0 = wg * (NT / 2); c0 < (wg + 1) * (NT / 2); c0 += 16) {
+        uint32_t acc0[16];
+        tmem_ld16(tbase + lane_off + c0, acc0);
+        if constexpr (MODE == MODE_GATEUP) {
+          uint32_t acc1[16];
+          tmem_ld16(tbase + lane_off + NT + c0, acc1);
+          tmem_wait_ld();
+          if (p.gu_acc == nullptr) {
+            const int oi = ((p.h_quad_swap >> ti.group) & 1) ? quad_swap(o) : o;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              if (c0 + c < ti.nrows) {
+                const float g = __uint_as_float(acc0[c]);
+                const float u = __uint_as_float(acc1[c]);
+                p.hbuf[(int64_t)(ti.row0 + c0 + c) * p.h_ld + oi] = __float2half_rn(silu_f(g) * u);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              if (c0 + c < ti.nrows) {
+                float* dst = p.gu_acc + (int64_t)(ti.row0 + c0 + c) * (2 * p.gu_half);
+                atomicAdd(dst + o, __uint_as_float(acc0[c]));
+                atomicAdd(dst + p.gu_half + o, __uint_as_float(acc1[c]));
+              }
+            }
+          }
+        } else {
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            if (c0 + c < ti.nrows) {
+              const int r = ti.row0 + c0 + c;
+              int64_t tok;
+              float wgt;
+              if (ti.group == 0) {
+                tok = r;
+                wgt = 1.0f;
+              } else {
+                tok = p.pair_tok[r];
+                wgt = p.pair_w[r];
+              }
+              atomicAdd(p.out + tok * p.out_ld + o, __uint_as_float(acc0[c]) * wgt);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(accempty);
+      ++tile_seq;
+    }
+  }
+
+  // ---------------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// launcher
+// ------------------------------------------------------------------------------------------
+template <int WT, int MODE, int NT>
+static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t st) {
+  using C = GemmCfg<WT, MODE, NT>;
+  auto kern = moe_gemm_kernel<WT, MODE, NT>;
+  static bool attr_set = false;  // per instantiation; set once per process (all devices)
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int WT, int MODE>
+static cudaError_t launch_nt(const GemmParams& p, int nt, int grid, cudaStream_t st) {
+  switch (nt) {
+    case 32: return launch_one<WT, MODE, 32>(p, grid, st);
+    case 64: return launch_one<WT, MODE, 64>(p, grid, st);
+    case 128: return launch_one<WT, MODE, 128>(p, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_moe_gemm(int wtype, int mode, int nt, const GemmParams& p, int grid, cudaStream_t st) {
+  if (mode == MODE_GATEUP) {
+    switch (wtype) {
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_GATEUP>(p, nt, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_GATEUP>(p, nt, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_GATEUP>(p, nt, grid, st);
+    }
+  } else {
+    switch (wtype) {
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_DOWN>(p, nt, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_DOWN>(p, nt, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_DOWN>(p, nt, grid, st);
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+int gemm_stage_k(int wtype) { return wtype == WT_Q4_K ? 256 : 128; }
+
+}  // namespace dmoe

@@ -1,0 +1,276 @@
+"""ctypes binding of libdiffuse_moe (C ABI: include/diffuse_moe.h).
+
+This is the host-side mirror of the reference's MoE call site
+(src/diffuse-moe-graph.cpp:195-287 inside diffuse_build_graph_moe): a layer is bound once from
+its GGUF tensors (struct diffuse_moe_layer, src/diffuse-common.h:59-86) and called with
+moe_in [n_tokens, n_embd] f32, returning moe_out (routed + shared, no residual).
+
+There is no CPU fallback: if the shared library is missing, or the machine has no CUDA device,
+the calls raise. Inputs may be numpy arrays (host memory; the call copies in and out and
+returns when done) or torch CUDA tensors (device memory; work is enqueued on the current torch
+stream and `sync()` waits for it).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdiffuse_moe.so")
+
+# ggml_type ids (ggml.h)
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K = 0, 1, 8, 12
+TYPE_NAMES = {TYPE_F32: "f32", TYPE_F16: "f16", TYPE_Q8_0: "q8_0", TYPE_Q4_K: "q4_K"}
+
+F_HOST_PTRS, F_ROUTE_ONLY, F_PROFILE = 1, 2, 4
+
+STATUS_NAMES = {
+    0: "DMOE_OK",
+    1: "DMOE_ERR_INVALID_ARG",
+    2: "DMOE_ERR_UNSUPPORTED",
+    3: "DMOE_ERR_NO_DEVICE",
+    4: "DMOE_ERR_CUDA",
+    5: "DMOE_ERR_NCCL",
+    6: "DMOE_ERR_TIMEOUT",
+    7: "DMOE_ERR_OOM",
+}
+
+
+class LayerDesc(ctypes.Structure):
+    _fields_ = [
+        ("n_embd", ctypes.c_int64),
+        ("n_ff_exp", ctypes.c_int64),
+        ("n_ff_shexp", ctypes.c_int64),
+        ("n_expert", ctypes.c_int64),
+        ("n_expert_used", ctypes.c_int64),
+        ("expert_capacity", ctypes.c_int64),
+        ("moe_block_size", ctypes.c_int64),
+        ("routed_scaling", ctypes.c_float),
+        ("norm_topk_prob", ctypes.c_int32),
+        ("expert_type", ctypes.c_int32),
+        ("shared_type", ctypes.c_int32),
+        ("w_gate", ctypes.c_void_p),
+        ("w_up", ctypes.c_void_p),
+        ("w_down", ctypes.c_void_p),
+        ("sw_gate", ctypes.c_void_p),
+        ("sw_up", ctypes.c_void_p),
+        ("sw_down", ctypes.c_void_p),
+        ("w_router", ctypes.c_void_p),
+        ("b_router", ctypes.c_void_p),
+    ]
+
+
+class DistCfg(ctypes.Structure):
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world_size", ctypes.c_int32),
+        ("device", ctypes.c_int32),
+        ("timeout_ms", ctypes.c_int32),
+        ("nccl_id", ctypes.c_void_p),
+    ]
+
+
+class RouteOut(ctypes.Structure):
+    _fields_ = [
+        ("idx", ctypes.c_void_p),
+        ("weights", ctypes.c_void_p),
+        ("allowed", ctypes.c_void_p),
+    ]
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [
+        ("n_active", ctypes.c_int32),
+        ("n_routed_tiles", ctypes.c_int32),
+        ("token_tile", ctypes.c_int32),
+        ("ksplit_gateup", ctypes.c_int32),
+        ("ksplit_down", ctypes.c_int32),
+        ("router_parts", ctypes.c_int32),
+        ("kernels", ctypes.c_int32),
+        ("used_block_routing", ctypes.c_int32),
+        ("ms_router", ctypes.c_float),
+        ("ms_dispatch", ctypes.c_float),
+        ("ms_gateup", ctypes.c_float),
+        ("ms_down", ctypes.c_float),
+        ("ms_total", ctypes.c_float),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class DmoeError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads libdiffuse_moe.so. Raises if it has not been built (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `make -C diffuse-cpp_b200` (no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    P = ctypes.c_void_p
+    lib.dmoe_create.argtypes = [ctypes.POINTER(LayerDesc), ctypes.POINTER(DistCfg), ctypes.POINTER(P)]
+    lib.dmoe_create.restype = ctypes.c_int
+    lib.dmoe_forward.argtypes = [P, P, ctypes.c_int64, P, ctypes.POINTER(RouteOut), P, ctypes.c_uint32]
+    lib.dmoe_forward.restype = ctypes.c_int
+    lib.dmoe_sync.argtypes = [P]
+    lib.dmoe_sync.restype = ctypes.c_int
+    lib.dmoe_get_stats.argtypes = [P, ctypes.POINTER(Stats)]
+    lib.dmoe_get_stats.restype = ctypes.c_int
+    lib.dmoe_destroy.argtypes = [P]
+    lib.dmoe_destroy.restype = None
+    lib.dmoe_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    lib.dmoe_last_error.restype = ctypes.c_size_t
+    lib.dmoe_abi_version.argtypes = []
+    lib.dmoe_abi_version.restype = ctypes.c_int32
+    lib.dmoe_quantize.argtypes = [ctypes.c_int32, P, P, ctypes.c_int64, ctypes.c_int64]
+    lib.dmoe_quantize.restype = ctypes.c_size_t
+    lib.dmoe_quantized_size.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int64]
+    lib.dmoe_quantized_size.restype = ctypes.c_size_t
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = ctypes.create_string_buffer(2048)
+    lib.dmoe_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        raise DmoeError(status, last_error())
+
+
+def quantized_size(qtype: int, nrows: int, n_per_row: int) -> int:
+    return int(load().dmoe_quantized_size(qtype, nrows, n_per_row))
+
+
+def quantize(values: np.ndarray, qtype: int) -> np.ndarray:
+    """Quantises a [rows, n_per_row] float32 array to GGUF block bytes (uint8 [rows, row_bytes])."""
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    if v.ndim == 1:
+        v = v[None, :]
+    rows, k = v.shape
+    rs = quantized_size(qtype, 1, k)
+    if rs == 0:
+        raise ValueError(f"row length {k} is not a whole number of blocks of type {qtype}")
+    out = np.empty((rows, rs), dtype=np.uint8)
+    n = load().dmoe_quantize(qtype, v.ctypes.data, out.ctypes.data, rows, k)
+    if n != rows * rs:
+        raise RuntimeError("dmoe_quantize failed")
+    return out
+
+
+def _ptr(a) -> int:
+    if a is None:
+        return 0
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return a.data_ptr()  # torch tensor
+
+
+class MoELayer:
+    """One bound MoE layer (dmoe_create). `tensors` holds the GGUF tensors:
+    w_gate/w_up/w_down (uint8 bytes or float16 arrays), sw_*, w_router [E, H] f32, b_router [E] f32 or None."""
+
+    def __init__(self, hp: dict, tensors: dict, dist: Optional[DistCfg] = None):
+        lib = load()
+        self._keep = {}
+        d = LayerDesc()
+        d.n_embd = hp["n_embd"]
+        d.n_ff_exp = hp["n_ff_exp"]
+        d.n_ff_shexp = hp.get("n_ff_shexp", 0)
+        d.n_expert = hp["n_expert"]
+        d.n_expert_used = hp["n_expert_used"]
+        d.expert_capacity = hp.get("expert_capacity", 48)
+        d.moe_block_size = hp.get("moe_block_size", 32)
+        d.routed_scaling = hp.get("routed_scaling", 1.0)
+        d.norm_topk_prob = hp.get("norm_topk_prob", 1)
+        d.expert_type = hp["expert_type"]
+        d.shared_type = hp.get("shared_type", hp["expert_type"])
+        for name in ("w_gate", "w_up", "w_down", "sw_gate", "sw_up", "sw_down", "w_router", "b_router"):
+            t = tensors.get(name)
+            if t is not None:
+                t = np.ascontiguousarray(t)
+                self._keep[name] = t
+                setattr(d, name, t.ctypes.data)
+            else:
+                setattr(d, name, None)
+        self.hp = dict(hp)
+        self.desc = d
+        h = ctypes.c_void_p()
+        _check(lib.dmoe_create(ctypes.byref(d), ctypes.byref(dist) if dist is not None else None, ctypes.byref(h)))
+        self._h = h
+        self._keep.clear()  # weights are on the device now
+
+    def forward(self, x, out=None, route: bool = False, route_only: bool = False, profile: bool = False,
+                stream: Optional[int] = None):
+        """x: numpy [n, H] float32 (host mode) or torch CUDA float32 tensor (device mode).
+        Returns out (and (idx, weights, allowed) when route=True)."""
+        lib = load()
+        H = self.hp["n_embd"]
+        K = self.hp["n_expert_used"]
+        E = self.hp["n_expert"]
+        blk = self.hp.get("moe_block_size", 32)
+        is_np = isinstance(x, np.ndarray)
+        n = int(x.shape[0])
+        flags = (F_HOST_PTRS if is_np else 0) | (F_ROUTE_ONLY if route_only else 0) | (F_PROFILE if profile else 0)
+        if is_np:
+            x = np.ascontiguousarray(x, dtype=np.float32)
+            if out is None and not route_only:
+                out = np.empty((n, H), dtype=np.float32)
+            mk = lambda shape, dt: np.empty(shape, dtype=dt)  # noqa: E731
+        else:
+            import torch
+
+            if out is None and not route_only:
+                out = torch.empty((n, H), dtype=torch.float32, device=x.device)
+            mk = lambda shape, dt: torch.empty(shape, dtype={np.int32: torch.int32, np.float32: torch.float32,  # noqa: E731
+                                                             np.uint8: torch.uint8}[dt], device=x.device)
+            if stream is None:
+                stream = torch.cuda.current_stream(x.device).cuda_stream
+        ro = None
+        routes = None
+        if route or route_only:
+            idx = mk((n, K), np.int32)
+            w = mk((n, K), np.float32)
+            allowed = mk((max(n // blk, 1), E), np.uint8) if blk > 0 else None
+            ro = RouteOut(_ptr(idx), _ptr(w), _ptr(allowed))
+            routes = (idx, w, allowed)
+        _check(lib.dmoe_forward(self._h, _ptr(x), n, _ptr(out), ctypes.byref(ro) if ro is not None else None,
+                                stream or None, flags))
+        if route or route_only:
+            return (out, routes) if not route_only else routes
+        return out
+
+    def sync(self) -> None:
+        _check(load().dmoe_sync(self._h))
+
+    def stats(self) -> dict:
+        s = Stats()
+        _check(load().dmoe_get_stats(self._h, ctypes.byref(s)))
+        return s.as_dict()
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            load().dmoe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

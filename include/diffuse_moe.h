@@ -1,0 +1,163 @@
+/*
+ * diffuse_moe.h — C ABI of libdiffuse_moe, a B200 (sm_100a) implementation of diffuse-cpp's
+ * block-routed MoE FFN layer (LLaDA2-style: sigmoid router, expert-bias selection, per-block
+ * expert capacity, per-token top-k, renormalised x routed_scaling gates, SwiGLU experts and an
+ * always-on shared expert).
+ *
+ * The library is a drop-in for the MoE subgraph the reference graph builder emits
+ * (Akicou/diffuse-cpp src/diffuse-moe-graph.cpp:195-287): same weight tensors in their GGUF
+ * layouts and quant types (F16, Q8_0, Q4_K), same router semantics, same output
+ * (moe_out, routed + shared, without the residual that :292 adds).
+ *
+ * Plain C types only. Every entry point returns a status; none exits the process and none
+ * falls back to the CPU: without a usable CUDA device dmoe_create returns DMOE_ERR_NO_DEVICE.
+ */
+#ifndef DIFFUSE_MOE_H
+#define DIFFUSE_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DMOE_ABI_VERSION 1
+
+/* Replaces the reference's bool returns + DIFFUSE_DIE/exit(1) (src/diffuse-common.h:22-27,
+ * src/diffuse-moe-graph.cpp:325-329). */
+typedef enum dmoe_status {
+  DMOE_OK = 0,
+  DMOE_ERR_INVALID_ARG = 1,  /* bad shape, null pointer, unsupported hyper-parameter */
+  DMOE_ERR_UNSUPPORTED = 2,  /* quant type / shape this build does not handle */
+  DMOE_ERR_NO_DEVICE = 3,    /* no CUDA device (there is no CPU fallback) */
+  DMOE_ERR_CUDA = 4,         /* CUDA runtime / driver error; see dmoe_last_error */
+  DMOE_ERR_NCCL = 5,         /* expert-parallel communication error */
+  DMOE_ERR_TIMEOUT = 6,      /* a bounded device-side wait expired (kernel gave up, no hang) */
+  DMOE_ERR_OOM = 7           /* device allocation failed */
+} dmoe_status;
+
+/* ggml_type ids (ggml.h enum ggml_type) of the weight formats on this path. The GGUF block
+ * layouts are unchanged: F16 rows; Q8_0 = 32-weight blocks {f16 d; int8 q[32]};
+ * Q4_K = 256-weight super-blocks {f16 d; f16 dmin; u8 scales[12]; u8 qs[128]}. */
+enum {
+  DMOE_TYPE_F32 = 0,
+  DMOE_TYPE_F16 = 1,
+  DMOE_TYPE_Q8_0 = 8,
+  DMOE_TYPE_Q4_K = 12
+};
+
+/* One MoE layer: the tensors of struct diffuse_moe_layer (src/diffuse-common.h:72-82) and the
+ * MoE hyper-parameters of struct diffuse_model (src/diffuse-common.h:103-116) as loaded by
+ * diffuse_model_load_impl (src/diffuse-model.cpp:141-158, 187-196). All pointers are HOST
+ * memory in GGUF layout (ggml ne order, fastest dimension first):
+ *   w_gate, w_up   ne = [n_embd, n_ff_exp, n_expert]   ("blk.N.moe_experts_{gate,up}.weight")
+ *   w_down         ne = [n_ff_exp, n_embd, n_expert]   ("blk.N.moe_experts_down.weight")
+ *   sw_gate, sw_up ne = [n_embd, n_ff_shexp]           ("blk.N.moe_shared_{gate,up}.weight")
+ *   sw_down        ne = [n_ff_shexp, n_embd]           ("blk.N.moe_shared_down.weight")
+ *   w_router       ne = [n_embd, n_expert], F32        ("blk.N.moe_gate.weight")
+ *   b_router       ne = [n_expert], F32, or NULL        ("blk.N.moe_gate_bias.weight")
+ * The data is copied to the device by dmoe_create; the caller may free it afterwards. */
+typedef struct dmoe_layer_desc {
+  int64_t n_embd;          /* H */
+  int64_t n_ff_exp;        /* I   expert_feed_forward_length */
+  int64_t n_ff_shexp;      /* I_s shared expert width; 0 = no shared expert (:281) */
+  int64_t n_expert;        /* E   expert_count */
+  int64_t n_expert_used;   /* top-k  expert_used_count (<= 16) */
+  int64_t expert_capacity; /* experts allowed per routing block (default 48) */
+  int64_t moe_block_size;  /* tokens per routing block (default 32) */
+  float routed_scaling;    /* routed_scaling_factor (default 1) */
+  int32_t norm_topk_prob;  /* renormalise the top-k gates (default 1) */
+  int32_t expert_type;     /* DMOE_TYPE_* of w_gate / w_up / w_down */
+  int32_t shared_type;     /* DMOE_TYPE_* of sw_gate / sw_up / sw_down */
+  const void* w_gate;
+  const void* w_up;
+  const void* w_down;
+  const void* sw_gate;
+  const void* sw_up;
+  const void* sw_down;
+  const float* w_router;
+  const float* b_router;
+} dmoe_layer_desc;
+
+/* Expert parallelism: one process per GPU; every rank calls dmoe_create and dmoe_forward
+ * collectively with its own token shard. NULL (or world_size 1) = single GPU. Rank r owns
+ * experts [r E / W, (r + 1) E / W); router and shared expert are replicated. */
+typedef struct dmoe_dist_cfg {
+  int32_t rank;
+  int32_t world_size;
+  int32_t device;          /* CUDA device ordinal for this rank */
+  int32_t timeout_ms;      /* host deadline for a collective; 0 = 60000 */
+  const void* nccl_id;     /* 128-byte ncclUniqueId, identical on all ranks */
+} dmoe_dist_cfg;
+
+/* Optional routing outputs (for parity checks and statistics). Any field may be NULL. */
+typedef struct dmoe_route_out {
+  int32_t* idx;            /* [n_tokens][n_expert_used] selected experts, slot order */
+  float* weights;          /* [n_tokens][n_expert_used] applied gates */
+  uint8_t* allowed;        /* [n_tokens / moe_block_size][n_expert] capacity mask (block routing) */
+} dmoe_route_out;
+
+/* Statistics of the last dmoe_forward, valid after dmoe_sync. */
+typedef struct dmoe_stats {
+  int32_t n_active;        /* distinct routed experts selected */
+  int32_t n_routed_tiles;  /* routed token tiles fed to the expert GEMMs */
+  int32_t token_tile;      /* token tile width of the expert GEMMs */
+  int32_t ksplit_gateup;   /* split-K factors used */
+  int32_t ksplit_down;
+  int32_t router_parts;    /* router segment partials (1 = fused running sum) */
+  int32_t kernels;         /* kernels enqueued by the last forward */
+  int32_t used_block_routing;
+  float ms_router;         /* per-stage device times, with DMOE_F_PROFILE */
+  float ms_dispatch;
+  float ms_gateup;
+  float ms_down;
+  float ms_total;
+} dmoe_stats;
+
+#define DMOE_F_HOST_PTRS 1u   /* x, out and route_out are host memory: the call copies them and
+                                 returns after the result is on the host */
+#define DMOE_F_ROUTE_ONLY 2u  /* run the router only (out is not touched) */
+#define DMOE_F_PROFILE 4u     /* record CUDA events around each stage (dmoe_get_stats) */
+
+/* Binds one layer: validates the shapes, uploads router, bias and expert weights to the device
+ * once (library-owned), prepares the TMA descriptors. Replaces the per-forward weight binding
+ * and F32 casts of src/diffuse-moe-graph.cpp:8-12,203,282-284 (weights are never re-staged). */
+dmoe_status dmoe_create(const dmoe_layer_desc* desc, const dmoe_dist_cfg* dist, struct dmoe_layer** out);
+
+/* moe_out = MoE(x). Replaces src/diffuse-moe-graph.cpp:195-287 (router :203-262, experts
+ * :264-278, shared expert :280-286). x and out are [n_tokens][n_embd] f32, row-major (ggml
+ * ne = [n_embd, n_tokens]). Without DMOE_F_HOST_PTRS they are device pointers and the work is
+ * enqueued on `stream` (a cudaStream_t; NULL = the layer's own stream); call dmoe_sync before
+ * reading results. Block routing is used iff moe_block_size > 1, 0 < expert_capacity <
+ * n_expert and n_tokens % moe_block_size == 0 (:215-216); otherwise plain per-token top-k.
+ * Calls on one layer handle are not reentrant. */
+dmoe_status dmoe_forward(struct dmoe_layer* layer, const float* x, int64_t n_tokens, float* out,
+                         const dmoe_route_out* route, void* stream, uint32_t flags);
+
+/* Waits for the layer's work, reports device-side timeouts, refreshes the statistics. */
+dmoe_status dmoe_sync(struct dmoe_layer* layer);
+
+dmoe_status dmoe_get_stats(const struct dmoe_layer* layer, dmoe_stats* stats);
+
+void dmoe_destroy(struct dmoe_layer* layer);
+
+/* Message of the last error on this thread; returns its full length. */
+size_t dmoe_last_error(char* buf, size_t len);
+
+int32_t dmoe_abi_version(void);
+
+/* Host-side GGUF quantiser for building weights. Replaces tools/quant_lib.c:16-27
+ * (quantize_to_type -> ggml_quantize_chunk): Q8_0 follows ggml's round-to-nearest scheme
+ * (amax / 127, roundf); Q4_K uses this library's own scale/min search over the same block
+ * format. F16 is round-to-nearest-even, F32 a copy. Returns the bytes written, 0 on error. */
+size_t dmoe_quantize(int32_t type, const float* src, void* dst, int64_t nrows, int64_t n_per_row);
+
+/* Bytes of nrows rows of n_per_row values. Replaces tools/quant_lib.c:30-33. */
+size_t dmoe_quantized_size(int32_t type, int64_t nrows, int64_t n_per_row);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIFFUSE_MOE_H */

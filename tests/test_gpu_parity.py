@@ -1,0 +1,89 @@
+"""CUDA path vs the CPU oracle on the same seeded inputs (through the C ABI).
+
+Bar: routing bit-exact (selected experts in slot order, applied gate weights bitwise, the
+per-block capacity mask); layer output relative L2 error <= 1e-3 for F16 weights and
+<= 2e-3 for Q8_0 / Q4_K weights, against the oracle's double-accumulation answer.
+"""
+import numpy as np
+import pytest
+
+import diffuse_moe as dm
+import oracle
+import synth
+
+TOL = {dm.TYPE_F16: 1e-3, dm.TYPE_Q8_0: 2e-3, dm.TYPE_Q4_K: 2e-3}
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a.astype(np.float64) - b.astype(np.float64)) / np.linalg.norm(b.astype(np.float64)))
+
+
+def check_layer(spec: synth.LayerSpec, n: int, t=None, x=None, layer=None):
+    hp = spec.hparams()
+    t = synth.make_layer(spec) if t is None else t
+    x = synth.make_input(n, spec.H, spec.seed) if x is None else x
+    L = dm.MoELayer(hp, t) if layer is None else layer
+    out, (idx, w, allowed) = L.forward(x, route=True)
+    r_out, r_idx, r_w, r_allowed, used = oracle.layer(hp, t, x)
+    assert np.array_equal(idx, r_idx), f"routing differs at {np.argwhere(idx != r_idx)[:5]}"
+    assert np.array_equal(w.view(np.uint32), r_w.view(np.uint32)), "gate weights differ"
+    if used:
+        assert np.array_equal(allowed[: n // spec.blk], r_allowed), "capacity mask differs"
+    err = rel_l2(out, r_out)
+    tol = max(TOL[spec.expert_type], TOL[spec.stype])
+    assert err <= tol, f"rel L2 {err:.3e} > {tol:.1e}"
+    return err, L
+
+
+def tiny(qtype, **kw):
+    base = dict(H=256, I=256, Is=256, E=16, top_k=4, cap=6, blk=32, expert_type=qtype, seed=11)
+    base.update(kw)
+    return synth.LayerSpec(**base)
+
+
+@pytest.fixture(autouse=True)
+def _need_gpu():
+    import torch
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype", [dm.TYPE_F16, dm.TYPE_Q8_0, dm.TYPE_Q4_K])
+@pytest.mark.parametrize("n", [32, 64, 50, 1])
+def test_tiny_layer(qtype, n):
+    check_layer(tiny(qtype), n)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype", [dm.TYPE_Q8_0, dm.TYPE_Q4_K])
+def test_tiny_variants(qtype):
+    check_layer(tiny(qtype, Is=0), 64)                         # no shared expert
+    check_layer(tiny(qtype, bias="none"), 64)                  # no expert bias
+    check_layer(tiny(qtype, norm_topk=0, scale=1.0), 64)      # no renormalisation / scaling
+    check_layer(tiny(qtype, shared_type=dm.TYPE_F16), 96)     # shared expert in another type
+    check_layer(tiny(qtype, I=512, Is=256, E=32, top_k=8, cap=12), 128)
+
+
+@pytest.mark.gpu
+def test_c1_f16_one_block():
+    err, _ = check_layer(synth.config("c1"), 32)
+    print("c1 rel L2", err)
+
+
+@pytest.mark.gpu
+@pytest.mark.slow
+def test_c2_q8_0_64_blocks():
+    err, _ = check_layer(synth.config("c2"), 2048)
+    print("c2 rel L2", err)
+
+
+@pytest.mark.gpu
+@pytest.mark.slow
+def test_c3_q4k_1_and_8_blocks():
+    spec = synth.config("c3")
+    t = synth.make_layer(spec)
+    L = dm.MoELayer(spec.hparams(), t)
+    for n in (32, 256):
+        err, _ = check_layer(spec, n, t=t, layer=L)
+        print("c3", n, "rel L2", err)
