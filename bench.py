@@ -1,0 +1,305 @@
+"""Benchmark of the block-routed MoE layer (BASELINE metric: MoE-layer tokens/s and HBM GB/s,
+256 experts, top-8, q4_K, at 1/2/4/8 B200).
+
+Workload: the LLaDA2.2-flash-shaped layer (hidden 4096, 256 routed SwiGLU experts of width 1024,
+one shared expert of width 1024, fp32 router, capacity 48 per 32-token block, top-8, x2.5) with
+q4_K weights quantised from F16 ~N(0, 0.02), on 256 blocks x 32 tokens of RMS-normalised
+N(0, 1) inputs per GPU (synthetic: no dataset exists for this path). The weights (1.8 GB) and
+the per-step activations exceed the 126 MB L2, so no extra flush is needed between steps.
+
+One step = one dmoe_forward over the GPU's 8192 tokens. `value` is device-resident throughput
+(inputs already in HBM); `e2e` goes through the public C ABI with pinned host buffers (H2D of x,
+D2H of out inside the timed region). With N > 1 (torchrun), every rank runs its own token shard
+(weak scaling); the timing is the max over ranks.
+
+`--impl reference` times the reference's CPU algorithm on the host cores instead: the ggml CPU
+path cannot be built (its ggml submodule is empty), so this is the C restatement in oracle/
+(fp32, OpenMP), on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "diffuse-cpp_b200"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "moe_layer_tokens_per_s"
+UNIT = "tokens/s"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic(key: str):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(key)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.send_signal(signal.SIGTERM)
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [c.strip() for c in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def algorithmic(spec, n_tokens: int, n_active: int):
+    import synth
+
+    B = (n_active * synth.expert_bytes(spec) + synth.shared_bytes(spec) + 4 * spec.H * spec.E + 4 * spec.E
+         + 8 * n_tokens * spec.H)
+    F = n_tokens * synth.flops_per_token(spec)
+    gateup_flops = n_tokens * (spec.top_k * 4 * spec.H * spec.I + 4 * spec.H * spec.Is)
+    return B, F, gateup_flops
+
+
+def run_cpu_reference(spec, t, n_tokens: int, budget_s: float = 15.0):
+    """Times the CPU restatement (oracle, fp32, all host threads) on a bounded sample of blocks.
+    Returns (tokens_per_s, cores, sample_description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # CPU baseline leg only
+    import synth
+
+    cores = os.cpu_count() or 1
+    hp = spec.hparams()
+    nblk = 1
+    done_tok, elapsed = 0, 0.0
+    while elapsed < budget_s and done_tok < n_tokens:
+        x = synth.make_input(32 * nblk, spec.H, spec.seed + 1000 + done_tok)
+        t0 = time.perf_counter()
+        oracle.layer(hp, t, x, mode=1, nthreads=cores)
+        dt = time.perf_counter() - t0
+        done_tok += 32 * nblk
+        elapsed += dt
+        nblk = min(nblk * 2, 16)
+    return done_tok / elapsed, cores, f"{done_tok} tokens ({done_tok // 32} blocks of the workload) in {elapsed:.1f} s"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--blocks", type=int, default=256, help="32-token routing blocks per GPU")
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    import synth
+
+    spec = synth.config(args.config)
+    n_tok = 32 * args.blocks
+    cfg = {"workload": f"{args.config}: flash-shaped MoE layer H4096 E256 I1024 Is1024 top8 cap48 q4_K, "
+                       f"{args.blocks} blocks x 32 tokens per GPU",
+           "tokens_per_gpu": n_tok, "global_tokens": n_tok * args.gpus, "weights": "q4_K (synthetic F16 N(0,0.02))",
+           "l2": "working set > L2 (1.8 GB weights), no flush", "parallelism": f"token-sharded x{args.gpus}"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        t = synth.make_layer(spec)
+        tps, cores, sample = run_cpu_reference(spec, t, n_tok)
+        line = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1000.0 * n_tok / tps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+                "impl": "reference",
+                "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+                "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "note": "ggml CPU path unbuildable here (empty ggml submodule); oracle/ C restatement, fp32, OpenMP"}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import diffuse_moe as dm
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    peaks = load_peaks()
+    hp = spec.hparams()
+    t = synth.make_layer(spec)
+    layer = dm.MoELayer(hp, t, dist=dm.DistCfg(0, 1, local_rank, 0, None))
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        tt = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    def time_device(n: int, steps: int, warmup: int, profile_pass: bool = True):
+        x = torch.from_numpy(synth.make_input(n, spec.H, spec.seed + 17 * rank)).to(dev)
+        out = torch.empty((n, spec.H), dtype=torch.float32, device=dev)
+        for _ in range(warmup):
+            layer.forward(x, out=out)
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(steps):
+            layer.forward(x, out=out)
+        ev1.record(stream)
+        barrier()
+        ms = ev0.elapsed_time(ev1) / steps
+        layer.sync()
+        st = layer.stats()
+        prof = None
+        if profile_pass:  # per-stage CUDA events on the launching stream (separate, untimed pass)
+            stages = []
+            for _ in range(max(3, min(steps, 10))):
+                layer.forward(x, out=out, profile=True)
+                layer.sync()
+                stages.append(layer.stats())
+            prof = {k: float(np.median([s[k] for s in stages])) for k in
+                    ("ms_router", "ms_dispatch", "ms_gateup", "ms_down", "ms_total")}
+        return max_over_ranks(ms), st, prof
+
+    peaks_hbm = peaks["hbm_gbs"]
+    sweep = []
+    if not args.no_sweep and world == 1:
+        for nb in (1, 8, 64):
+            n = 32 * nb
+            ms, st, prof = time_device(n, max(args.steps, 20), args.warmup)
+            B, F, _ = algorithmic(spec, n, st["n_active"])
+            t_roof = max(B / (peaks_hbm * 1e9), F / (peaks["bf16_tflops"] * 1e12))
+            sweep.append({"blocks": nb, "tokens": n, "ms": ms, "tokens_per_s": n / (ms / 1e3),
+                          "hbm_gbs": B / (ms / 1e3) / 1e9, "tflops": F / (ms / 1e3) / 1e12,
+                          "n_active": st["n_active"], "roofline_frac": t_roof / (ms / 1e3),
+                          "bound": "hbm" if B / (peaks_hbm * 1e9) >= F / (peaks["bf16_tflops"] * 1e12) else "tensor",
+                          "stages_ms": prof, "token_tile": st["token_tile"], "ksplit": [st["ksplit_gateup"],
+                                                                                        st["ksplit_down"]]})
+
+    # ---- headline: device-resident throughput on this GPU's token shard
+    with ClockSampler(torch.cuda.current_device()) as cs:
+        ms, st, prof = time_device(n_tok, args.steps, args.warmup)
+    clocks = cs.summary()
+    B, F, gu_flops = algorithmic(spec, n_tok, st["n_active"])
+    value = n_tok * world / (ms / 1e3)
+
+    # ---- e2e through the public API with pinned host buffers
+    xh = torch.from_numpy(synth.make_input(n_tok, spec.H, spec.seed + 17 * rank)).pin_memory().numpy()
+    oh = torch.empty((n_tok, spec.H), dtype=torch.float32).pin_memory().numpy()
+    for _ in range(args.warmup):
+        layer.forward(xh, out=oh)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        layer.forward(xh, out=oh)
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+    e2e = {"value": n_tok * world / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(xh.nbytes),
+           "d2h_bytes_per_step": int(oh.nbytes), "ms_per_step": e2e_s * 1e3}
+
+    # ---- roofline of the dominant kernel (gate/up grouped GEMM: 2/3 of the layer's flops)
+    gu_ms = prof["ms_gateup"]
+    achieved = gu_flops / (gu_ms / 1e3) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    roofline = {"kernel": "moe_gemm_kernel<q4_K, gate/up>", "bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic(f"gateup_{args.blocks}blk"),
+                "peak_source": f"{peaks['source']} bf16 sustained",
+                "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms}
+    t_roof = max(B / (peaks_hbm * 1e9), F / (peaks["bf16_tflops"] * 1e12))
+    layer_roof = {"bytes": B, "flops": F, "hbm_gbs": B / (ms / 1e3) / 1e9, "tflops": F / (ms / 1e3) / 1e12,
+                  "frac": t_roof / (ms / 1e3), "peak_source": peaks["source"]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tps, cores, sample = run_cpu_reference(spec, t, n_tok)
+        cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16",
+                "precision": "q4_K weights dequantised to fp16, fp16 activations, fp32 accumulation",
+                "data": "synthetic", "config": cfg, "e2e": e2e, "roofline": roofline, "layer_roofline": layer_roof,
+                "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": int(st["kernels"]) * args.steps,
+                "stages_ms": prof, "n_active": st["n_active"], "token_tile": st["token_tile"],
+                "ksplit": [st["ksplit_gateup"], st["ksplit_down"]], "sweep": sweep}
+        print(json.dumps(line))
+    layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

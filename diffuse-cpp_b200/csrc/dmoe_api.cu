@@ -168,7 +168,7 @@ struct dmoe_layer {
   int device = 0, sms = 148;
   cudaStream_t own_stream = nullptr;
   // weights
-  float* wr = nullptr;
+  float* wr = nullptr;  // router weight transposed, [H][E]
   float* br = nullptr;
   DevWeight gate, up, down, sgate, sup, sdown;
   // workspace (grown, never shrunk)
@@ -191,7 +191,7 @@ struct dmoe_layer {
   int32_t* host_counters = nullptr;  // pinned: n_tiles, n_active
   cudaEvent_t ev[6] = {};
   bool profiled = false;
-  cudaStream_t last_stream = nullptr;
+  cudaStream_t last_stream = nullptr;  // stream of the last forward (NULL = default stream)
 };
 
 namespace {
@@ -202,7 +202,7 @@ dmoe_status validate(const dmoe_layer_desc* d) {
     return fail(DMOE_ERR_INVALID_ARG, "non-positive layer dimension");
   if (d->n_expert_used > 16 || d->n_expert_used > d->n_expert)
     return fail(DMOE_ERR_INVALID_ARG, "n_expert_used must be <= min(16, n_expert)");
-  if (d->n_expert > 1024) return fail(DMOE_ERR_UNSUPPORTED, "n_expert > 1024");
+  if (d->n_expert > 1024 || d->n_expert % 4) return fail(DMOE_ERR_UNSUPPORTED, "n_expert must be a multiple of 4, <= 1024");
   if (d->expert_capacity < 0 || d->moe_block_size < 0) return fail(DMOE_ERR_INVALID_ARG, "negative capacity/block");
   const int64_t tpb = d->moe_block_size > 1 ? std::max<int64_t>(d->moe_block_size, 32) : 32;
   if ((2 * tpb * d->n_expert + d->n_expert) * 4 > 200 * 1024)
@@ -314,9 +314,15 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
     return bail(fail(DMOE_ERR_CUDA, "stream create"));
   for (auto& e : L->ev)
     if (cudaEventCreate(&e) != cudaSuccess) return bail(fail(DMOE_ERR_CUDA, "event create"));
-  if (cudaMalloc(&L->wr, (size_t)L->E * L->H * 4) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "router alloc"));
-  if (cudaMemcpy(L->wr, d->w_router, (size_t)L->E * L->H * 4, cudaMemcpyHostToDevice) != cudaSuccess)
-    return bail(fail(DMOE_ERR_CUDA, "router upload"));
+  {
+    // router weight, stored transposed [H][E] so the logits kernel reads contiguous weight rows
+    std::vector<float> wrt((size_t)L->E * L->H);
+    for (int64_t e = 0; e < L->E; ++e)
+      for (int64_t k = 0; k < L->H; ++k) wrt[(size_t)k * L->E + e] = d->w_router[(size_t)e * L->H + k];
+    if (cudaMalloc(&L->wr, (size_t)L->E * L->H * 4) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "router alloc"));
+    if (cudaMemcpy(L->wr, wrt.data(), (size_t)L->E * L->H * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(fail(DMOE_ERR_CUDA, "router upload"));
+  }
   if (L->has_bias) {
     if (cudaMalloc(&L->br, (size_t)L->E * 4) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "bias alloc"));
     if (cudaMemcpy(L->br, d->b_router, (size_t)L->E * 4, cudaMemcpyHostToDevice) != cudaSuccess)
@@ -342,7 +348,7 @@ void dmoe_destroy(dmoe_layer* L) {
   if (!L) return;
   cudaSetDevice(L->device);
   if (L->own_stream) cudaStreamSynchronize(L->own_stream);
-  if (L->last_stream) cudaStreamSynchronize(L->last_stream);
+  cudaStreamSynchronize(L->last_stream);
   cudaFree(L->wr);
   cudaFree(L->br);
   for (DevWeight* w : {&L->gate, &L->up, &L->down, &L->sgate, &L->sup, &L->sdown}) free_weight(*w);
@@ -377,7 +383,10 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if (!route_only && n > 0 && !out) return fail(DMOE_ERR_INVALID_ARG, "null output");
   if (n * (1 + L->K) >= (1ll << 31)) return fail(DMOE_ERR_UNSUPPORTED, "too many tokens in one call");
   DMOE_CUDA(cudaSetDevice(L->device));
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : L->own_stream;
+  // device mode: the caller's stream as given (NULL = the CUDA default stream);
+  // host mode without a stream: the layer's own stream
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (host && !stream) st = L->own_stream;
   L->last_stream = st;
   L->profiled = prof;
   std::memset(&L->stats, 0, sizeof(L->stats));
@@ -585,8 +594,7 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
 dmoe_status dmoe_sync(dmoe_layer* L) {
   if (!L) return fail(DMOE_ERR_INVALID_ARG, "null layer");
   DMOE_CUDA(cudaSetDevice(L->device));
-  cudaStream_t st = L->last_stream ? L->last_stream : L->own_stream;
-  DMOE_CUDA(cudaStreamSynchronize(st));
+  DMOE_CUDA(cudaStreamSynchronize(L->last_stream));
   uint32_t e = 0;
   DMOE_CUDA(cudaMemcpy(&e, L->err, 4, cudaMemcpyDeviceToHost));
   L->stats.n_routed_tiles = L->host_counters[0];

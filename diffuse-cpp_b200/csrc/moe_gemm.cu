@@ -40,14 +40,17 @@ struct GemmCfg {
   // + 128 x 4 fp32 scales; f16 two SW128 boxes of 128 x 64.
   static constexpr int W_BYTES = (WT == WT_Q4_K) ? 128 * 144 : (WT == WT_Q8_0) ? (128 * 128 + 128 * 16) : (128 * 128 * 2);
   static constexpr int STAGE_BYTES = B_BYTES + MATS * W_BYTES;
-  static constexpr int SMEM_BUDGET = 227 * 1024 - 2048;
+  // per epilogue warp: a 16-column x 32-feature fp32 transpose tile (row pitch 33: no bank
+  // conflicts either way), so stores and reductions leave as 16-byte vectors
+  static constexpr int EPI_BYTES = ((8 * 16 * 33 * 4 + 1023) / 1024) * 1024;
+  static constexpr int SMEM_BUDGET = 227 * 1024 - 2048 - EPI_BYTES;
   static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
   static constexpr int ACC_COLS = MATS * NT;
   static constexpr int A_COLS = MATS * 64;
   static constexpr int NA_RAW = QUANT ? (512 - ACC_COLS) / A_COLS : 0;
   static constexpr int NA = NA_RAW > 4 ? 4 : NA_RAW;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   static constexpr int THREADS = 320;
   static constexpr int EMPTY_COUNT = QUANT ? 1 + 4 * (KB_PER_STAGE >= 2 ? 2 : 1) : 1;
   static_assert(STAGES >= 2, "smem ring needs two stages");
@@ -221,7 +224,8 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
   using C = GemmCfg<WT, MODE, NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  float* epi = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = full + C::STAGES;
   uint64_t* afull = empty + C::STAGES;
@@ -408,7 +412,8 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
       // ---------------------------------------------------------------- epilogue
       if (!role_wait(accfull, tile_seq & 1u, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
       tc_fence_after();
-      const int o = ti.mt * kMTile + row;  // output feature (gate/up: i, down: o)
+      const int obase = ti.mt * kMTile + quarter * 32;  // first output feature of this warp
+      float* scr = epi + (warp - 2) * (16 * 33);
 #pragma unroll 1
       for (int c0 = wg * (NT / 2); c0 < (wg + 1) * (NT / 2); c0 += 16) {
         uint32_t acc0[16];
@@ -418,43 +423,68 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
           tmem_ld16(tbase + lane_off + NT + c0, acc1);
           tmem_wait_ld();
           if (p.gu_acc == nullptr) {
-            const int oi = ((p.h_quad_swap >> ti.group) & 1) ? quad_swap(o) : o;
+            // h = silu(g) * u, stored as 16-byte chunks of the (possibly quad-swapped) h row
+            const int pl = ((p.h_quad_swap >> ti.group) & 1) ? quad_swap(lane) : lane;
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
+            for (int c = 0; c < 16; ++c)
+              scr[c * 33 + pl] = silu_f(__uint_as_float(acc0[c])) * __uint_as_float(acc1[c]);
+            __syncwarp();
+#pragma unroll
+            for (int it = 0; it < 2; ++it) {
+              const int idx = it * 32 + lane, c = idx >> 2, j = idx & 3;
               if (c0 + c < ti.nrows) {
-                const float g = __uint_as_float(acc0[c]);
-                const float u = __uint_as_float(acc1[c]);
-                p.hbuf[(int64_t)(ti.row0 + c0 + c) * p.h_ld + oi] = __float2half_rn(silu_f(g) * u);
+                const float* sp = scr + c * 33 + 8 * j;
+                uint4 v;
+                v.x = as_u32(__floats2half2_rn(sp[0], sp[1]));
+                v.y = as_u32(__floats2half2_rn(sp[2], sp[3]));
+                v.z = as_u32(__floats2half2_rn(sp[4], sp[5]));
+                v.w = as_u32(__floats2half2_rn(sp[6], sp[7]));
+                *reinterpret_cast<uint4*>(p.hbuf + (int64_t)(ti.row0 + c0 + c) * p.h_ld + obase + 8 * j) = v;
               }
             }
+            __syncwarp();
           } else {
+            // split-K: fp32 partial sums of g and u, reduced with 16-byte vector atomics
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              if (c0 + c < ti.nrows) {
-                float* dst = p.gu_acc + (int64_t)(ti.row0 + c0 + c) * (2 * p.gu_half);
-                atomicAdd(dst + o, __uint_as_float(acc0[c]));
-                atomicAdd(dst + p.gu_half + o, __uint_as_float(acc1[c]));
+            for (int half = 0; half < 2; ++half) {
+#pragma unroll
+              for (int c = 0; c < 16; ++c) scr[c * 33 + lane] = __uint_as_float(half ? acc1[c] : acc0[c]);
+              __syncwarp();
+#pragma unroll
+              for (int it = 0; it < 4; ++it) {
+                const int idx = it * 32 + lane, c = idx >> 3, g4 = idx & 7;
+                if (c0 + c < ti.nrows) {
+                  const float* sp = scr + c * 33 + 4 * g4;
+                  float* dst = p.gu_acc + (int64_t)(ti.row0 + c0 + c) * (2 * p.gu_half) + half * p.gu_half + obase +
+                               4 * g4;
+                  atomicAdd(reinterpret_cast<float4*>(dst), make_float4(sp[0], sp[1], sp[2], sp[3]));
+                }
               }
+              __syncwarp();
             }
           }
         } else {
           tmem_wait_ld();
+          // out[tok] += w * y: transpose so each lane reduces 4 consecutive features of a token
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
+            float wgt = 1.0f;
+            if (ti.group != 0) wgt = (c0 + c < ti.nrows) ? p.pair_w[ti.row0 + c0 + c] : 0.0f;
+            scr[c * 33 + lane] = __uint_as_float(acc0[c]) * wgt;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int idx = it * 32 + lane, c = idx >> 3, g4 = idx & 7;
             if (c0 + c < ti.nrows) {
               const int r = ti.row0 + c0 + c;
-              int64_t tok;
-              float wgt;
-              if (ti.group == 0) {
-                tok = r;
-                wgt = 1.0f;
-              } else {
-                tok = p.pair_tok[r];
-                wgt = p.pair_w[r];
-              }
-              atomicAdd(p.out + tok * p.out_ld + o, __uint_as_float(acc0[c]) * wgt);
+              const int64_t tok = ti.group == 0 ? (int64_t)r : (int64_t)p.pair_tok[r];
+              const float* sp = scr + c * 33 + 4 * g4;
+              atomicAdd(reinterpret_cast<float4*>(p.out + tok * p.out_ld + obase + 4 * g4),
+                        make_float4(sp[0], sp[1], sp[2], sp[3]));
             }
           }
+          __syncwarp();
         }
       }
       tc_fence_before();

@@ -55,75 +55,97 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Router logits: a 32-token x 64-expert tile per CTA (128 threads, 4 x 4 outputs each), over
-// router segments [s_begin, s_end). With one segment per CTA (grid.z = #segments) it writes
-// the segment partials P_s, which route_kernel sums in order; with all segments in one CTA it
-// keeps the running sum tot = P_0 + ... + P_s itself. Both give the canonical bits.
+// Router logits: a 32-token x 64-expert tile per CTA over router segments [s_begin, s_end).
+// `wrt` is the router weight transposed to [h][e] (done once at bind time) so weight tiles are
+// contiguous rows. Two shapes of the same arithmetic:
+//   <4, 4, 128>: 128 threads x (4 tokens x 4 experts); one segment per CTA (grid.z = #segments),
+//                writing the segment partials P_s that route_kernel sums in order (small N);
+//   <8, 8, 32>:  32 threads x (8 tokens x 8 experts); all segments in one CTA with the running
+//                sum tot = P_0 + P_1 + ... (large N, 1024+ CTAs).
+// Both produce the canonical bits.
 // ------------------------------------------------------------------------------------------
 constexpr int RL_TOK = 32, RL_EXP = 64, RL_KC = 64;
 
-__global__ void __launch_bounds__(128) router_logits_kernel(const float* __restrict__ x, const float* __restrict__ wr,
+template <int TM, int TN, int NTH>
+__global__ void __launch_bounds__(NTH) router_logits_kernel(const float* __restrict__ x, const float* __restrict__ wrt,
                                                             float* __restrict__ part, int64_t n, int h, int e,
                                                             int segs_per_cta) {
+  static_assert((RL_TOK / TM) * (RL_EXP / TN) == NTH, "thread tiles cover the CTA tile");
   __shared__ __align__(16) float xs[RL_KC][RL_TOK + 4];
-  __shared__ __align__(16) float ws[RL_KC][RL_EXP + 4];
+  __shared__ __align__(16) float ws[RL_KC][RL_EXP];
   const int tid = threadIdx.x;
-  const int tq = tid >> 4;  // token quad: tokens 4 tq .. 4 tq + 3
-  const int te = tid & 15;  // expert quad: experts 4 te .. 4 te + 3
+  constexpr int NX = RL_EXP / TN;
+  const int ty = tid / NX;  // tokens TM ty ..
+  const int tx = tid % NX;  // experts TN tx ..
   const int64_t t0 = (int64_t)blockIdx.x * RL_TOK;
   const int e0 = blockIdx.y * RL_EXP;
   const int nseg = (h + kRouterSeg - 1) / kRouterSeg;
   const int s_begin = blockIdx.z * segs_per_cta;
   const int s_end = min(nseg, s_begin + segs_per_cta);
-  float tot[4][4], acc[4][4];
+  float tot[TM][TN], acc[TM][TN];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < TM; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) tot[i][j] = 0.0f;
+    for (int j = 0; j < TN; ++j) tot[i][j] = 0.0f;
   for (int s = s_begin; s < s_end; ++s) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < TM; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+      for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
     const int k_end = min(h, (s + 1) * kRouterSeg);
     for (int kc = s * kRouterSeg; kc < k_end; kc += RL_KC) {
       const int klen = min(RL_KC, k_end - kc);
       __syncthreads();
-      // x tile: 32 tokens x 64 k -> xs[k][t]
-      for (int idx = tid; idx < RL_TOK * RL_KC; idx += 128) {
-        const int t = idx / RL_KC, k = idx % RL_KC;
+      // x tile: 32 tokens x 64 k (float4 along k) -> xs[k][t]
+      for (int q = tid; q < RL_TOK * (RL_KC / 4); q += NTH) {
+        const int t = q / (RL_KC / 4), k4 = q % (RL_KC / 4);
         const int64_t tok = t0 + t;
-        xs[k][t] = (tok < n && k < klen) ? x[tok * h + kc + k] : 0.0f;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tok < n && 4 * k4 < klen) v = *reinterpret_cast<const float4*>(x + tok * h + kc + 4 * k4);
+        xs[4 * k4 + 0][t] = v.x;
+        xs[4 * k4 + 1][t] = v.y;
+        xs[4 * k4 + 2][t] = v.z;
+        xs[4 * k4 + 3][t] = v.w;
       }
-      for (int idx = tid; idx < RL_EXP * RL_KC; idx += 128) {
-        const int ee = idx / RL_KC, k = idx % RL_KC;
-        ws[k][ee] = (e0 + ee < e && k < klen) ? wr[(int64_t)(e0 + ee) * h + kc + k] : 0.0f;
+      // weight tile: 64 k rows x 64 experts, contiguous in wrt
+      for (int q = tid; q < RL_KC * (RL_EXP / 4); q += NTH) {
+        const int k = q / (RL_EXP / 4), e4 = q % (RL_EXP / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < klen && e0 + 4 * e4 < e) v = *reinterpret_cast<const float4*>(wrt + (int64_t)(kc + k) * e + e0 + 4 * e4);
+        *reinterpret_cast<float4*>(&ws[k][4 * e4]) = v;
       }
       __syncthreads();
       for (int k = 0; k < klen; ++k) {
-        const float4 xv = *reinterpret_cast<const float4*>(&xs[k][4 * tq]);
-        const float4 wv = *reinterpret_cast<const float4*>(&ws[k][4 * te]);
-        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-        const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+        float xa[TM], wa[TN];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < TM; i += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(&xs[k][TM * ty + i]);
+          xa[i] = v.x; xa[i + 1] = v.y; xa[i + 2] = v.z; xa[i + 3] = v.w;
+        }
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(xa[i], wa[j], acc[i][j]);
+        for (int j = 0; j < TN; j += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(&ws[k][TN * tx + j]);
+          wa[j] = v.x; wa[j + 1] = v.y; wa[j + 2] = v.z; wa[j + 3] = v.w;
+        }
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(xa[i], wa[j], acc[i][j]);
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < TM; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) tot[i][j] = (s == s_begin) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
+      for (int j = 0; j < TN; ++j) tot[i][j] = (s == s_begin) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
   }
   float* dst = part + (int64_t)blockIdx.z * n * e;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t tok = t0 + 4 * tq + i;
+  for (int i = 0; i < TM; ++i) {
+    const int64_t tok = t0 + TM * ty + i;
     if (tok >= n) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int ee = e0 + 4 * te + j;
+    for (int j = 0; j < TN; ++j) {
+      const int ee = e0 + TN * tx + j;
       if (ee < e) dst[tok * e + ee] = tot[i][j];
     }
   }
@@ -151,8 +173,17 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
   for (int idx = tid; idx < ntok * a.e; idx += blockDim.x) {
     const int t = idx / a.e, ee = idx % a.e;
     const int64_t off = (t0 + t) * a.e + ee;
+    // partials P_0 .. P_{nparts-1}: loads issued together, summed left to right
+    const int64_t pstride = a.n * a.e;
     float l = a.part[off];
-    for (int q = 1; q < a.nparts; ++q) l = __fadd_rn(l, a.part[(int64_t)q * a.n * a.e + off]);
+    for (int q0 = 1; q0 < a.nparts; q0 += 8) {
+      float pv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) pv[u] = (q0 + u < a.nparts) ? a.part[(int64_t)(q0 + u) * pstride + off] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < a.nparts) l = __fadd_rn(l, pv[u]);
+    }
     const float pv = sigmoid_canonical(l);
     ps[t * a.e + ee] = pv;
     ss[t * a.e + ee] = a.bias ? __fadd_rn(pv, a.bias[ee]) : pv;
@@ -244,12 +275,16 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
   }
 }
 
-cudaError_t launch_router(const float* x, const float* wr, float* part, int64_t n, int h, int e, int nparts,
+// nparts must be 1 (running sum) or the number of segments (one partial per segment).
+cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, int nparts,
                           cudaStream_t st) {
   const int nseg = (h + kRouterSeg - 1) / kRouterSeg;
-  const int segs_per_cta = (nseg + nparts - 1) / nparts;
+  if (nparts != 1 && nparts != nseg) return cudaErrorInvalidValue;
   dim3 grid((unsigned)((n + RL_TOK - 1) / RL_TOK), (unsigned)((e + RL_EXP - 1) / RL_EXP), (unsigned)nparts);
-  router_logits_kernel<<<grid, 128, 0, st>>>(x, wr, part, n, h, e, segs_per_cta);
+  if (nparts == 1)
+    router_logits_kernel<8, 8, 32><<<grid, 32, 0, st>>>(x, wrt, part, n, h, e, nseg);
+  else
+    router_logits_kernel<4, 4, 128><<<grid, 128, 0, st>>>(x, wrt, part, n, h, e, 1);
   return cudaGetLastError();
 }
 

@@ -251,7 +251,7 @@ class MoELayer:
             ro = RouteOut(_ptr(idx), _ptr(w), _ptr(allowed))
             routes = (idx, w, allowed)
         _check(lib.dmoe_forward(self._h, _ptr(x), n, _ptr(out), ctypes.byref(ro) if ro is not None else None,
-                                stream or None, flags))
+                                stream if stream else None, flags))
         if route or route_only:
             return (out, routes) if not route_only else routes
         return out

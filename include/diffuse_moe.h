@@ -128,8 +128,9 @@ dmoe_status dmoe_create(const dmoe_layer_desc* desc, const dmoe_dist_cfg* dist, 
 /* moe_out = MoE(x). Replaces src/diffuse-moe-graph.cpp:195-287 (router :203-262, experts
  * :264-278, shared expert :280-286). x and out are [n_tokens][n_embd] f32, row-major (ggml
  * ne = [n_embd, n_tokens]). Without DMOE_F_HOST_PTRS they are device pointers and the work is
- * enqueued on `stream` (a cudaStream_t; NULL = the layer's own stream); call dmoe_sync before
- * reading results. Block routing is used iff moe_block_size > 1, 0 < expert_capacity <
+ * enqueued on `stream` (a cudaStream_t, NULL = the CUDA default stream); call dmoe_sync (or
+ * synchronise the stream) before reading results. With DMOE_F_HOST_PTRS a NULL stream selects
+ * the layer's own stream and the call returns when the results are on the host. Block routing is used iff moe_block_size > 1, 0 < expert_capacity <
  * n_expert and n_tokens % moe_block_size == 0 (:215-216); otherwise plain per-token top-k.
  * Calls on one layer handle are not reentrant. */
 dmoe_status dmoe_forward(struct dmoe_layer* layer, const float* x, int64_t n_tokens, float* out,
