@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -172,7 +173,9 @@ struct dmoe_layer {
   float* br = nullptr;
   DevWeight gate, up, down, sgate, sup, sdown;
   // workspace (grown, never shrunk)
-  float* parts = nullptr; size_t parts_cap = 0;
+  float* parts = nullptr; size_t parts_cap = 0;    // router segment partials (split path)
+  float* probs = nullptr; size_t probs_cap = 0;      // sigmoid(router logits)
+  float* sel = nullptr; size_t sel_cap = 0;          // probs + expert bias
   int32_t* idx = nullptr; size_t idx_cap = 0;
   float* wts = nullptr; size_t wts_cap = 0;
   uint8_t* allowed = nullptr; size_t allowed_cap = 0;
@@ -215,6 +218,7 @@ dmoe_status validate(const dmoe_layer_desc* d) {
     return fail(DMOE_ERR_INVALID_ARG, "null shared-expert weight pointer");
   auto kmul = [](int32_t t) { return t == DMOE_TYPE_Q4_K ? 256 : 128; };
   const int64_t H = d->n_embd, I = d->n_ff_exp, Is = d->n_ff_shexp;
+  if (H % kRouterSeg) return fail(DMOE_ERR_UNSUPPORTED, "n_embd must be a multiple of %d (router segments)", kRouterSeg);
   if (H % 128 || H % kmul(d->expert_type) || I % kmul(d->expert_type))
     return fail(DMOE_ERR_UNSUPPORTED, "n_embd / n_ff_exp must be multiples of %d for type %d", kmul(d->expert_type),
                 d->expert_type);
@@ -223,19 +227,41 @@ dmoe_status validate(const dmoe_layer_desc* d) {
   return DMOE_OK;
 }
 
+// Tuning overrides (DMOE_NT = 32 / 64 / 128, DMOE_KSPLIT_GU / DMOE_KSPLIT_DN = 1 / 2 / 4 / 8);
+// unset or invalid values keep the automatic choice.
+int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  if (!v || !*v) return dflt;
+  return atoi(v);
+}
+
 int pick_nt(const dmoe_layer* L, int64_t n) {
+  const int forced = env_int("DMOE_NT", 0);
+  if (forced == 32 || forced == 64 || forced == 128) return forced;
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < L->E && n % L->blk == 0;
   const int64_t pairs = n * L->K;
   int64_t active = std::min<int64_t>(L->E, pairs);
   if (use_block) active = std::min<int64_t>(active, L->cap * (n / L->blk));
+  // weights are streamed once per token tile: size the tile for the busiest expert, whose
+  // count is at most n (each token picks an expert once) and is estimated as 3x the mean + 8
   const double avg = active > 0 ? (double)pairs / (double)active : 0.0;
-  if (avg <= 24.0) return 32;
-  if (avg <= 80.0) return 64;
+  const double busiest = std::min((double)n, 3.0 * avg + 8.0);
+  if (busiest <= 32.0) return 32;
+  if (busiest <= 64.0) return 64;
   return 128;
 }
 
 // Smallest power-of-two split (<= 8) dividing every K-stage count that gives >= 4 waves.
 int pick_ksplit(int64_t tiles_est, int sms, std::initializer_list<int> kstages) {
+  // Measured on B200: the per-tile epilogue and pipeline refill cost more than the wave
+  // quantisation they remove, at every block count, so split-K is off unless forced.
+  (void)tiles_est;
+  (void)sms;
+  (void)kstages;
+  return 1;
+}
+
+[[maybe_unused]] int pick_ksplit_waves(int64_t tiles_est, int sms, std::initializer_list<int> kstages) {
   int best = 1;
   for (int s = 2; s <= 8; s *= 2) {
     if (tiles_est * (best) >= 4LL * sms) break;
@@ -353,6 +379,8 @@ void dmoe_destroy(dmoe_layer* L) {
   cudaFree(L->br);
   for (DevWeight* w : {&L->gate, &L->up, &L->down, &L->sgate, &L->sup, &L->sdown}) free_weight(*w);
   cudaFree(L->parts);
+  cudaFree(L->probs);
+  cudaFree(L->sel);
   cudaFree(L->idx);
   cudaFree(L->wts);
   cudaFree(L->allowed);
@@ -397,14 +425,19 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   const int64_t Imax = std::max(L->I, L->Is);
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;
   const int nseg = (int)((H + kRouterSeg - 1) / kRouterSeg);
-  const int64_t rl_ctas = ((n + 31) / 32) * ((E + 63) / 64);
-  const int nparts = rl_ctas < 2LL * L->sms ? nseg : 1;
+  const int64_t rl_tiles = ((n + 31) / 32) * ((E + 63) / 64);
+  const bool rl_split = rl_tiles < 2LL * L->sms;  // too few 32x64 tiles to fill the GPU: split by segment
+  const int nparts = rl_split ? nseg : 1;
   const int nt = pick_nt(L, n);
 
   dmoe_status s;
   size_t dummy_cap;
   (void)dummy_cap;
-  if ((s = grow(L->parts, L->parts_cap, (size_t)nparts * n * E)) != DMOE_OK) return s;
+  if ((s = grow(L->probs, L->probs_cap, (size_t)n * E)) != DMOE_OK) return s;
+  if ((s = grow(L->sel, L->sel_cap, (size_t)n * E)) != DMOE_OK) return s;
+  if (rl_split) {
+    if ((s = grow(L->parts, L->parts_cap, (size_t)nseg * n * E)) != DMOE_OK) return s;
+  }
   if ((s = grow(L->idx, L->idx_cap, (size_t)n * K)) != DMOE_OK) return s;
   if ((s = grow(L->wts, L->wts_cap, (size_t)n * K)) != DMOE_OK) return s;
   if ((s = grow(L->ints, L->ints_cap, (size_t)3 * E + 8)) != DMOE_OK) return s;
@@ -431,12 +464,11 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
 
   // ---- router (src/diffuse-moe-graph.cpp:203-262)
   DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)E, st));
-  DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, nparts, st));
-  ++kernels;
+  DMOE_CUDA(launch_router(xd, L->wr, L->br, L->parts, L->probs, L->sel, n, (int)H, (int)E, rl_split, st));
+  kernels += rl_split ? 2 : 1;
   RouteArgs ra{};
-  ra.part = L->parts;
-  ra.nparts = nparts;
-  ra.bias = L->br;
+  ra.probs = L->probs;
+  ra.sel = L->sel;
   ra.n = n;
   ra.e = (int)E;
   ra.top_k = (int)K;
@@ -448,7 +480,6 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   ra.idx = (route && route->idx && !host) ? route->idx : L->idx;
   ra.w = (route && route->weights && !host) ? route->weights : L->wts;
   ra.allowed = use_block ? ((route && route->allowed && !host) ? route->allowed : L->allowed) : nullptr;
-  ra.probs = nullptr;
   ra.counts = counts;
   DMOE_CUDA(launch_route(ra, st));
   ++kernels;
@@ -488,6 +519,16 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
     const int64_t dn_tiles = (tt_est + sh_tt) * (H / kMTile);
     int ks_dn = pick_ksplit(dn_tiles, L->sms,
                             {(int)(L->I / gu_stage_r), L->has_shared ? (int)(L->Is / gu_stage_s) : (int)(L->I / gu_stage_r)});
+    {
+      const int f_gu = env_int("DMOE_KSPLIT_GU", 0), f_dn = env_int("DMOE_KSPLIT_DN", 0);
+      auto divides = [&](int ks, int64_t k_r, int64_t k_s) {
+        return ks >= 1 && ks <= 8 && (ks & (ks - 1)) == 0 && k_r % ks == 0 && k_s % ks == 0;
+      };
+      const int64_t gr = H / gu_stage_r, gs = L->has_shared ? H / gu_stage_s : gr;
+      const int64_t dr = L->I / gu_stage_r, ds = L->has_shared ? L->Is / gu_stage_s : dr;
+      if (divides(f_gu, gr, gs) && (size_t)rows * 2 * Imax * 4 <= (256ull << 20)) ks_gu = f_gu;
+      if (divides(f_dn, dr, ds)) ks_dn = f_dn;
+    }
     if (ks_gu > 1) {
       if ((s = grow(L->gu, L->gu_cap, (size_t)rows * 2 * Imax)) != DMOE_OK) return s;
       DMOE_CUDA(cudaMemsetAsync(L->gu, 0, (size_t)rows * 2 * Imax * 4, st));
@@ -519,15 +560,16 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
     gp.tm_s[1][1] = L->up.tm_s;
     fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I);
     const int grid = L->sms;
+    const int ndq = env_int("DMOE_NDQ", 2);  // dequant warpgroups per CTA (2, 3 or 4)
     if (same_type) {
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, gp, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, gp, grid, st));
       ++kernels;
     } else {
       GemmParams g0 = gp, g1 = gp;
       g0.grp[1].present = 0;
       g1.grp[0].present = 0;
-      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, g0, grid, st));
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, g1, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, ndq, g0, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, g1, grid, st));
       kernels += 2;
     }
     if (ks_gu > 1) {
@@ -557,14 +599,14 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
     dp.tm_s[1][0] = L->down.tm_s;
     fill_group(dp.grp[1], L->down, L->etype, L->H, L->H);
     if (same_type) {
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, dp, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, dp, grid, st));
       ++kernels;
     } else {
       GemmParams d0 = dp, d1 = dp;
       d0.grp[1].present = 0;
       d1.grp[0].present = 0;
-      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, d0, grid, st));
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, d1, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, d0, grid, st));
+      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, d1, grid, st));
       kernels += 2;
     }
     if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));

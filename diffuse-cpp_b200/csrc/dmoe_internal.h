@@ -62,9 +62,8 @@ struct GemmParams {
 
 // Router: one routing block per CTA (src/diffuse-moe-graph.cpp:203-262).
 struct RouteArgs {
-  const float* part;   // [nparts][n][e] logit partials (segment partials, or the full logits)
-  int nparts;
-  const float* bias;   // [e] or null
+  const float* probs;  // [n][e] sigmoid(router logits), canonical bits
+  const float* sel;    // [n][e] probs + expert bias (selection scores)
   int64_t n;
   int e, top_k, cap, blk;
   int use_block;       // block routing switch, evaluated on the host (:215-216)
@@ -73,12 +72,11 @@ struct RouteArgs {
   int32_t* idx;        // [n][top_k]
   float* w;            // [n][top_k]
   uint8_t* allowed;    // [n / blk][e] or null
-  float* probs;        // [n][e] or null
   int32_t* counts;     // [e] per-expert pair counts (atomics; zeroed by the caller)
 };
 
-cudaError_t launch_router(const float* x, const float* wr, float* part, int64_t n, int h, int e, int nparts,
-                          cudaStream_t st);
+cudaError_t launch_router(const float* x, const float* wrt, const float* bias, float* part, float* probs, float* sel,
+                          int64_t n, int h, int e, bool split, cudaStream_t st);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
 cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, int32_t* off, int32_t* fill,
                               TokTile* tiles, int32_t* n_tiles, int32_t* n_active, cudaStream_t st);
@@ -87,7 +85,7 @@ cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int
                           int swap_shared, int swap_routed, int with_shared, cudaStream_t st);
 cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows, int64_t n, int is, int iw,
                                  __half* hbuf, int64_t h_ld, int swap_shared, int swap_routed, cudaStream_t st);
-cudaError_t launch_moe_gemm(int wtype, int mode, int nt, const GemmParams& p, int grid, cudaStream_t st);
+cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st);
 int gemm_stage_k(int wtype);
 
 // host-side codecs (quant.cpp)

@@ -29,7 +29,7 @@
 
 namespace dmoe {
 
-template <int WT, int MODE, int NT>
+template <int WT, int MODE, int NT, int NDQ_ = 2>
 struct GemmCfg {
   static constexpr bool QUANT = (WT != WT_F16);
   static constexpr int MATS = (MODE == MODE_GATEUP) ? 2 : 1;
@@ -40,23 +40,35 @@ struct GemmCfg {
   // + 128 x 4 fp32 scales; f16 two SW128 boxes of 128 x 64.
   static constexpr int W_BYTES = (WT == WT_Q4_K) ? 128 * 144 : (WT == WT_Q8_0) ? (128 * 128 + 128 * 16) : (128 * 128 * 2);
   static constexpr int STAGE_BYTES = B_BYTES + MATS * W_BYTES;
+  // roles: warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue, then NDQ dequant warpgroups
+  static constexpr int NDQ = QUANT ? NDQ_ : 0;
+  static constexpr int EPI_WARP0 = 2, DQ_WARP0 = 6;
+  static constexpr int THREADS = 32 * (DQ_WARP0 + 4 * NDQ);
   // per epilogue warp: a 16-column x 32-feature fp32 transpose tile (row pitch 33: no bank
   // conflicts either way), so stores and reductions leave as 16-byte vectors
-  static constexpr int EPI_BYTES = ((8 * 16 * 33 * 4 + 1023) / 1024) * 1024;
+  static constexpr int EPI_BYTES = ((4 * 16 * 33 * 4 + 1023) / 1024) * 1024;
   static constexpr int SMEM_BUDGET = 227 * 1024 - 2048 - EPI_BYTES;
   static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+  // TMEM: accumulators (double-buffered when they fit next to a 2+ deep A ring), A ring
   static constexpr int ACC_COLS = MATS * NT;
   static constexpr int A_COLS = MATS * 64;
-  static constexpr int NA_RAW = QUANT ? (512 - ACC_COLS) / A_COLS : 0;
+  static constexpr int ACC_BUFS = (2 * ACC_COLS + (QUANT ? 2 * A_COLS : 0) <= 512) ? 2 : 1;
+  static constexpr int NA_RAW = QUANT ? (512 - ACC_BUFS * ACC_COLS) / A_COLS : 0;
   static constexpr int NA = NA_RAW > 4 ? 4 : NA_RAW;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
-  static constexpr int THREADS = 320;
-  static constexpr int EMPTY_COUNT = QUANT ? 1 + 4 * (KB_PER_STAGE >= 2 ? 2 : 1) : 1;
+  // every dequant warp arrives on each stage's `empty` (after its own k-blocks, if any)
+  static constexpr int EMPTY_COUNT = 1 + 4 * NDQ;
   static_assert(STAGES >= 2, "smem ring needs two stages");
   static_assert(!QUANT || NA >= 2, "TMEM A ring needs two buffers");
   static_assert(B_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1024-B aligned stage parts");
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "tcgen05 M=128 needs N % 16 == 0");
+  static_assert(ACC_BUFS * ACC_COLS + NA * A_COLS <= 512, "TMEM budget");
+  // The dequant warpgroups share the A ring round-robin (k-block kbs -> group kbs % NDQ,
+  // buffer kbs % NA). A group then waits for buffer use u only after the MMA has consumed
+  // k-block kbs - NDQ - NA, which implies completion u - 1 of that buffer's `aempty` iff
+  // NA >= NDQ; with fewer buffers a parity wait could alias two completions ahead.
+  static constexpr bool RING_OK = !QUANT || NA >= NDQ;
 };
 
 struct TileInfo {
@@ -124,7 +136,9 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > DMOE_WAIT_NS) {
       atomicOr(err, errbit);
@@ -137,9 +151,12 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
 // ------------------------------------------------------------------------------------------
 // dequantisation of one 128-K block of one weight row into 64 TMEM columns (fp16 pairs)
 // ------------------------------------------------------------------------------------------
-// q4_K: `rowp` points at the row's 144-byte super-block in smem; kb selects K half 0/1.
-__device__ __forceinline__ void dequant_q4k_kblock(const uint8_t* rowp, int kb, uint32_t taddr) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(rowp);
+// q4_K: `rowp` = shared address of the row's 144-byte super-block; kb selects K half 0/1.
+// Low nibbles: (q & 0x000F000F) | 0x6400 -> 1024 + q, exact; minus 1024 -> q; fma(q, d, -m).
+// High nibbles: (q & 0x00F000F0) | 0x6400 -> 1024 + 16 q; minus 1024 -> 16 q (exact);
+// fma(16 q, d / 16, -m) with d / 16 an exact power-of-two rescaling of d (no shift needed).
+__device__ __forceinline__ void dequant_q4k_kblock(uint32_t rowp, int kb, uint32_t taddr) {
+  const uint4 hdr = lds128(rowp);
   const __half2 dd = as_h2(__byte_perm(hdr.x, 0, 0x1010));    // {d, d}
   const __half2 dmn = as_h2(__byte_perm(hdr.x, 0, 0x3232));   // {dmin, dmin}
   uint32_t scw, mw;
@@ -151,6 +168,7 @@ __device__ __forceinline__ void dequant_q4k_kblock(const uint8_t* rowp, int kb, 
     mw = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
   }
   const __half2 k1024 = __float2half2_rn(1024.0f);
+  const __half2 k1_16 = __float2half2_rn(0.0625f);
   // 6-bit ints -> fp16 exactly (magic 1024), then one rounding of d*sc / dmin*m
   const __half2 sc01 = __hsub2(as_h2(__byte_perm(scw, 0x64646464u, 0x5140)), k1024);
   const __half2 sc23 = __hsub2(as_h2(__byte_perm(scw, 0x64646464u, 0x5342)), k1024);
@@ -158,24 +176,26 @@ __device__ __forceinline__ void dequant_q4k_kblock(const uint8_t* rowp, int kb, 
   const __half2 mn23 = __hsub2(as_h2(__byte_perm(mw, 0x64646464u, 0x5342)), k1024);
   const __half2 dq01 = __hmul2(sc01, dd), dq23 = __hmul2(sc23, dd);
   const __half2 nm01 = __hneg2(__hmul2(mn01, dmn)), nm23 = __hneg2(__hmul2(mn23, dmn));
+  // all of this K half's quants (64 bytes) are loaded before the first TMEM store
+  const uint32_t qp = rowp + 16 + 64 * kb;
+  const uint4 q0 = lds128(qp), q1 = lds128(qp + 16), q2 = lds128(qp + 32), q3 = lds128(qp + 48);
 #pragma unroll
   for (int gl = 0; gl < 2; ++gl) {
     // sub-blocks 2 gl (low nibbles) and 2 gl + 1 (high nibbles) of this K half
     const __half2 dlo = gl == 0 ? __low2half2(dq01) : __low2half2(dq23);
-    const __half2 dhi = gl == 0 ? __high2half2(dq01) : __high2half2(dq23);
+    const __half2 dhi = __hmul2(gl == 0 ? __high2half2(dq01) : __high2half2(dq23), k1_16);
     const __half2 mlo = gl == 0 ? __low2half2(nm01) : __low2half2(nm23);
     const __half2 mhi = gl == 0 ? __high2half2(nm01) : __high2half2(nm23);
-    const uint4* qp = reinterpret_cast<const uint4*>(rowp + 16 + 32 * (2 * kb + gl));
-    const uint4 qa = qp[0], qb = qp[1];
+    const uint4 qa = gl == 0 ? q0 : q2, qb = gl == 0 ? q1 : q3;
     const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     uint32_t lo[16], hi[16];
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-      const uint32_t q = qw[w];
+      const uint32_t q = qw[w], q8 = q >> 8;
       const uint32_t v02 = lop3_and_or(q, 0x000F000Fu, 0x64006400u);
-      const uint32_t v13 = lop3_and_or(q >> 8, 0x000F000Fu, 0x64006400u);
-      const uint32_t h02 = lop3_and_or(q >> 4, 0x000F000Fu, 0x64006400u);
-      const uint32_t h13 = lop3_and_or(q >> 12, 0x000F000Fu, 0x64006400u);
+      const uint32_t v13 = lop3_and_or(q8, 0x000F000Fu, 0x64006400u);
+      const uint32_t h02 = lop3_and_or(q, 0x00F000F0u, 0x64006400u);
+      const uint32_t h13 = lop3_and_or(q8, 0x00F000F0u, 0x64006400u);
       lo[2 * w] = as_u32(__hfma2(__hsub2(as_h2(v02), k1024), dlo, mlo));
       lo[2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(v13), k1024), dlo, mlo));
       hi[2 * w] = as_u32(__hfma2(__hsub2(as_h2(h02), k1024), dhi, mhi));
@@ -186,21 +206,23 @@ __device__ __forceinline__ void dequant_q4k_kblock(const uint8_t* rowp, int kb, 
   }
 }
 
-// q8_0 (repacked): `qtile` = 128 x 128 int8 tile (128B-swizzled), `stile` = 128 x 4 fp32 scales.
-__device__ __forceinline__ void dequant_q80_kblock(const uint8_t* qtile, const uint8_t* stile, int row,
-                                                   uint32_t taddr) {
-  const float4 sc = *reinterpret_cast<const float4*>(stile + row * 16);
+// q8_0 (repacked): `qtile` = shared address of a 128 x 128 int8 tile (128B-swizzled), `stile` =
+// 128 x 4 fp32 scales.
+__device__ __forceinline__ void dequant_q80_kblock(uint32_t qtile, uint32_t stile, int row, uint32_t taddr) {
+  const float4 sc = lds128f(stile + row * 16);
   const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
   const __half2 k1152 = __float2half2_rn(1152.0f);
-  const uint8_t* rp = qtile + row * 128;
+  const uint32_t rp = qtile + row * 128;
+  uint4 qv8[8];  // the row's 128 quants, loaded before the first TMEM store
+#pragma unroll
+  for (int c = 0; c < 8; ++c) qv8[c] = lds128(rp + ((c ^ (row & 7)) << 4));
 #pragma unroll
   for (int blk = 0; blk < 4; ++blk) {
     const __half2 d2 = __float2half2_rn(scv[blk]);
     uint32_t r[16];
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
-      const int c = 2 * blk + cc;
-      const uint4 qv = *reinterpret_cast<const uint4*>(rp + ((c ^ (row & 7)) << 4));
+      const uint4 qv = qv8[2 * blk + cc];
       const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
@@ -219,9 +241,11 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)
 
 __device__ __forceinline__ int quad_swap(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
 
-template <int WT, int MODE, int NT>
-__global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant__ GemmParams p) {
-  using C = GemmCfg<WT, MODE, NT>;
+template <int WT, int MODE, int NT, int NDQ_>
+__global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
+    moe_gemm_kernel(const __grid_constant__ GemmParams p) {
+  using C = GemmCfg<WT, MODE, NT, NDQ_>;
+  static_assert(C::RING_OK, "A ring needs at least one buffer per dequant warpgroup");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* epi = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -231,8 +255,8 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
   uint64_t* afull = empty + C::STAGES;
   uint64_t* aempty = afull + 4;
   uint64_t* accfull = aempty + 4;
-  uint64_t* accempty = accfull + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 1);
+  uint64_t* accempty = accfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -247,8 +271,10 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
       mbar_init(&afull[a], 4);
       mbar_init(&aempty[a], 1);
     }
-    mbar_init(accfull, 1);
-    mbar_init(accempty, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], 4);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -313,8 +339,11 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
       uint32_t stage_seq = 0, tile_seq = 0;
       for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
         const TileInfo ti = decode_tile<NT>(p, t);
-        if (!role_wait(accempty, (tile_seq & 1u) ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) break;
+        const int ab = tile_seq % C::ACC_BUFS;
+        const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
+        if (!role_wait(&accempty[ab], aph ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) break;
         tc_fence_after();
+        const uint32_t dbase = tbase + ab * C::ACC_COLS;
         bool first = true;
         bool ok = true;
         for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
@@ -333,14 +362,14 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
               const uint32_t u = kbs / C::NA;
               if (!role_wait(&afull[a], u & 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
               tc_fence_after();
-              abuf = tbase + C::ACC_COLS + a * C::A_COLS;
+              abuf = tbase + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const uint64_t bdesc = sdesc_sw128(bbase + (kb * 2 + j / 4) * (NT * 128) + (j % 4) * 32, 1024);
 #pragma unroll
               for (int m = 0; m < C::MATS; ++m) {
-                const uint32_t dcol = tbase + m * NT;
+                const uint32_t dcol = dbase + m * NT;
                 if constexpr (C::QUANT) {
                   mma_f16_ts(dcol, abuf + m * 64 + 8 * j, bdesc, idesc, first ? 0u : 1u);
                 } else {
@@ -357,88 +386,52 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
           ++stage_seq;
         }
         if (!ok) break;
-        mma_commit(accfull);
+        mma_commit(&accfull[ab]);
         ++tile_seq;
       }
     }
-  } else {
-    // ------------------------------------------------------------------ dequant + epilogue
-    const int wg = (warp - 2) >> 2;          // 0 or 1
-    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;     // weight row inside the 128-row tile
+  } else if (warp < C::DQ_WARP0) {
+    // ------------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    uint32_t stage_seq = 0, tile_seq = 0;
+    const uint32_t scr = smem_u32(epi) + (warp - C::EPI_WARP0) * (16 * 33 * 4);
+    uint32_t tile_seq = 0;
     for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
       const TileInfo ti = decode_tile<NT>(p, t);
-      bool ok = true;
-      if constexpr (C::QUANT) {
-        for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
-          const int s = stage_seq % C::STAGES;
-          const uint32_t ph = (stage_seq / C::STAGES) & 1u;
-          const bool reads = (C::KB_PER_STAGE >= 2) || ((stage_seq & 1u) == (uint32_t)wg);
-          if (reads) {
-            if (!role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
-#pragma unroll
-            for (int kb = 0; kb < C::KB_PER_STAGE; ++kb) {
-              const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
-              if ((kbs & 1u) != (uint32_t)wg) continue;
-              const int a = kbs % C::NA;
-              const uint32_t u = kbs / C::NA;
-              if (!role_wait(&aempty[a], (u & 1u) ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
-              tc_fence_after();
-              const uint32_t abuf = tbase + lane_off + C::ACC_COLS + a * C::A_COLS;
-#pragma unroll
-              for (int m = 0; m < C::MATS; ++m) {
-                const uint8_t* wt = wtile_ptr(s, m);
-                if constexpr (WT == WT_Q4_K) {
-                  dequant_q4k_kblock(wt + row * 144, kb, abuf + m * 64);
-                } else {
-                  dequant_q80_kblock(wt, wt + 128 * 128, row, abuf + m * 64);
-                }
-              }
-              tmem_wait_st();
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&afull[a]);
-            }
-            if (!ok) break;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-          }
-          ++stage_seq;
-        }
-      }
-      if (!ok) break;
-      // ---------------------------------------------------------------- epilogue
-      if (!role_wait(accfull, tile_seq & 1u, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
+      const int ab = tile_seq % C::ACC_BUFS;
+      const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
+      if (!role_wait(&accfull[ab], aph, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
       tc_fence_after();
+      const uint32_t dbase = tbase + lane_off + ab * C::ACC_COLS;
       const int obase = ti.mt * kMTile + quarter * 32;  // first output feature of this warp
-      float* scr = epi + (warp - 2) * (16 * 33);
 #pragma unroll 1
-      for (int c0 = wg * (NT / 2); c0 < (wg + 1) * (NT / 2); c0 += 16) {
+      for (int c0 = 0; c0 < NT && c0 < ti.nrows; c0 += 16) {
         uint32_t acc0[16];
-        tmem_ld16(tbase + lane_off + c0, acc0);
+        tmem_ld16(dbase + c0, acc0);
         if constexpr (MODE == MODE_GATEUP) {
           uint32_t acc1[16];
-          tmem_ld16(tbase + lane_off + NT + c0, acc1);
+          tmem_ld16(dbase + NT + c0, acc1);
           tmem_wait_ld();
           if (p.gu_acc == nullptr) {
             // h = silu(g) * u, stored as 16-byte chunks of the (possibly quad-swapped) h row
             const int pl = ((p.h_quad_swap >> ti.group) & 1) ? quad_swap(lane) : lane;
 #pragma unroll
             for (int c = 0; c < 16; ++c)
-              scr[c * 33 + pl] = silu_f(__uint_as_float(acc0[c])) * __uint_as_float(acc1[c]);
+              sts32f(scr + (c * 33 + pl) * 4, silu_f(__uint_as_float(acc0[c])) * __uint_as_float(acc1[c]));
             __syncwarp();
 #pragma unroll
             for (int it = 0; it < 2; ++it) {
               const int idx = it * 32 + lane, c = idx >> 2, j = idx & 3;
               if (c0 + c < ti.nrows) {
-                const float* sp = scr + c * 33 + 8 * j;
+                const uint32_t sp = scr + (c * 33 + 8 * j) * 4;
+                float f[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) f[u] = lds32f(sp + 4 * u);
                 uint4 v;
-                v.x = as_u32(__floats2half2_rn(sp[0], sp[1]));
-                v.y = as_u32(__floats2half2_rn(sp[2], sp[3]));
-                v.z = as_u32(__floats2half2_rn(sp[4], sp[5]));
-                v.w = as_u32(__floats2half2_rn(sp[6], sp[7]));
+                v.x = as_u32(__floats2half2_rn(f[0], f[1]));
+                v.y = as_u32(__floats2half2_rn(f[2], f[3]));
+                v.z = as_u32(__floats2half2_rn(f[4], f[5]));
+                v.w = as_u32(__floats2half2_rn(f[6], f[7]));
                 *reinterpret_cast<uint4*>(p.hbuf + (int64_t)(ti.row0 + c0 + c) * p.h_ld + obase + 8 * j) = v;
               }
             }
@@ -448,16 +441,17 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
 #pragma unroll
-              for (int c = 0; c < 16; ++c) scr[c * 33 + lane] = __uint_as_float(half ? acc1[c] : acc0[c]);
+              for (int c = 0; c < 16; ++c) sts32f(scr + (c * 33 + lane) * 4, __uint_as_float(half ? acc1[c] : acc0[c]));
               __syncwarp();
 #pragma unroll
               for (int it = 0; it < 4; ++it) {
                 const int idx = it * 32 + lane, c = idx >> 3, g4 = idx & 7;
                 if (c0 + c < ti.nrows) {
-                  const float* sp = scr + c * 33 + 4 * g4;
+                  const uint32_t sp = scr + (c * 33 + 4 * g4) * 4;
                   float* dst = p.gu_acc + (int64_t)(ti.row0 + c0 + c) * (2 * p.gu_half) + half * p.gu_half + obase +
                                4 * g4;
-                  atomicAdd(reinterpret_cast<float4*>(dst), make_float4(sp[0], sp[1], sp[2], sp[3]));
+                  atomicAdd(reinterpret_cast<float4*>(dst),
+                            make_float4(lds32f(sp), lds32f(sp + 4), lds32f(sp + 8), lds32f(sp + 12)));
                 }
               }
               __syncwarp();
@@ -470,7 +464,7 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
           for (int c = 0; c < 16; ++c) {
             float wgt = 1.0f;
             if (ti.group != 0) wgt = (c0 + c < ti.nrows) ? p.pair_w[ti.row0 + c0 + c] : 0.0f;
-            scr[c * 33 + lane] = __uint_as_float(acc0[c]) * wgt;
+            sts32f(scr + (c * 33 + lane) * 4, __uint_as_float(acc0[c]) * wgt);
           }
           __syncwarp();
 #pragma unroll
@@ -479,9 +473,9 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
             if (c0 + c < ti.nrows) {
               const int r = ti.row0 + c0 + c;
               const int64_t tok = ti.group == 0 ? (int64_t)r : (int64_t)p.pair_tok[r];
-              const float* sp = scr + c * 33 + 4 * g4;
+              const uint32_t sp = scr + (c * 33 + 4 * g4) * 4;
               atomicAdd(reinterpret_cast<float4*>(p.out + tok * p.out_ld + obase + 4 * g4),
-                        make_float4(sp[0], sp[1], sp[2], sp[3]));
+                        make_float4(lds32f(sp), lds32f(sp + 4), lds32f(sp + 8), lds32f(sp + 12)));
             }
           }
           __syncwarp();
@@ -489,8 +483,51 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(accempty);
+      if (lane == 0) mbar_arrive(&accempty[ab]);
       ++tile_seq;
+    }
+  } else if constexpr (C::QUANT) {
+    // ------------------------------------------------------------------ dequant warpgroups
+    const int wg = (warp - C::DQ_WARP0) >> 2;  // 0 .. NDQ-1
+    const int quarter = warp & 3;              // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;       // weight row inside the 128-row tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint32_t stage_seq = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
+      const TileInfo ti = decode_tile<NT>(p, t);
+      for (int kc = ti.k0; kc < ti.k1; ++kc) {
+        const int s = stage_seq % C::STAGES;
+        const uint32_t ph = (stage_seq / C::STAGES) & 1u;
+        if (!role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
+#pragma unroll
+        for (int kb = 0; kb < C::KB_PER_STAGE; ++kb) {
+          const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
+          if ((int)(kbs % C::NDQ) != wg) continue;
+          const int a = kbs % C::NA;
+          const uint32_t u = kbs / C::NA;
+          if (!role_wait(&aempty[a], (u & 1u) ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t abuf = tbase + lane_off + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
+#pragma unroll
+          for (int m = 0; m < C::MATS; ++m) {
+            const uint32_t wt = smem_u32(wtile_ptr(s, m));
+            if constexpr (WT == WT_Q4_K) {
+              dequant_q4k_kblock(wt + row * 144, kb, abuf + m * 64);
+            } else {
+              dequant_q80_kblock(wt, wt + 128 * 128, row, abuf + m * 64);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[a]);
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        ++stage_seq;
+      }
     }
   }
 
@@ -507,42 +544,55 @@ __global__ void __launch_bounds__(320, 1) moe_gemm_kernel(const __grid_constant_
 // ------------------------------------------------------------------------------------------
 // launcher
 // ------------------------------------------------------------------------------------------
-template <int WT, int MODE, int NT>
+template <int WT, int MODE, int NT, int NDQ>
 static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t st) {
-  using C = GemmCfg<WT, MODE, NT>;
-  auto kern = moe_gemm_kernel<WT, MODE, NT>;
-  static bool attr_set = false;  // per instantiation; set once per process (all devices)
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  using C = GemmCfg<WT, MODE, NT, NDQ>;
+  auto kern = moe_gemm_kernel<WT, MODE, NT, NDQ>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
   kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(p);
   return cudaGetLastError();
 }
 
+// Launches with `ndq` dequant warpgroups when that configuration keeps NA >= NDQ, otherwise
+// with the largest smaller one that does (2 always does).
+template <int WT, int MODE, int NT>
+static cudaError_t launch_ndq(const GemmParams& p, int ndq, int grid, cudaStream_t st) {
+  if constexpr (WT == WT_F16) {
+    return launch_one<WT, MODE, NT, 2>(p, grid, st);
+  } else {
+    if constexpr (GemmCfg<WT, MODE, NT, 4>::RING_OK) {
+      if (ndq >= 4) return launch_one<WT, MODE, NT, 4>(p, grid, st);
+    }
+    if constexpr (GemmCfg<WT, MODE, NT, 3>::RING_OK) {
+      if (ndq >= 3) return launch_one<WT, MODE, NT, 3>(p, grid, st);
+    }
+    return launch_one<WT, MODE, NT, 2>(p, grid, st);
+  }
+}
+
 template <int WT, int MODE>
-static cudaError_t launch_nt(const GemmParams& p, int nt, int grid, cudaStream_t st) {
+static cudaError_t launch_nt(const GemmParams& p, int nt, int ndq, int grid, cudaStream_t st) {
   switch (nt) {
-    case 32: return launch_one<WT, MODE, 32>(p, grid, st);
-    case 64: return launch_one<WT, MODE, 64>(p, grid, st);
-    case 128: return launch_one<WT, MODE, 128>(p, grid, st);
+    case 32: return launch_ndq<WT, MODE, 32>(p, ndq, grid, st);
+    case 64: return launch_ndq<WT, MODE, 64>(p, ndq, grid, st);
+    case 128: return launch_ndq<WT, MODE, 128>(p, ndq, grid, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t launch_moe_gemm(int wtype, int mode, int nt, const GemmParams& p, int grid, cudaStream_t st) {
+cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st) {
   if (mode == MODE_GATEUP) {
     switch (wtype) {
-      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_GATEUP>(p, nt, grid, st);
-      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_GATEUP>(p, nt, grid, st);
-      case WT_F16: return launch_nt<WT_F16, MODE_GATEUP>(p, nt, grid, st);
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_GATEUP>(p, nt, ndq, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_GATEUP>(p, nt, ndq, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_GATEUP>(p, nt, ndq, grid, st);
     }
   } else {
     switch (wtype) {
-      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_DOWN>(p, nt, grid, st);
-      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_DOWN>(p, nt, grid, st);
-      case WT_F16: return launch_nt<WT_F16, MODE_DOWN>(p, nt, grid, st);
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_DOWN>(p, nt, ndq, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_DOWN>(p, nt, ndq, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_DOWN>(p, nt, ndq, grid, st);
     }
   }
   return cudaErrorInvalidValue;

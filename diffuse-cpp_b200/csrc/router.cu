@@ -55,143 +55,203 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Router logits: a 32-token x 64-expert tile per CTA over router segments [s_begin, s_end).
-// `wrt` is the router weight transposed to [h][e] (done once at bind time) so weight tiles are
-// contiguous rows. Two shapes of the same arithmetic:
-//   <4, 4, 128>: 128 threads x (4 tokens x 4 experts); one segment per CTA (grid.z = #segments),
-//                writing the segment partials P_s that route_kernel sums in order (small N);
-//   <8, 8, 32>:  32 threads x (8 tokens x 8 experts); all segments in one CTA with the running
-//                sum tot = P_0 + P_1 + ... (large N, 1024+ CTAs).
-// Both produce the canonical bits.
+// Router logits: one CTA = 64 threads computing a 32-token x 64-expert tile; thread (ty, tx)
+// owns tokens 4 ty .. 4 ty + 3 and experts {4 tx .. 4 tx + 3} u {32 + 4 tx .. 32 + 4 tx + 3}.
+// Tiles of x [token][k] and of the transposed router weight wrt [k][expert] (transposed once at
+// bind time) arrive by cp.async into a double-buffered shared-memory ring.
+//   SPLIT = false: one CTA runs every segment, keeping tot = P_0 + P_1 + ... (large N).
+//   SPLIT = true:  one CTA per (tile, segment) writes its segment partial P_s, and
+//                  router_finish_kernel sums P_0 .. P_{S-1} left to right (small N, where the
+//                  tiles alone cannot fill the GPU).
+// Both produce the canonical logits, turned into probs = sigmoid(logit) and selection scores
+// sel = probs + bias (src/diffuse-moe-graph.cpp:204-210).
 // ------------------------------------------------------------------------------------------
-constexpr int RL_TOK = 32, RL_EXP = 64, RL_KC = 64;
+constexpr int RL_TOK = 32, RL_EXP = 64, RL_KC = 64, RL_THREADS = 64;
+constexpr int RL_XP = RL_KC + 4;  // x tile row pitch (floats)
+constexpr int RL_SMEM = 2 * (RL_TOK * RL_XP + RL_KC * RL_EXP) * 4;
 
-template <int TM, int TN, int NTH>
-__global__ void __launch_bounds__(NTH) router_logits_kernel(const float* __restrict__ x, const float* __restrict__ wrt,
-                                                            float* __restrict__ part, int64_t n, int h, int e,
-                                                            int segs_per_cta) {
-  static_assert((RL_TOK / TM) * (RL_EXP / TN) == NTH, "thread tiles cover the CTA tile");
-  __shared__ __align__(16) float xs[RL_KC][RL_TOK + 4];
-  __shared__ __align__(16) float ws[RL_KC][RL_EXP];
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* __restrict__ x,
+                                                                   const float* __restrict__ wrt,
+                                                                   const float* __restrict__ bias,
+                                                                   float* __restrict__ part, float* __restrict__ probs,
+                                                                   float* __restrict__ sel, int64_t n, int h,
+                                                                   int e) {
+  extern __shared__ __align__(16) float rl_smem[];
+  const uint32_t xs0 = smem_u32(rl_smem);                     // [2][32][RL_XP]
+  const uint32_t ws0 = xs0 + 2 * RL_TOK * RL_XP * 4;          // [2][64 k][64 e]
   const int tid = threadIdx.x;
-  constexpr int NX = RL_EXP / TN;
-  const int ty = tid / NX;  // tokens TM ty ..
-  const int tx = tid % NX;  // experts TN tx ..
+  const int ty = tid >> 3, tx = tid & 7;
   const int64_t t0 = (int64_t)blockIdx.x * RL_TOK;
   const int e0 = blockIdx.y * RL_EXP;
-  const int nseg = (h + kRouterSeg - 1) / kRouterSeg;
-  const int s_begin = blockIdx.z * segs_per_cta;
-  const int s_end = min(nseg, s_begin + segs_per_cta);
-  float tot[TM][TN], acc[TM][TN];
+  const int nseg = h / kRouterSeg;
+  const int s_begin = SPLIT ? (int)blockIdx.z : 0;
+  const int s_end = SPLIT ? s_begin + 1 : nseg;
+  const int kc0 = s_begin * kRouterSeg, nchunks = (s_end - s_begin) * (kRouterSeg / RL_KC);
+
+  auto load_chunk = [&](int c, int buf) {
+    const int kc = kc0 + c * RL_KC;
+    const uint32_t xs = xs0 + buf * RL_TOK * RL_XP * 4, ws = ws0 + buf * RL_KC * RL_EXP * 4;
 #pragma unroll
-  for (int i = 0; i < TM; ++i)
-#pragma unroll
-    for (int j = 0; j < TN; ++j) tot[i][j] = 0.0f;
-  for (int s = s_begin; s < s_end; ++s) {
-#pragma unroll
-    for (int i = 0; i < TM; ++i)
-#pragma unroll
-      for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
-    const int k_end = min(h, (s + 1) * kRouterSeg);
-    for (int kc = s * kRouterSeg; kc < k_end; kc += RL_KC) {
-      const int klen = min(RL_KC, k_end - kc);
-      __syncthreads();
-      // x tile: 32 tokens x 64 k (float4 along k) -> xs[k][t]
-      for (int q = tid; q < RL_TOK * (RL_KC / 4); q += NTH) {
-        const int t = q / (RL_KC / 4), k4 = q % (RL_KC / 4);
-        const int64_t tok = t0 + t;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (tok < n && 4 * k4 < klen) v = *reinterpret_cast<const float4*>(x + tok * h + kc + 4 * k4);
-        xs[4 * k4 + 0][t] = v.x;
-        xs[4 * k4 + 1][t] = v.y;
-        xs[4 * k4 + 2][t] = v.z;
-        xs[4 * k4 + 3][t] = v.w;
-      }
-      // weight tile: 64 k rows x 64 experts, contiguous in wrt
-      for (int q = tid; q < RL_KC * (RL_EXP / 4); q += NTH) {
-        const int k = q / (RL_EXP / 4), e4 = q % (RL_EXP / 4);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (k < klen && e0 + 4 * e4 < e) v = *reinterpret_cast<const float4*>(wrt + (int64_t)(kc + k) * e + e0 + 4 * e4);
-        *reinterpret_cast<float4*>(&ws[k][4 * e4]) = v;
-      }
-      __syncthreads();
-      for (int k = 0; k < klen; ++k) {
-        float xa[TM], wa[TN];
-#pragma unroll
-        for (int i = 0; i < TM; i += 4) {
-          const float4 v = *reinterpret_cast<const float4*>(&xs[k][TM * ty + i]);
-          xa[i] = v.x; xa[i + 1] = v.y; xa[i + 2] = v.z; xa[i + 3] = v.w;
-        }
-#pragma unroll
-        for (int j = 0; j < TN; j += 4) {
-          const float4 v = *reinterpret_cast<const float4*>(&ws[k][TN * tx + j]);
-          wa[j] = v.x; wa[j + 1] = v.y; wa[j + 2] = v.z; wa[j + 3] = v.w;
-        }
-#pragma unroll
-        for (int i = 0; i < TM; ++i)
-#pragma unroll
-          for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(xa[i], wa[j], acc[i][j]);
-      }
+    for (int r = 0; r < (RL_TOK * RL_KC / 4) / RL_THREADS; ++r) {  // 8 per thread
+      const int q = tid + r * RL_THREADS, t = q >> 4, k4 = q & 15;
+      const bool ok = t0 + t < n;
+      const float* src = ok ? x + (t0 + t) * h + kc + 4 * k4 : x;
+      cp_async16(xs + (t * RL_XP + 4 * k4) * 4, src, ok);
     }
 #pragma unroll
-    for (int i = 0; i < TM; ++i)
+    for (int r = 0; r < (RL_KC * RL_EXP / 4) / RL_THREADS; ++r) {  // 16 per thread
+      const int q = tid + r * RL_THREADS, k = q >> 4, e4 = q & 15;
+      const bool ok = e0 + 4 * e4 < e;
+      const float* src = ok ? wrt + (int64_t)(kc + k) * e + e0 + 4 * e4 : wrt;
+      cp_async16(ws + (k * RL_EXP + 4 * e4) * 4, src, ok);
+    }
+    cp_async_commit();
+  };
+
+  float tot[4][8], acc[4][8];
 #pragma unroll
-      for (int j = 0; j < TN; ++j) tot[i][j] = (s == s_begin) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tot[i][j] = acc[i][j] = 0.0f;
+
+  load_chunk(0, 0);
+  for (int c = 0; c < nchunks; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nchunks) {
+      load_chunk(c + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t xs = xs0 + buf * RL_TOK * RL_XP * 4, ws = ws0 + buf * RL_KC * RL_EXP * 4;
+#pragma unroll 2
+    for (int k4 = 0; k4 < RL_KC / 4; ++k4) {
+      float4 xv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xv[i] = lds128f(xs + ((4 * ty + i) * RL_XP + 4 * k4) * 4);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t wrow = ws + ((4 * k4 + kk) * RL_EXP) * 4;
+        const float4 wa = lds128f(wrow + (4 * tx) * 4), wb = lds128f(wrow + (32 + 4 * tx) * 4);
+        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float xi = kk == 0 ? xv[i].x : kk == 1 ? xv[i].y : kk == 2 ? xv[i].z : xv[i].w;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xi, wv[j], acc[i][j]);
+        }
+      }
+    }
+    __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
+    if (((c + 1) % (kRouterSeg / RL_KC)) == 0) {  // end of a segment: fold its partial in order
+      const bool first = (c + 1) == (kRouterSeg / RL_KC);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          tot[i][j] = first ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
+          acc[i][j] = 0.0f;
+        }
+    }
   }
-  float* dst = part + (int64_t)blockIdx.z * n * e;
 #pragma unroll
-  for (int i = 0; i < TM; ++i) {
-    const int64_t tok = t0 + TM * ty + i;
+  for (int i = 0; i < 4; ++i) {
+    const int64_t tok = t0 + 4 * ty + i;
     if (tok >= n) continue;
 #pragma unroll
-    for (int j = 0; j < TN; ++j) {
-      const int ee = e0 + TN * tx + j;
-      if (ee < e) dst[tok * e + ee] = tot[i][j];
+    for (int j = 0; j < 8; ++j) {
+      const int ee = e0 + (j < 4 ? 4 * tx + j : 32 + 4 * tx + (j - 4));
+      if (ee >= e) continue;
+      if constexpr (SPLIT) {
+        part[(int64_t)s_begin * n * e + tok * e + ee] = tot[i][j];
+      } else {
+        const float pv = sigmoid_canonical(tot[i][j]);
+        probs[tok * e + ee] = pv;
+        sel[tok * e + ee] = bias ? __fadd_rn(pv, bias[ee]) : pv;
+      }
     }
   }
 }
 
-// ------------------------------------------------------------------------------------------
-// Routing: one CTA per block of `rblk` tokens (32 tokens when block routing is off).
-// ------------------------------------------------------------------------------------------
+// Small-N finish: one thread per (token, expert) logit; all segment partials are loaded before
+// the left-to-right sum.
+__global__ void __launch_bounds__(256) router_finish_kernel(const float* __restrict__ part,
+                                                            const float* __restrict__ bias, float* __restrict__ probs,
+                                                            float* __restrict__ sel, int64_t n, int e, int nseg) {
+  const int64_t off = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (off >= n * e) return;
+  const int64_t ps = n * e;
+  float pp[16];
+  float l = __ldcs(part + off);
+  for (int s0 = 1; s0 < nseg; s0 += 16) {
+#pragma unroll
+    for (int u = 0; u < 16; ++u) pp[u] = (s0 + u < nseg) ? __ldcs(part + (int64_t)(s0 + u) * ps + off) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      if (s0 + u < nseg) l = __fadd_rn(l, pp[u]);
+  }
+  const float pv = sigmoid_canonical(l);
+  probs[off] = pv;
+  sel[off] = bias ? __fadd_rn(pv, bias[off % e]) : pv;
+}
 
+// ------------------------------------------------------------------------------------------
+// Routing: one CTA of 1024 threads per block of `blk` tokens (32 tokens when block routing is
+// off), from the probs / selection scores of the logits kernel.
+// ------------------------------------------------------------------------------------------
 __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
 }
 
-__global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
+constexpr int RT_THREADS = 1024;
+
+__global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
   extern __shared__ float rsm[];
   const int tpb = a.use_block ? a.blk : 32;  // tokens per CTA
-  float* ps = rsm;                           // [tpb][e] probs
-  float* ss = rsm + tpb * a.e;               // [tpb][e] selection scores
-  float* bmax = ss + tpb * a.e;              // [e]
+  float* ss = rsm;                           // [tpb][e] selection scores (masked in place)
+  float* bmax = ss + tpb * a.e;              // [e] block max of the selection scores
+  float* addv = bmax + a.e;                  // [e] 0 or -1e30
+  int* gt_s = reinterpret_cast<int*>(addv + a.e);  // [e]
+  int* eq_s = gt_s + a.e;                          // [e]
   __shared__ float thr_s;
   const int tid = threadIdx.x;
   const int64_t t0 = (int64_t)blockIdx.x * tpb;
   const int ntok = (int)min((int64_t)tpb, a.n - t0);
-  // logits -> probs, selection scores
-  for (int idx = tid; idx < ntok * a.e; idx += blockDim.x) {
-    const int t = idx / a.e, ee = idx % a.e;
-    const int64_t off = (t0 + t) * a.e + ee;
-    // partials P_0 .. P_{nparts-1}: loads issued together, summed left to right
-    const int64_t pstride = a.n * a.e;
-    float l = a.part[off];
-    for (int q0 = 1; q0 < a.nparts; q0 += 8) {
-      float pv[8];
+  const int cnt = ntok * a.e;
+  // stage the block's selection scores (coalesced, 4 loads in flight per thread)
+  const float* sg = a.sel + t0 * a.e;
+  for (int base = 0; base < cnt; base += 4 * RT_THREADS) {
+    float v[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) pv[u] = (q0 + u < a.nparts) ? a.part[(int64_t)(q0 + u) * pstride + off] : 0.0f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (q0 + u < a.nparts) l = __fadd_rn(l, pv[u]);
+    for (int u = 0; u < 4; ++u) {
+      const int idx = base + u * RT_THREADS + tid;
+      v[u] = idx < cnt ? sg[idx] : 0.0f;
     }
-    const float pv = sigmoid_canonical(l);
-    ps[t * a.e + ee] = pv;
-    ss[t * a.e + ee] = a.bias ? __fadd_rn(pv, a.bias[ee]) : pv;
-    if (a.probs) a.probs[off] = pv;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = base + u * RT_THREADS + tid;
+      if (idx < cnt) ss[idx] = v[u];
+    }
+  }
+  for (int ee = tid; ee < a.e; ee += RT_THREADS) {
+    gt_s[ee] = 0;
+    eq_s[ee] = 0;
   }
   __syncthreads();
   if (a.use_block) {
-    for (int ee = tid; ee < a.e; ee += blockDim.x) {
+    // block max by the fold m = s_t + relu(m - s_t), t = 1 .. blk-1 in order (:223-229)
+    for (int ee = tid; ee < a.e; ee += RT_THREADS) {
       float m = ss[ee];
       for (int t = 1; t < tpb; ++t) {
         const float st = ss[t * a.e + ee];
@@ -202,31 +262,44 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
       bmax[ee] = m;
     }
     __syncthreads();
-    for (int ee = tid; ee < a.e; ee += blockDim.x) {
+    // thr = value at position cap-1 of bmax sorted descending (:231-236): rank counts split
+    // over `nsp` threads per expert
+    const int nsp = max(1, RT_THREADS / a.e);
+    const int chunk = (a.e + nsp - 1) / nsp;
+    if (tid < nsp * a.e) {
+      const int ee = tid % a.e, q = tid / a.e;
       const float v = bmax[ee];
       int gt = 0, eq = 0;
-      for (int j = 0; j < a.e; ++j) {
+      const int j1 = min(a.e, (q + 1) * chunk);
+      for (int j = q * chunk; j < j1; ++j) {
         const float u = bmax[j];
         gt += u > v;
         eq += u == v;
       }
-      if (gt <= a.cap - 1 && a.cap - 1 < gt + eq) thr_s = v;  // all writers store the same value
+      atomicAdd(&gt_s[ee], gt);
+      atomicAdd(&eq_s[ee], eq);
     }
     __syncthreads();
+    for (int ee = tid; ee < a.e; ee += RT_THREADS) {
+      const int gt = gt_s[ee], eq = eq_s[ee];
+      if (gt <= a.cap - 1 && a.cap - 1 < gt + eq) thr_s = bmax[ee];  // all writers store the same value
+    }
+    __syncthreads();
+    // keep = step(bmax - (thr - 1e-6)); masked scores += -1e30 (:238-248)
     const float thr_m = __fadd_rn(__fmul_rn(thr_s, 1.0f), -1e-6f);
-    for (int ee = tid; ee < a.e; ee += blockDim.x) {
+    for (int ee = tid; ee < a.e; ee += RT_THREADS) {
       const float dlt = __fsub_rn(bmax[ee], thr_m);
       const bool keep = dlt > 0.0f;
       if (a.allowed) a.allowed[(int64_t)blockIdx.x * a.e + ee] = keep ? 1 : 0;
-      const float add = keep ? 0.0f : -1e30f;
-      for (int t = 0; t < tpb; ++t) ss[t * a.e + ee] = __fadd_rn(ss[t * a.e + ee], add);
+      addv[ee] = keep ? 0.0f : -1e30f;
     }
     __syncthreads();
+    for (int idx = tid; idx < cnt; idx += RT_THREADS) ss[idx] = __fadd_rn(ss[idx], addv[idx % a.e]);
+    __syncthreads();
   }
-  // per-token top-k: one warp per token
+  // per-token top-k (:252): one warp per token, ties to the lower expert id
   const int warp = tid >> 5, lane = tid & 31;
-  const int nwarps = blockDim.x >> 5;
-  for (int t = warp; t < ntok; t += nwarps) {
+  for (int t = warp; t < ntok; t += RT_THREADS / 32) {
     const float* st = ss + t * a.e;
     uint32_t taken = 0;  // bit j: candidate lane + 32 j already selected (e <= 1024)
     int sel_idx[16];
@@ -254,12 +327,13 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
       if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
       sel_idx[s] = bi;
     }
+    // gates from the unbiased probs, renormalised (sum in double) and scaled (:253-262)
     if (lane == 0) {
       const int64_t tok = t0 + t;
       float wv[16];
       double sum = 0.0;
       for (int s = 0; s < a.top_k; ++s) {
-        wv[s] = ps[t * a.e + sel_idx[s]];
+        wv[s] = a.probs[tok * a.e + sel_idx[s]];
         sum = __dadd_rn(sum, (double)wv[s]);
       }
       const float fs = __double2float_rn(sum);
@@ -275,29 +349,33 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a) {
   }
 }
 
-// nparts must be 1 (running sum) or the number of segments (one partial per segment).
-cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, int nparts,
-                          cudaStream_t st) {
-  const int nseg = (h + kRouterSeg - 1) / kRouterSeg;
-  if (nparts != 1 && nparts != nseg) return cudaErrorInvalidValue;
-  dim3 grid((unsigned)((n + RL_TOK - 1) / RL_TOK), (unsigned)((e + RL_EXP - 1) / RL_EXP), (unsigned)nparts);
-  if (nparts == 1)
-    router_logits_kernel<8, 8, 32><<<grid, 32, 0, st>>>(x, wrt, part, n, h, e, nseg);
-  else
-    router_logits_kernel<4, 4, 128><<<grid, 128, 0, st>>>(x, wrt, part, n, h, e, 1);
+// Fills probs and sel [n][e]. split = true: one CTA per (tile, segment) with partials in `part`
+// [h / 256][n][e], then the elementwise finish.
+cudaError_t launch_router(const float* x, const float* wrt, const float* bias, float* part, float* probs, float* sel,
+                          int64_t n, int h, int e, bool split, cudaStream_t st) {
+  if (h % kRouterSeg) return cudaErrorInvalidValue;
+  const int nseg = h / kRouterSeg;
+  dim3 grid((unsigned)((n + RL_TOK - 1) / RL_TOK), (unsigned)((e + RL_EXP - 1) / RL_EXP), split ? (unsigned)nseg : 1u);
+  if (split) {
+    cudaFuncSetAttribute(router_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, RL_SMEM);
+    router_logits_kernel<true><<<grid, RL_THREADS, RL_SMEM, st>>>(x, wrt, bias, part, probs, sel, n, h, e);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    const int64_t cnt = n * e;
+    router_finish_kernel<<<(unsigned)((cnt + 255) / 256), 256, 0, st>>>(part, bias, probs, sel, n, e, nseg);
+  } else {
+    cudaFuncSetAttribute(router_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, RL_SMEM);
+    router_logits_kernel<false><<<grid, RL_THREADS, RL_SMEM, st>>>(x, wrt, bias, part, probs, sel, n, h, e);
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
   const int tpb = a.use_block ? a.blk : 32;
   const int64_t nblocks = (a.n + tpb - 1) / tpb;
-  const size_t smem = sizeof(float) * ((size_t)2 * tpb * a.e + a.e);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
-  route_kernel<<<(unsigned)nblocks, 256, smem, st>>>(a);
+  const size_t smem = sizeof(float) * ((size_t)tpb * a.e + 4 * (size_t)a.e);
+  cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  route_kernel<<<(unsigned)nblocks, RT_THREADS, smem, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,171 @@
+"""CPU model of the grouped-GEMM kernel's mbarrier protocol (moe_gemm.cu, moe_gemm_kernel).
+
+Every role is a step machine that waits for an absolute completion count of a barrier and
+arrives on others, exactly as the kernel's producer, MMA issuer, epilogue and dequant warps do.
+The hardware only compares parities, which is correct only while the barrier's phase is the
+needed completion or the one before it; the model flags any wait evaluated outside that window
+(aliasing) and any state where no role can move (deadlock), over randomised interleavings.
+It covers every configuration the launcher can instantiate (the TMEM/smem budget formulas of
+GemmCfg are restated below) and checks that an unsafe ring (fewer A buffers than dequant
+warpgroups) is caught.
+"""
+import itertools
+import random
+
+import pytest
+
+F16, Q8_0, Q4_K = 1, 8, 12
+GATEUP, DOWN = 0, 1
+
+
+def gemm_cfg(wt, mode, nt, ndq):
+    """Restates GemmCfg<WT, MODE, NT, NDQ> (stage ring, TMEM ring) from moe_gemm.cu."""
+    quant = wt != F16
+    mats = 2 if mode == GATEUP else 1
+    stage_k = 256 if wt == Q4_K else 128
+    kb = stage_k // 128
+    b_bytes = stage_k * nt * 2
+    w_bytes = 128 * 144 if wt == Q4_K else (128 * 128 + 128 * 16 if wt == Q8_0 else 128 * 128 * 2)
+    stage_bytes = b_bytes + mats * w_bytes
+    epi_bytes = ((4 * 16 * 33 * 4 + 1023) // 1024) * 1024
+    stages = min(6, (227 * 1024 - 2048 - epi_bytes) // stage_bytes)
+    acc_cols = mats * nt
+    a_cols = mats * 64
+    acc_bufs = 2 if 2 * acc_cols + (2 * a_cols if quant else 0) <= 512 else 1
+    na = min(4, (512 - acc_bufs * acc_cols) // a_cols) if quant else 0
+    ndq = ndq if quant else 0
+    return dict(stages=stages, na=na, ndq=ndq, kb=kb, acc_bufs=acc_bufs, quant=quant,
+                ring_ok=(not quant) or na >= ndq)
+
+
+class Bar:
+    def __init__(self, name, count):
+        self.name, self.count, self.pending, self.phase = name, count, count, 0
+
+    def arrive(self):
+        self.pending -= 1
+        assert self.pending >= 0, f"{self.name}: more arrivals than the count"
+        if self.pending == 0:
+            self.phase += 1
+            self.pending = self.count
+
+
+def roles(cfg, tiles):
+    S, NA, NDQ, KB, ACCB = cfg["stages"], max(cfg["na"], 1), cfg["ndq"], cfg["kb"], cfg["acc_bufs"]
+    quant = cfg["quant"]
+    full = [Bar(f"full{i}", 1) for i in range(S)]
+    empty = [Bar(f"empty{i}", 1 + 4 * NDQ) for i in range(S)]
+    afull = [Bar(f"afull{i}", 4) for i in range(NA)]
+    aempty = [Bar(f"aempty{i}", 1) for i in range(NA)]
+    accfull = [Bar(f"accfull{i}", 1) for i in range(ACCB)]
+    accempty = [Bar(f"accempty{i}", 4) for i in range(ACCB)]
+
+    def producer():
+        seq = 0
+        for t in tiles:
+            for _ in range(t):
+                s = seq % S
+                yield empty[s], seq // S
+                full[s].arrive()  # the stage's TMA transactions complete
+                seq += 1
+
+    def mma():
+        seq = tseq = 0
+        for t in tiles:
+            ab = tseq % ACCB
+            yield accempty[ab], tseq // ACCB
+            for _ in range(t):
+                s = seq % S
+                yield full[s], seq // S + 1
+                for kb in range(KB):
+                    if quant:
+                        kbs = seq * KB + kb
+                        a, u = kbs % NA, kbs // NA
+                        yield afull[a], u + 1
+                        aempty[a].arrive()  # tcgen05.commit after the k-block's MMAs
+                empty[s].arrive()
+                seq += 1
+            accfull[ab].arrive()
+            tseq += 1
+
+    def epilogue():
+        tseq = 0
+        for t in tiles:
+            ab = tseq % ACCB
+            yield accfull[ab], tseq // ACCB + 1
+            accempty[ab].arrive()
+            tseq += 1
+
+    def dequant(g):
+        seq = 0
+        for t in tiles:
+            for _ in range(t):
+                s = seq % S
+                yield full[s], seq // S + 1
+                for kb in range(KB):
+                    kbs = seq * KB + kb
+                    if kbs % NDQ != g:
+                        continue
+                    a, u = kbs % NA, kbs // NA
+                    yield aempty[a], u
+                    afull[a].arrive()
+                empty[s].arrive()
+                seq += 1
+
+    rs = [producer(), mma()] + [epilogue() for _ in range(4)]
+    rs += [dequant(g) for g in range(NDQ) for _ in range(4)]
+    return rs
+
+
+def run(cfg, tiles, seed):
+    rng = random.Random(seed)
+    rs = roles(cfg, tiles)
+    cur = [None] * len(rs)
+    alive = set(range(len(rs)))
+    while alive:
+        changed = True
+        while changed:  # advance every role to its next wait (arrivals happen on the way)
+            changed = False
+            for i in list(alive):
+                if cur[i] is None:
+                    try:
+                        cur[i] = next(rs[i])
+                    except StopIteration:
+                        alive.discard(i)
+                    changed = True
+        if not alive:
+            return None
+        ready = []
+        for i in alive:
+            bar, k = cur[i]
+            if bar.phase < k - 1 or bar.phase > k:
+                return f"parity alias on {bar.name}: needs completion {k}, at phase {bar.phase}"
+            if bar.phase >= k:
+                ready.append(i)
+        if not ready:
+            return "deadlock"
+        cur[rng.choice(ready)] = None
+    return None
+
+
+LAUNCHABLE = []
+for wt, mode, nt, ndq in itertools.product([F16, Q8_0, Q4_K], [GATEUP, DOWN], [32, 64, 128], [2, 3, 4]):
+    c = gemm_cfg(wt, mode, nt, ndq)
+    if c["ring_ok"] and (wt != F16 or ndq == 2):
+        LAUNCHABLE.append((wt, mode, nt, ndq))
+
+
+@pytest.mark.parametrize("wt,mode,nt,ndq", LAUNCHABLE)
+def test_launchable_configs_are_safe(wt, mode, nt, ndq):
+    cfg = gemm_cfg(wt, mode, nt, ndq)
+    assert cfg["stages"] >= 2 and (not cfg["quant"] or cfg["na"] >= 2)
+    for tiles in ([16, 16, 16], [3, 1, 2], [1, 1, 1, 1, 1]):
+        for seed in range(12):
+            assert run(cfg, tiles, seed) is None, (cfg, tiles, seed)
+
+
+def test_model_catches_a_short_ring():
+    # fewer A buffers than dequant warpgroups: a group can wait two completions ahead
+    cfg = dict(stages=4, na=3, ndq=4, kb=2, acc_bufs=2, quant=True, ring_ok=False)
+    results = [run(cfg, [16, 16, 16], seed) for seed in range(25)]
+    assert any(r and "alias" in r for r in results)
