@@ -351,7 +351,16 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
           const uint32_t ph = (stage_seq / C::STAGES) & 1u;
           if (!role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t bbase = smem_u32(stage_ptr(s));
+          // Shared-memory descriptors are built once per stage; each (k-block, k-step) slice adds
+          // a compile-time offset to the 14-bit start-address field (no carry: smem < 256 KB), so
+          // the issuing thread spends one add per MMA between the blocking tcgen05.mma issues.
+          const uint64_t bdesc0 = sdesc_sw128(smem_u32(stage_ptr(s)), 1024);
+          const uint32_t acc_first = first ? 0u : 1u;
+          uint64_t adesc0[C::MATS];
+          if constexpr (!C::QUANT) {
+#pragma unroll
+            for (int m = 0; m < C::MATS; ++m) adesc0[m] = sdesc_sw128(smem_u32(wtile_ptr(s, m)), 1024);
+          }
 #pragma unroll
           for (int kb = 0; kb < C::KB_PER_STAGE; ++kb) {
             uint32_t abuf = 0;
@@ -366,22 +375,22 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const uint64_t bdesc = sdesc_sw128(bbase + (kb * 2 + j / 4) * (NT * 128) + (j % 4) * 32, 1024);
+              const uint64_t bdesc = bdesc0 + (uint64_t)(((kb * 2 + j / 4) * (NT * 128) + (j % 4) * 32) >> 4);
+              const uint32_t acc = (kb == 0 && j == 0) ? acc_first : 1u;
 #pragma unroll
               for (int m = 0; m < C::MATS; ++m) {
                 const uint32_t dcol = dbase + m * NT;
                 if constexpr (C::QUANT) {
-                  mma_f16_ts(dcol, abuf + m * 64 + 8 * j, bdesc, idesc, first ? 0u : 1u);
+                  mma_f16_ts(dcol, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
                 } else {
-                  const uint32_t wb = smem_u32(wtile_ptr(s, m));
-                  const uint64_t adesc = sdesc_sw128(wb + (j / 4) * (128 * 128) + (j % 4) * 32, 1024);
-                  mma_f16_ss(dcol, adesc, bdesc, idesc, first ? 0u : 1u);
+                  const uint64_t adesc = adesc0[m] + (uint64_t)(((j / 4) * (128 * 128) + (j % 4) * 32) >> 4);
+                  mma_f16_ss(dcol, adesc, bdesc, idesc, acc);
                 }
               }
-              first = false;
             }
             if constexpr (C::QUANT) mma_commit(&aempty[a]);
           }
+          first = false;
           mma_commit(&empty[s]);
           ++stage_seq;
         }
