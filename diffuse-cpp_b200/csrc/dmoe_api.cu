@@ -159,6 +159,8 @@ dmoe_status grow(T*& p, size_t& cap, size_t need) {
 
 }  // namespace
 
+void dmoe::set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 struct dmoe_layer {
   // shapes / hyper-parameters
   int64_t H = 0, I = 0, Is = 0, E = 0, K = 0, cap = 0, blk = 0;

@@ -88,6 +88,9 @@ cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows,
 cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st);
 int gemm_stage_k(int wtype);
 
+// records the message returned by dmoe_last_error on this thread (dmoe_api.cu)
+void set_last_error(const char* msg);
+
 // host-side codecs (quant.cpp)
 uint16_t f32_to_f16_bits(float f);
 float f16_bits_to_f32(uint16_t h);

@@ -138,6 +138,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.dmoe_quantize.restype = ctypes.c_size_t
     lib.dmoe_quantized_size.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int64]
     lib.dmoe_quantized_size.restype = ctypes.c_size_t
+    lib.dmoe_route_static.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, P, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_int32, P, P, P]
+    lib.dmoe_route_static.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -274,3 +277,18 @@ class MoELayer:
             self.close()
         except Exception:
             pass
+
+
+def route_static(x, w_router, b_router, hp: dict, idx, weights, stream: Optional[int] = None) -> None:
+    """dmoe_route_static: routing with the library's fixed scratch array, for callers that cannot
+    allocate device memory. Every argument is a torch CUDA tensor (device memory) owned by the
+    caller: x [n, H] f32, w_router [E, H] f32, b_router [E] f32 or None, and the outputs
+    idx [n, top_k] int32 and weights [n, top_k] f32. Enqueued on the current torch stream."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+    _check(load().dmoe_route_static(_ptr(x), int(x.shape[0]), hp["n_embd"], _ptr(w_router), _ptr(b_router),
+                                    hp["n_expert"], hp["n_expert_used"], hp.get("expert_capacity", 48),
+                                    hp.get("moe_block_size", 32), hp.get("routed_scaling", 1.0),
+                                    hp.get("norm_topk_prob", 1), _ptr(idx), _ptr(weights), stream if stream else None))

@@ -157,6 +157,33 @@ size_t dmoe_quantize(int32_t type, const float* src, void* dst, int64_t nrows, i
 /* Bytes of nrows rows of n_per_row values. Replaces tools/quant_lib.c:30-33. */
 size_t dmoe_quantized_size(int32_t type, int64_t nrows, int64_t n_per_row);
 
+/* Routing without any device allocation. No counterpart in the reference: it exists for callers
+ * that cannot call cudaMalloc, such as a process whose device memory is owned by another
+ * allocator (a serving stack that reserves its whole budget at start-up, or a host framework
+ * that hands out every buffer itself). It computes exactly what dmoe_forward with
+ * DMOE_F_ROUTE_ONLY computes (same kernels, same canonical bits), but takes every tensor as a
+ * DEVICE pointer from the caller and needs no dmoe_create:
+ *   x         [n_tokens][n_embd] f32          w_router [n_expert][n_embd] f32 (GGUF layout)
+ *   b_router  [n_expert] f32 or NULL          idx / weights [n_tokens][n_expert_used] (outputs)
+ * The work is enqueued on `stream` (NULL = the CUDA default stream) of the current device.
+ * Its scratch is one fixed array of DMOE_STATIC_SCRATCH_BYTES inside the library, held by every
+ * GPU that loads the library until the process exits. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture. All calls share the array: calls that overlap on the GPU (other
+ * streams or threads) race on it. Sizes above n_tokens <= DMOE_STATIC_MAX_TOKENS,
+ * n_expert <= DMOE_STATIC_MAX_EXPERTS, n_embd <= DMOE_STATIC_MAX_EMBD are rejected with
+ * DMOE_ERR_UNSUPPORTED; n_embd must be a multiple of 256, n_expert of 4. */
+#define DMOE_STATIC_MAX_TOKENS 4096
+#define DMOE_STATIC_MAX_EXPERTS 256
+#define DMOE_STATIC_MAX_EMBD 8192
+#define DMOE_STATIC_SCRATCH_BYTES                                                                  \
+  (4ull * (2ull * DMOE_STATIC_MAX_TOKENS * DMOE_STATIC_MAX_EXPERTS +                                \
+           (unsigned long long)DMOE_STATIC_MAX_EMBD * DMOE_STATIC_MAX_EXPERTS + DMOE_STATIC_MAX_EXPERTS))
+dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64_t n_embd, const float* w_router,
+                              const float* b_router, int64_t n_expert, int64_t n_expert_used,
+                              int64_t expert_capacity, int64_t moe_block_size, float routed_scaling,
+                              int32_t norm_topk_prob, int32_t* idx, float* weights, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
