@@ -1,0 +1,59 @@
+"""The C ABI library (no GPU needed): it loads, exports every entry point include/*.h declares,
+and rejects bad arguments with status codes (never an exit, never a CPU fallback)."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+import diffuse_moe as dm
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"\b(dmoe_[a-z_0-9]+)\s*\(", src):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_every_declared_symbol_is_exported():
+    lib = dm.load()
+    names = declared_functions()
+    assert "dmoe_forward" in names and "dmoe_create" in names
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_abi_version():
+    assert dm.load().dmoe_abi_version() == 1
+
+
+def test_argument_errors_are_status_codes():
+    lib = dm.load()
+    h = ctypes.c_void_p()
+    assert lib.dmoe_create(None, None, ctypes.byref(h)) == 1  # DMOE_ERR_INVALID_ARG
+    assert "null layer descriptor" in dm.last_error()
+    d = dm.LayerDesc()
+    d.n_embd, d.n_ff_exp, d.n_expert, d.n_expert_used = 256, 256, 16, 32  # top-k > 16
+    assert lib.dmoe_create(ctypes.byref(d), None, ctypes.byref(h)) == 1
+    assert lib.dmoe_forward(None, None, 0, None, None, None, 0) == 1
+    assert lib.dmoe_sync(None) == 1
+
+
+def test_no_device_is_reported_not_worked_around():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    import numpy as np
+    import synth
+
+    spec = synth.config("tiny")
+    with pytest.raises(dm.DmoeError) as ei:
+        dm.MoELayer(spec.hparams(), synth.make_layer(spec))
+    assert ei.value.status == 3  # DMOE_ERR_NO_DEVICE
