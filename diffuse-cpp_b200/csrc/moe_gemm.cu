@@ -148,6 +148,17 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// Warp-uniform forms for roles whose whole warp walks the schedule: every lane waits, and
+// lane 0's verdict is the warp's, so the warp stays converged around its tcgen05 issue blocks.
+__device__ __forceinline__ bool warp_role_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t errbit,
+                                               volatile int* abort_flag) {
+  const bool ok = role_wait(bar, parity, err, errbit, abort_flag);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+__device__ __forceinline__ bool warp_abort(volatile int* abort_flag) {
+  return __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
+}
+
 // ------------------------------------------------------------------------------------------
 // dequantisation of one 128-K block of one weight row into 64 TMEM columns (fp16 pairs)
 // ------------------------------------------------------------------------------------------
@@ -301,16 +312,18 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
-      uint32_t stage_seq = 0;
-      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-        const TileInfo ti = decode_tile<NT>(p, t);
-        const int wrow = ti.expert * p.grp[ti.group].rows_per_exp + ti.mt * kMTile;
-        for (int kc = ti.k0; kc < ti.k1; ++kc) {
-          const int s = stage_seq % C::STAGES;
-          const uint32_t ph = (stage_seq / C::STAGES) & 1u;
-          if (!role_wait(&empty[s], ph ^ 1u, p.err, ERRBIT_TIMEOUT_EMPTY, abort_flag)) break;
+    // (whole warp walks the schedule; one elected lane issues each stage's copies)
+    const uint64_t pol_w = l2_policy_evict_first();
+    uint32_t stage_seq = 0;
+    for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
+      const TileInfo ti = decode_tile<NT>(p, t);
+      const int wrow = ti.expert * p.grp[ti.group].rows_per_exp + ti.mt * kMTile;
+      bool ok = true;
+      for (int kc = ti.k0; kc < ti.k1; ++kc) {
+        const int s = stage_seq % C::STAGES;
+        const uint32_t ph = (stage_seq / C::STAGES) & 1u;
+        if (!warp_role_wait(&empty[s], ph ^ 1u, p.err, ERRBIT_TIMEOUT_EMPTY, abort_flag)) { ok = false; break; }
+        if (elect_one()) {
           mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
 #pragma unroll
           for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
@@ -328,76 +341,87 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
               tma_load_2d_hint(wt + 128 * 128, &p.tm_w[ti.group][m], kc * 128 + 64, wrow, &full[s], pol_w);
             }
           }
-          ++stage_seq;
         }
+        __syncwarp();
+        ++stage_seq;
       }
+      if (!ok) break;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(128, NT);
-      uint32_t stage_seq = 0, tile_seq = 0;
-      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-        const TileInfo ti = decode_tile<NT>(p, t);
-        const int ab = tile_seq % C::ACC_BUFS;
-        const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
-        if (!role_wait(&accempty[ab], aph ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) break;
+    // The whole warp walks the schedule, waits included, and one elected lane issues each
+    // k-block's MMAs as one straight-line block. Issued this way a kind::f16 M=128 MMA costs
+    // 24 / 32 / 64 cycles at N = 32 / 64 / 128; issued from a lane-0-only branch it costs
+    // 46 cycles or more even at N <= 64, and a run-time branch between two MMAs about 100.
+    constexpr uint32_t idesc = idesc_f16_f32(128, NT);
+    uint32_t stage_seq = 0, tile_seq = 0;
+    for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
+      const TileInfo ti = decode_tile<NT>(p, t);
+      const int ab = tile_seq % C::ACC_BUFS;
+      const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
+      if (!warp_role_wait(&accempty[ab], aph ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t dbase = tbase + ab * C::ACC_COLS;
+      bool first = true;
+      bool ok = true;
+      for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
+        const int s = stage_seq % C::STAGES;
+        const uint32_t ph = (stage_seq / C::STAGES) & 1u;
+        if (!warp_role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t dbase = tbase + ab * C::ACC_COLS;
-        bool first = true;
-        bool ok = true;
-        for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
-          const int s = stage_seq % C::STAGES;
-          const uint32_t ph = (stage_seq / C::STAGES) & 1u;
-          if (!role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          // Shared-memory descriptors are built once per stage; each (k-block, k-step) slice adds
-          // a compile-time offset to the 14-bit start-address field (no carry: smem < 256 KB), so
-          // the issuing thread spends one add per MMA between the blocking tcgen05.mma issues.
-          const uint64_t bdesc0 = sdesc_sw128(smem_u32(stage_ptr(s)), 1024);
-          const uint32_t acc_first = first ? 0u : 1u;
-          uint64_t adesc0[C::MATS];
-          if constexpr (!C::QUANT) {
-#pragma unroll
-            for (int m = 0; m < C::MATS; ++m) adesc0[m] = sdesc_sw128(smem_u32(wtile_ptr(s, m)), 1024);
-          }
+        // Shared-memory descriptors are built once per stage; each (k-block, k-step) slice adds
+        // a compile-time offset to the 14-bit start-address field (no carry: smem < 256 KB).
+        const uint64_t bdesc0 = sdesc_sw128(smem_u32(stage_ptr(s)), 1024);
+        const uint32_t acc_first = first ? 0u : 1u;
+        if constexpr (C::QUANT) {
 #pragma unroll
           for (int kb = 0; kb < C::KB_PER_STAGE; ++kb) {
-            uint32_t abuf = 0;
-            int a = 0;
-            if constexpr (C::QUANT) {
-              const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
-              a = kbs % C::NA;
-              const uint32_t u = kbs / C::NA;
-              if (!role_wait(&afull[a], u & 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
-              tc_fence_after();
-              abuf = tbase + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
+            const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
+            const int a = kbs % C::NA;
+            const uint32_t u = kbs / C::NA;
+            if (!warp_role_wait(&afull[a], u & 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t abuf = tbase + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
+            if (elect_one()) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint64_t bdesc = bdesc0 + (uint64_t)(((kb * 2 + j / 4) * (NT * 128) + (j % 4) * 32) >> 4);
+                const uint32_t acc = (kb == 0 && j == 0) ? acc_first : 1u;
+#pragma unroll
+                for (int m = 0; m < C::MATS; ++m) mma_f16_ts(dbase + m * NT, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
+              }
+              mma_commit(&aempty[a]);
             }
+            __syncwarp();
+          }
+          if (!ok) break;
+        } else {
+          uint64_t adesc0[C::MATS];
+#pragma unroll
+          for (int m = 0; m < C::MATS; ++m) adesc0[m] = sdesc_sw128(smem_u32(wtile_ptr(s, m)), 1024);
+          if (elect_one()) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const uint64_t bdesc = bdesc0 + (uint64_t)(((kb * 2 + j / 4) * (NT * 128) + (j % 4) * 32) >> 4);
-              const uint32_t acc = (kb == 0 && j == 0) ? acc_first : 1u;
+              const uint64_t bdesc = bdesc0 + (uint64_t)(((j / 4) * (NT * 128) + (j % 4) * 32) >> 4);
+              const uint32_t acc = j == 0 ? acc_first : 1u;
 #pragma unroll
               for (int m = 0; m < C::MATS; ++m) {
-                const uint32_t dcol = dbase + m * NT;
-                if constexpr (C::QUANT) {
-                  mma_f16_ts(dcol, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
-                } else {
-                  const uint64_t adesc = adesc0[m] + (uint64_t)(((j / 4) * (128 * 128) + (j % 4) * 32) >> 4);
-                  mma_f16_ss(dcol, adesc, bdesc, idesc, acc);
-                }
+                const uint64_t adesc = adesc0[m] + (uint64_t)(((j / 4) * (128 * 128) + (j % 4) * 32) >> 4);
+                mma_f16_ss(dbase + m * NT, adesc, bdesc, idesc, acc);
               }
             }
-            if constexpr (C::QUANT) mma_commit(&aempty[a]);
           }
-          first = false;
-          mma_commit(&empty[s]);
-          ++stage_seq;
+          __syncwarp();
         }
-        if (!ok) break;
-        mma_commit(&accfull[ab]);
-        ++tile_seq;
+        first = false;
+        if (elect_one()) mma_commit(&empty[s]);
+        __syncwarp();
+        ++stage_seq;
       }
+      if (!ok) break;
+      if (elect_one()) mma_commit(&accfull[ab]);
+      __syncwarp();
+      ++tile_seq;
     }
   } else if (warp < C::DQ_WARP0) {
     // ------------------------------------------------------------------ epilogue
