@@ -10,6 +10,8 @@
 // scan_tiles_kernel  exclusive scan of the per-expert counts + the token-tile list
 // gather_kernel      x (fp32) -> fp16 rows of the gathered buffer, pair -> token / weight maps
 // swiglu_finish      split-K path: h = silu(g) * u from the fp32 partial sums
+// combine_kernel     out[t] = ((y_0 + y_1) + ... + y_{k-1}) + shared[t], the slot sum and the
+//                    shared-expert add of src/diffuse-moe-graph.cpp:273-286 in that order
 #include "dmoe_internal.h"
 
 namespace dmoe {
@@ -71,8 +73,8 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ x
                                                      const int32_t* __restrict__ idx, const float* __restrict__ w,
                                                      const int32_t* __restrict__ off, int32_t* __restrict__ fill,
                                                      __half* __restrict__ xg, int32_t* __restrict__ pair_tok,
-                                                     float* __restrict__ pair_w, int swap_shared, int swap_routed,
-                                                     int with_shared) {
+                                                     float* __restrict__ pair_w, int32_t* __restrict__ pair_row,
+                                                     int swap_shared, int swap_routed, int with_shared) {
   __shared__ int64_t rows[17];
   const int64_t t = blockIdx.x;
   const int tid = threadIdx.x;
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ x
       const int64_t pos = off[ee] + atomicAdd(&fill[ee], 1);
       pair_tok[pos] = (int32_t)t;
       pair_w[pos] = w[t * top_k + s];
+      pair_row[t * top_k + s] = (int32_t)pos;
       rows[nrows++] = pos;
     }
   }
@@ -127,6 +130,50 @@ __global__ void swiglu_finish_kernel(const float* __restrict__ gu, int64_t gu_ha
   }
 }
 
+// One CTA per token. y holds the weighted routed rows (row r of the gathered layout at
+// y + (r - n) * y_ld); out holds the shared expert's rows when add_out is set.
+constexpr int kMaxTopK = 16;
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, int64_t y_ld, int64_t n,
+                                                      const int32_t* __restrict__ pair_row, int top_k,
+                                                      float* __restrict__ out, int64_t h, int add_out) {
+  __shared__ int64_t rows[kMaxTopK];
+  const int64_t t = blockIdx.x;
+  if (threadIdx.x < top_k) rows[threadIdx.x] = (int64_t)(pair_row[t * top_k + threadIdx.x] - n) * y_ld;
+  __syncthreads();
+  float4* o = reinterpret_cast<float4*>(out + t * h);
+  for (int64_t q = threadIdx.x; q < h / 4; q += blockDim.x) {
+    float4 v[kMaxTopK];
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s)
+      if (s < top_k) v[s] = __ldcs(reinterpret_cast<const float4*>(y + rows[s]) + q);
+    float4 a = v[0];
+#pragma unroll
+    for (int s = 1; s < kMaxTopK; ++s)
+      if (s < top_k) {
+        a.x = __fadd_rn(a.x, v[s].x);
+        a.y = __fadd_rn(a.y, v[s].y);
+        a.z = __fadd_rn(a.z, v[s].z);
+        a.w = __fadd_rn(a.w, v[s].w);
+      }
+    if (add_out) {
+      const float4 b = o[q];
+      a.x = __fadd_rn(a.x, b.x);
+      a.y = __fadd_rn(a.y, b.y);
+      a.z = __fadd_rn(a.z, b.z);
+      a.w = __fadd_rn(a.w, b.w);
+    }
+    o[q] = a;
+  }
+}
+
+cudaError_t launch_combine(const float* y, int64_t y_ld, int64_t n, const int32_t* pair_row, int top_k, float* out,
+                           int64_t h, int add_out, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  if (top_k < 1 || top_k > kMaxTopK || h % 4) return cudaErrorInvalidValue;
+  combine_kernel<<<(unsigned)n, 256, 0, st>>>(y, y_ld, n, pair_row, top_k, out, h, add_out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, int32_t* off, int32_t* fill,
                               TokTile* tiles, int32_t* n_tiles, int32_t* n_active, cudaStream_t st) {
   scan_tiles_kernel<<<1, 1024, 0, st>>>(counts, e, n, nt, off, fill, tiles, n_tiles, n_active);
@@ -135,10 +182,10 @@ cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, i
 
 cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
                           const int32_t* off, int32_t* fill, __half* xg, int32_t* pair_tok, float* pair_w,
-                          int swap_shared, int swap_routed, int with_shared, cudaStream_t st) {
+                          int32_t* pair_row, int swap_shared, int swap_routed, int with_shared, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  gather_kernel<<<(unsigned)n, 256, 0, st>>>(x, n, h, top_k, idx, w, off, fill, xg, pair_tok, pair_w, swap_shared,
-                                             swap_routed, with_shared);
+  gather_kernel<<<(unsigned)n, 256, 0, st>>>(x, n, h, top_k, idx, w, off, fill, xg, pair_tok, pair_w, pair_row,
+                                             swap_shared, swap_routed, with_shared);
   return cudaGetLastError();
 }
 

@@ -175,9 +175,8 @@ struct dmoe_layer {
   float* br = nullptr;
   DevWeight gate, up, down, sgate, sup, sdown;
   // workspace (grown, never shrunk)
-  float* parts = nullptr; size_t parts_cap = 0;    // router segment partials (split path)
-  float* probs = nullptr; size_t probs_cap = 0;      // sigmoid(router logits)
-  float* sel = nullptr; size_t sel_cap = 0;          // probs + expert bias
+  float* parts = nullptr; size_t parts_cap = 0;    // router logits, or their segment partials (split path)
+  int32_t* arrivals = nullptr; size_t arrivals_cap = 0;  // split router: per-tile arrival counters
   int32_t* idx = nullptr; size_t idx_cap = 0;
   float* wts = nullptr; size_t wts_cap = 0;
   uint8_t* allowed = nullptr; size_t allowed_cap = 0;
@@ -188,6 +187,8 @@ struct dmoe_layer {
   float* gu = nullptr; size_t gu_cap = 0;
   int32_t* pair_tok = nullptr; size_t pair_tok_cap = 0;
   float* pair_w = nullptr; size_t pair_w_cap = 0;
+  int32_t* pair_row = nullptr; size_t pair_row_cap = 0;
+  float* ybuf = nullptr; size_t ybuf_cap = 0;
   float* xdev = nullptr; size_t xdev_cap = 0;
   float* odev = nullptr; size_t odev_cap = 0;
   uint32_t* err = nullptr;
@@ -210,7 +211,7 @@ dmoe_status validate(const dmoe_layer_desc* d) {
   if (d->n_expert > 1024 || d->n_expert % 4) return fail(DMOE_ERR_UNSUPPORTED, "n_expert must be a multiple of 4, <= 1024");
   if (d->expert_capacity < 0 || d->moe_block_size < 0) return fail(DMOE_ERR_INVALID_ARG, "negative capacity/block");
   const int64_t tpb = d->moe_block_size > 1 ? std::max<int64_t>(d->moe_block_size, 32) : 32;
-  if ((2 * tpb * d->n_expert + d->n_expert) * 4 > 200 * 1024)
+  if (route_smem_bytes(tpb, d->n_expert) > kRouteSmemMax)
     return fail(DMOE_ERR_UNSUPPORTED, "moe_block_size x n_expert too large for the routing kernel");
   if (!type_supported(d->expert_type)) return fail(DMOE_ERR_UNSUPPORTED, "expert weight type %d", d->expert_type);
   if (d->n_ff_shexp > 0 && !type_supported(d->shared_type))
@@ -229,8 +230,9 @@ dmoe_status validate(const dmoe_layer_desc* d) {
   return DMOE_OK;
 }
 
-// Tuning overrides (DMOE_NT = 32 / 64 / 128, DMOE_KSPLIT_GU / DMOE_KSPLIT_DN = 1 / 2 / 4 / 8);
-// unset or invalid values keep the automatic choice.
+// Tuning overrides (DMOE_NT = 32 / 64 / 128, DMOE_KSPLIT_GU / DMOE_KSPLIT_DN = 1 / 2 / 4 / 8,
+// DMOE_ROUTER_SPLIT = 0 / 1, DMOE_COMBINE_MIN = tokens); unset or invalid values keep the
+// automatic choice.
 int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   if (!v || !*v) return dflt;
@@ -381,8 +383,7 @@ void dmoe_destroy(dmoe_layer* L) {
   cudaFree(L->br);
   for (DevWeight* w : {&L->gate, &L->up, &L->down, &L->sgate, &L->sup, &L->sdown}) free_weight(*w);
   cudaFree(L->parts);
-  cudaFree(L->probs);
-  cudaFree(L->sel);
+  cudaFree(L->arrivals);
   cudaFree(L->idx);
   cudaFree(L->wts);
   cudaFree(L->allowed);
@@ -393,6 +394,8 @@ void dmoe_destroy(dmoe_layer* L) {
   cudaFree(L->gu);
   cudaFree(L->pair_tok);
   cudaFree(L->pair_w);
+  cudaFree(L->pair_row);
+  cudaFree(L->ybuf);
   cudaFree(L->xdev);
   cudaFree(L->odev);
   cudaFree(L->err);
@@ -427,18 +430,25 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   const int64_t Imax = std::max(L->I, L->Is);
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;
   const int nseg = (int)((H + kRouterSeg - 1) / kRouterSeg);
-  const int64_t rl_tiles = ((n + 31) / 32) * ((E + 63) / 64);
-  const bool rl_split = rl_tiles < 2LL * L->sms;  // too few 32x64 tiles to fill the GPU: split by segment
+  bool rl_split = router_split(n, (int)E, L->sms);  // too few whole-K tiles: split by segment
+  if (const int f = env_int("DMOE_ROUTER_SPLIT", -1); f == 0 || f == 1) rl_split = f == 1;
   const int nparts = rl_split ? nseg : 1;
   const int nt = pick_nt(L, n);
 
   dmoe_status s;
   size_t dummy_cap;
   (void)dummy_cap;
-  if ((s = grow(L->probs, L->probs_cap, (size_t)n * E)) != DMOE_OK) return s;
-  if ((s = grow(L->sel, L->sel_cap, (size_t)n * E)) != DMOE_OK) return s;
+  if ((s = grow(L->parts, L->parts_cap, (size_t)nparts * n * E)) != DMOE_OK) return s;
   if (rl_split) {
-    if ((s = grow(L->parts, L->parts_cap, (size_t)nseg * n * E)) != DMOE_OK) return s;
+    // per-tile arrival counters: zeroed when (re)allocated, re-armed by the kernel after use
+    const size_t need = (size_t)router_arrivals(n, (int)E);
+    if (need > L->arrivals_cap) {
+      cudaFree(L->arrivals);
+      L->arrivals = nullptr;
+      L->arrivals_cap = 0;
+      if ((s = grow(L->arrivals, L->arrivals_cap, need)) != DMOE_OK) return s;
+      DMOE_CUDA(cudaMemsetAsync(L->arrivals, 0, L->arrivals_cap * sizeof(int32_t), st));
+    }
   }
   if ((s = grow(L->idx, L->idx_cap, (size_t)n * K)) != DMOE_OK) return s;
   if ((s = grow(L->wts, L->wts_cap, (size_t)n * K)) != DMOE_OK) return s;
@@ -466,11 +476,11 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
 
   // ---- router (src/diffuse-moe-graph.cpp:203-262)
   DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)E, st));
-  DMOE_CUDA(launch_router(xd, L->wr, L->br, L->parts, L->probs, L->sel, n, (int)H, (int)E, rl_split, st));
-  kernels += rl_split ? 2 : 1;
+  DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, rl_split, L->arrivals, st));
+  ++kernels;
   RouteArgs ra{};
-  ra.probs = L->probs;
-  ra.sel = L->sel;
+  ra.probs = L->parts;
+  ra.bias = L->br;
   ra.n = n;
   ra.e = (int)E;
   ra.top_k = (int)K;
@@ -494,8 +504,9 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
     if ((s = grow(L->hbuf, L->hbuf_cap, (size_t)rows * Imax)) != DMOE_OK) return s;
     if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows)) != DMOE_OK) return s;
     if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
+    if ((s = grow(L->pair_row, L->pair_row_cap, (size_t)n * K)) != DMOE_OK) return s;
     DMOE_CUDA(launch_scan_tiles(counts, (int)E, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
-    DMOE_CUDA(launch_gather(xd, n, (int)H, (int)K, ra.idx, ra.w, off, fill, L->xg, L->pair_tok, L->pair_w,
+    DMOE_CUDA(launch_gather(xd, n, (int)H, (int)K, ra.idx, ra.w, off, fill, L->xg, L->pair_tok, L->pair_w, L->pair_row,
                             L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, L->has_shared ? 1 : 0, st));
     kernels += 2;
     if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
@@ -582,13 +593,23 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
     if (prof) DMOE_CUDA(cudaEventRecord(L->ev[3], st));
 
     // ---- down GEMM (+ gate weights, slot sum, shared expert)
-    DMOE_CUDA(cudaMemsetAsync(od, 0, (size_t)n * H * 4, st));
+    // Deterministic path (DMOE_F_DETERMINISTIC): routed rows are stored to y and summed per
+    // token in slot order by combine_kernel, the shared rows stored straight into out.
+    // Otherwise the epilogue reduces every row into a zeroed out with fp32 atomics (measured
+    // faster at every size: the y round trip costs more than the reductions).
+    const bool combine = ks_dn == 1 && ((flags & DMOE_F_DETERMINISTIC) || n >= env_int("DMOE_COMBINE_MIN", 1 << 30));
+    if (combine) {
+      if ((s = grow(L->ybuf, L->ybuf_cap, (size_t)n * K * H)) != DMOE_OK) return s;
+    }
+    if (!combine || !L->has_shared) DMOE_CUDA(cudaMemsetAsync(od, 0, (size_t)n * H * 4, st));
     GemmParams dp = gp;
     dp.tm_b = tm_h;
     dp.ksplit = ks_dn;
     dp.gu_acc = nullptr;
     dp.out = od;
     dp.out_ld = H;
+    dp.y = combine ? L->ybuf : nullptr;
+    dp.y_ld = H;
     dp.pair_tok = L->pair_tok;
     dp.pair_w = L->pair_w;
     std::memset(&dp.grp, 0, sizeof(dp.grp));
@@ -610,6 +631,10 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
       DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, d0, grid, st));
       DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, d1, grid, st));
       kernels += 2;
+    }
+    if (combine) {
+      DMOE_CUDA(launch_combine(L->ybuf, H, n, L->pair_row, (int)K, od, H, L->has_shared ? 1 : 0, st));
+      ++kernels;
     }
     if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));
     L->stats.token_tile = nt;

@@ -52,9 +52,13 @@ struct GemmParams {
   int32_t h_quad_swap;  // bit g: group g's down matrix is q4_K, write its h with the quad swap
   float* gu_acc;        // split-K partial accumulators [rows][2 * gu_half], or null
   int64_t gu_half;
-  // down epilogue
+  // down epilogue: with y == null every row is reduced into out (fp32 vector atomics);
+  // otherwise shared rows store into out and routed row r stores w_r * (W_d h_r) into
+  // y[r - n_tokens] for combine_kernel (deterministic slot-order sum)
   float* out;
   int64_t out_ld;
+  float* y;
+  int64_t y_ld;
   const int32_t* pair_tok;
   const float* pair_w;
   uint32_t* err;
@@ -62,8 +66,8 @@ struct GemmParams {
 
 // Router: one routing block per CTA (src/diffuse-moe-graph.cpp:203-262).
 struct RouteArgs {
-  const float* probs;  // [n][e] sigmoid(router logits), canonical bits
-  const float* sel;    // [n][e] probs + expert bias (selection scores)
+  const float* probs;  // [n][e] p = sigmoid(router logit), canonical bits
+  const float* bias;   // [e] expert bias for the selection, or null
   int64_t n;
   int e, top_k, cap, blk;
   int use_block;       // block routing switch, evaluated on the host (:215-216)
@@ -75,14 +79,21 @@ struct RouteArgs {
   int32_t* counts;     // [e] per-expert pair counts (atomics; zeroed by the caller)
 };
 
-cudaError_t launch_router(const float* x, const float* wrt, const float* bias, float* part, float* probs, float* sel,
-                          int64_t n, int h, int e, bool split, cudaStream_t st);
+cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, bool split,
+                          int32_t* arrivals, cudaStream_t st);
+bool router_split(int64_t n, int e, int sms);
+int64_t router_arrivals(int64_t n, int e);  // split path: per-tile arrival counters needed
+// shared memory of route_kernel for `tpb` tokens per CTA and e experts; at most kRouteSmemMax
+constexpr size_t kRouteSmemMax = 200 * 1024;
+size_t route_smem_bytes(int64_t tpb, int64_t e);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
 cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, int32_t* off, int32_t* fill,
                               TokTile* tiles, int32_t* n_tiles, int32_t* n_active, cudaStream_t st);
 cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
                           const int32_t* off, int32_t* fill, __half* xg, int32_t* pair_tok, float* pair_w,
-                          int swap_shared, int swap_routed, int with_shared, cudaStream_t st);
+                          int32_t* pair_row, int swap_shared, int swap_routed, int with_shared, cudaStream_t st);
+cudaError_t launch_combine(const float* y, int64_t y_ld, int64_t n, const int32_t* pair_row, int top_k, float* out,
+                           int64_t h, int add_out, cudaStream_t st);
 cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows, int64_t n, int is, int iw,
                                  __half* hbuf, int64_t h_ld, int swap_shared, int swap_routed, cudaStream_t st);
 cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st);

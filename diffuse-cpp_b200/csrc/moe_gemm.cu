@@ -6,17 +6,19 @@
 //
 //   MODE_GATEUP: h[row][i] = silu(Wg_e[i] . x_row) * (Wu_e[i] . x_row)   -> fp16 hbuf
 //   MODE_DOWN:   out[tok][o] += w_row * (Wd_e[o] . h_row)                  -> fp32 out (red.add)
+//                or, for large N, y[row][o] = w_row * (Wd_e[o] . h_row) summed by combine_kernel
 //
 // "Swap-AB" orientation: weights are the MMA's M side (128 rows per tile), the tokens of one
 // expert the N side (NT per tile), K runs along the GGUF rows, so quantised weights stream
 // through TMA in their native block layout.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over a device-side tile list):
+// Warp roles (one CTA per SM, persistent over a device-side tile list):
 //   warp 0      TMA producer: weight tiles (raw GGUF bytes / fp16) + activation tiles -> smem ring
 //   warp 1      TMEM allocator + MMA issuer (tcgen05.mma kind::f16, fp32 accumulators in TMEM)
-//   warps 2..9  two dequant warpgroups: q4_K / q8_0 tile -> fp16 in registers -> tcgen05.st into
-//               TMEM (the A operand of the TS-form MMA, no shared-memory round trip), then the
-//               tile epilogue (tcgen05.ld of the accumulators, SwiGLU / weighted scatter-add).
+//   warps 2..9  epilogue: tcgen05.ld of the accumulators, SwiGLU (gate/up) or weighted rows /
+//               reductions (down), stored straight from the accumulator lanes
+//   warps 10..  dequant warpgroups: q4_K / q8_0 tile -> fp16 in registers -> tcgen05.st into
+//               TMEM (the A operand of the TS-form MMA, no shared-memory round trip)
 // F16 weights skip the dequant: TMA lands them 128B-swizzled and the SS-form MMA reads smem.
 //
 // q4_K K-order: a q4_K 32-bit word of quants holds bytes b0..b3 of weights (k, k+1, k+2, k+3)
@@ -40,14 +42,13 @@ struct GemmCfg {
   // + 128 x 4 fp32 scales; f16 two SW128 boxes of 128 x 64.
   static constexpr int W_BYTES = (WT == WT_Q4_K) ? 128 * 144 : (WT == WT_Q8_0) ? (128 * 128 + 128 * 16) : (128 * 128 * 2);
   static constexpr int STAGE_BYTES = B_BYTES + MATS * W_BYTES;
-  // roles: warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue, then NDQ dequant warpgroups
+  // roles: warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 epilogue (two per TMEM lane
+  // quarter, one per column half), then NDQ dequant warpgroups
   static constexpr int NDQ = QUANT ? NDQ_ : 0;
-  static constexpr int EPI_WARP0 = 2, DQ_WARP0 = 6;
+  static constexpr int EPI_WARP0 = 2, EPI_WARPS = 8, DQ_WARP0 = EPI_WARP0 + EPI_WARPS;
   static constexpr int THREADS = 32 * (DQ_WARP0 + 4 * NDQ);
-  // per epilogue warp: a 16-column x 32-feature fp32 transpose tile (row pitch 33: no bank
-  // conflicts either way), so stores and reductions leave as 16-byte vectors
-  static constexpr int EPI_BYTES = ((4 * 16 * 33 * 4 + 1023) / 1024) * 1024;
-  static constexpr int SMEM_BUDGET = 227 * 1024 - 2048 - EPI_BYTES;
+  static constexpr int EPI_COLS = NT / 2;  // accumulator columns per epilogue warp
+  static constexpr int SMEM_BUDGET = 227 * 1024 - 2048;
   static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
   // TMEM: accumulators (double-buffered when they fit next to a 2+ deep A ring), A ring
@@ -56,13 +57,13 @@ struct GemmCfg {
   static constexpr int ACC_BUFS = (2 * ACC_COLS + (QUANT ? 2 * A_COLS : 0) <= 512) ? 2 : 1;
   static constexpr int NA_RAW = QUANT ? (512 - ACC_BUFS * ACC_COLS) / A_COLS : 0;
   static constexpr int NA = NA_RAW > 4 ? 4 : NA_RAW;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
   // every dequant warp arrives on each stage's `empty` (after its own k-blocks, if any)
   static constexpr int EMPTY_COUNT = 1 + 4 * NDQ;
   static_assert(STAGES >= 2, "smem ring needs two stages");
   static_assert(!QUANT || NA >= 2, "TMEM A ring needs two buffers");
   static_assert(B_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1024-B aligned stage parts");
-  static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "tcgen05 M=128 needs N % 16 == 0");
+  static_assert(NT % 32 == 0 && NT >= 32 && NT <= 256, "tcgen05 M=128 needs N % 16 == 0; two column halves");
   static_assert(ACC_BUFS * ACC_COLS + NA * A_COLS <= 512, "TMEM budget");
   // The dequant warpgroups share the A ring round-robin (k-block kbs -> group kbs % NDQ,
   // buffer kbs % NA). A group then waits for buffer use u only after the MMA has consumed
@@ -248,7 +249,8 @@ __device__ __forceinline__ void dequant_q80_kblock(uint32_t qtile, uint32_t stil
   }
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+// silu(g) = g * (1 / (1 + e^-g)); for g -> -inf the reciprocal of inf is 0 and the product -0
+__device__ __forceinline__ float silu_f(float g) { return g * __frcp_rn(1.0f + __expf(-g)); }
 
 __device__ __forceinline__ int quad_swap(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
 
@@ -259,8 +261,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
   static_assert(C::RING_OK, "A ring needs at least one buffer per dequant warpgroup");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* epi = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = full + C::STAGES;
   uint64_t* afull = empty + C::STAGES;
@@ -284,7 +285,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], 4);
+      mbar_init(&accempty[b], C::EPI_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -425,93 +426,89 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     }
   } else if (warp < C::DQ_WARP0) {
     // ------------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // Warp w reads TMEM lane quarter w % 4 (the hardware's rule) and column half (w - 2) / 4.
+    // Lane = output feature, so every store below covers one contiguous 64 / 128-byte segment
+    // of a token's row; the down tile's gate weights and token ids sit in registers, loaded
+    // before the accumulator wait.
+    constexpr int HC = C::EPI_COLS, NCH = HC / 16, NWR = (HC + 31) / 32;
+    const int quarter = warp & 3;
+    const int cb = ((warp - C::EPI_WARP0) >> 2) * HC;  // first accumulator column of this warp
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t scr = smem_u32(epi) + (warp - C::EPI_WARP0) * (16 * 33 * 4);
     uint32_t tile_seq = 0;
     for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
       const TileInfo ti = decode_tile<NT>(p, t);
       const int ab = tile_seq % C::ACC_BUFS;
       const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
+      float wv[NWR];
+      int tv[NWR];
+#pragma unroll
+      for (int j = 0; j < NWR; ++j) {
+        const int c = cb + 32 * j + lane;
+        const bool routed = MODE == MODE_DOWN && ti.group != 0 && c < ti.nrows && 32 * j + lane < HC;
+        wv[j] = routed ? p.pair_w[ti.row0 + c] : 1.0f;
+        tv[j] = (routed && p.y == nullptr) ? p.pair_tok[ti.row0 + c] : ti.row0 + c;
+      }
       if (!role_wait(&accfull[ab], aph, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
       tc_fence_after();
       const uint32_t dbase = tbase + lane_off + ab * C::ACC_COLS;
       const int obase = ti.mt * kMTile + quarter * 32;  // first output feature of this warp
-#pragma unroll 1
-      for (int c0 = 0; c0 < NT && c0 < ti.nrows; c0 += 16) {
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const int c0 = cb + 16 * ch;
+        if (c0 >= ti.nrows) break;  // warp-uniform
         uint32_t acc0[16];
         tmem_ld16(dbase + c0, acc0);
         if constexpr (MODE == MODE_GATEUP) {
           uint32_t acc1[16];
           tmem_ld16(dbase + NT + c0, acc1);
           tmem_wait_ld();
+          const int64_t r0 = ti.row0 + c0;
           if (p.gu_acc == nullptr) {
-            // h = silu(g) * u, stored as 16-byte chunks of the (possibly quad-swapped) h row
+            // h = silu(g) * u into the (possibly quad-swapped) h row
             const int pl = ((p.h_quad_swap >> ti.group) & 1) ? quad_swap(lane) : lane;
+            __half* hcol = p.hbuf + r0 * p.h_ld + obase + pl;
 #pragma unroll
             for (int c = 0; c < 16; ++c)
-              sts32f(scr + (c * 33 + pl) * 4, silu_f(__uint_as_float(acc0[c])) * __uint_as_float(acc1[c]));
-            __syncwarp();
-#pragma unroll
-            for (int it = 0; it < 2; ++it) {
-              const int idx = it * 32 + lane, c = idx >> 2, j = idx & 3;
-              if (c0 + c < ti.nrows) {
-                const uint32_t sp = scr + (c * 33 + 8 * j) * 4;
-                float f[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) f[u] = lds32f(sp + 4 * u);
-                uint4 v;
-                v.x = as_u32(__floats2half2_rn(f[0], f[1]));
-                v.y = as_u32(__floats2half2_rn(f[2], f[3]));
-                v.z = as_u32(__floats2half2_rn(f[4], f[5]));
-                v.w = as_u32(__floats2half2_rn(f[6], f[7]));
-                *reinterpret_cast<uint4*>(p.hbuf + (int64_t)(ti.row0 + c0 + c) * p.h_ld + obase + 8 * j) = v;
-              }
-            }
-            __syncwarp();
+              if (c0 + c < ti.nrows)
+                hcol[(int64_t)c * p.h_ld] = __float2half_rn(silu_f(__uint_as_float(acc0[c])) * __uint_as_float(acc1[c]));
           } else {
-            // split-K: fp32 partial sums of g and u, reduced with 16-byte vector atomics
+            // split-K: fp32 partial sums of g and u
+            float* gcol = p.gu_acc + r0 * (2 * p.gu_half) + obase + lane;
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-#pragma unroll
-              for (int c = 0; c < 16; ++c) sts32f(scr + (c * 33 + lane) * 4, __uint_as_float(half ? acc1[c] : acc0[c]));
-              __syncwarp();
-#pragma unroll
-              for (int it = 0; it < 4; ++it) {
-                const int idx = it * 32 + lane, c = idx >> 3, g4 = idx & 7;
-                if (c0 + c < ti.nrows) {
-                  const uint32_t sp = scr + (c * 33 + 4 * g4) * 4;
-                  float* dst = p.gu_acc + (int64_t)(ti.row0 + c0 + c) * (2 * p.gu_half) + half * p.gu_half + obase +
-                               4 * g4;
-                  atomicAdd(reinterpret_cast<float4*>(dst),
-                            make_float4(lds32f(sp), lds32f(sp + 4), lds32f(sp + 8), lds32f(sp + 12)));
-                }
+            for (int c = 0; c < 16; ++c)
+              if (c0 + c < ti.nrows) {
+                atomicAdd(gcol + (int64_t)c * (2 * p.gu_half), __uint_as_float(acc0[c]));
+                atomicAdd(gcol + (int64_t)c * (2 * p.gu_half) + p.gu_half, __uint_as_float(acc1[c]));
               }
-              __syncwarp();
-            }
           }
         } else {
           tmem_wait_ld();
-          // out[tok] += w * y: transpose so each lane reduces 4 consecutive features of a token
+          if (p.y != nullptr) {
+            // shared rows into out, routed rows weighted into y
+            if (ti.group == 0) {
+              float* ocol = p.out + (int64_t)(ti.row0 + c0) * p.out_ld + obase + lane;
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            float wgt = 1.0f;
-            if (ti.group != 0) wgt = (c0 + c < ti.nrows) ? p.pair_w[ti.row0 + c0 + c] : 0.0f;
-            sts32f(scr + (c * 33 + lane) * 4, __uint_as_float(acc0[c]) * wgt);
-          }
-          __syncwarp();
+              for (int c = 0; c < 16; ++c)
+                if (c0 + c < ti.nrows) ocol[(int64_t)c * p.out_ld] = __uint_as_float(acc0[c]);
+            } else {
+              float* ycol = p.y + (int64_t)(ti.row0 + c0 - p.n_tokens) * p.y_ld + obase + lane;
 #pragma unroll
-          for (int it = 0; it < 4; ++it) {
-            const int idx = it * 32 + lane, c = idx >> 3, g4 = idx & 7;
-            if (c0 + c < ti.nrows) {
-              const int r = ti.row0 + c0 + c;
-              const int64_t tok = ti.group == 0 ? (int64_t)r : (int64_t)p.pair_tok[r];
-              const uint32_t sp = scr + (c * 33 + 4 * g4) * 4;
-              atomicAdd(reinterpret_cast<float4*>(p.out + tok * p.out_ld + obase + 4 * g4),
-                        make_float4(lds32f(sp), lds32f(sp + 4), lds32f(sp + 8), lds32f(sp + 12)));
+              for (int c = 0; c < 16; ++c) {
+                const int k = 16 * ch + c;
+                const float wgt = __shfl_sync(0xffffffffu, wv[k >> 5], k & 31);
+                if (c0 + c < ti.nrows) ycol[(int64_t)c * p.y_ld] = __uint_as_float(acc0[c]) * wgt;
+              }
+            }
+          } else {
+            // out[tok] += w * y, fp32 reductions of one 128-byte segment per token
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const int k = 16 * ch + c;
+              const float wgt = __shfl_sync(0xffffffffu, wv[k >> 5], k & 31);
+              const int tok = __shfl_sync(0xffffffffu, tv[k >> 5], k & 31);
+              if (c0 + c < ti.nrows) atomicAdd(p.out + (int64_t)tok * p.out_ld + obase + lane, __uint_as_float(acc0[c]) * wgt);
             }
           }
-          __syncwarp();
         }
       }
       tc_fence_before();

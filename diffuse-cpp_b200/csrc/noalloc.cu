@@ -30,10 +30,9 @@ constexpr int64_t kStaticMaxTokens = DMOE_STATIC_MAX_TOKENS;
 constexpr int64_t kStaticMaxExperts = DMOE_STATIC_MAX_EXPERTS;
 constexpr int64_t kStaticMaxEmbd = DMOE_STATIC_MAX_EMBD;
 
-// layout (floats): probs [T][E] | sel [T][E] | router weight transposed [H][E] | counts [E]
-constexpr size_t kProbsOff = 0;
-constexpr size_t kSelOff = kProbsOff + (size_t)kStaticMaxTokens * kStaticMaxExperts;
-constexpr size_t kWrtOff = kSelOff + (size_t)kStaticMaxTokens * kStaticMaxExperts;
+// layout (floats): logits [T][E] | router weight transposed [H][E] | counts [E]
+constexpr size_t kLogitsOff = 0;
+constexpr size_t kWrtOff = kLogitsOff + (size_t)kStaticMaxTokens * kStaticMaxExperts;
 constexpr size_t kCountsOff = kWrtOff + (size_t)kStaticMaxEmbd * kStaticMaxExperts;
 constexpr size_t kScratchFloats = kCountsOff + (size_t)kStaticMaxExperts;
 static_assert(kScratchFloats * sizeof(float) == DMOE_STATIC_SCRATCH_BYTES, "header states the scratch size");
@@ -105,7 +104,7 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
     return DMOE_ERR_UNSUPPORTED;
   }
   const int64_t tpb = moe_block_size > 1 ? std::max<int64_t>(moe_block_size, 32) : 32;
-  if ((tpb + 4) * n_expert * 4 > 200 * 1024) {
+  if (route_smem_bytes(tpb, n_expert) > kRouteSmemMax) {
     set_last_error("dmoe_route_static: moe_block_size x n_expert too large for the routing kernel");
     return DMOE_ERR_UNSUPPORTED;
   }
@@ -122,8 +121,7 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
     return DMOE_ERR_CUDA;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* probs = scratch + kProbsOff;
-  float* sel = scratch + kSelOff;
+  float* logits = scratch + kLogitsOff;
   float* wrt = scratch + kWrtOff;
   int32_t* counts = reinterpret_cast<int32_t*>(scratch + kCountsOff);
   const int H = (int)n_embd, E = (int)n_expert;
@@ -131,11 +129,11 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
       w_router, wrt, E, H);
   e = cudaGetLastError();
   if (e == cudaSuccess) e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)E, st);
-  if (e == cudaSuccess) e = launch_router(x, wrt, b_router, nullptr, probs, sel, n_tokens, H, E, false, st);
+  if (e == cudaSuccess) e = launch_router(x, wrt, logits, n_tokens, H, E, false, nullptr, st);
   if (e == cudaSuccess) {
     RouteArgs ra{};
-    ra.probs = probs;
-    ra.sel = sel;
+    ra.probs = logits;
+    ra.bias = b_router;
     ra.n = n_tokens;
     ra.e = E;
     ra.top_k = (int)n_expert_used;

@@ -14,6 +14,10 @@
 //   keep = (bmax - (thr * 1 + (-1e-6f))) > 0;  sel += keep ? 0 : -1e30            (:238-248)
 //   idx  = top-k of sel, descending, ties to the lower expert id                   (:252)
 //   w    = p[idx] / (float)(sum_s (double) p[idx_s]) * scale                       (:253-262)
+//
+// Two launches: router_logits_kernel (the GEMM, either whole logits or per-segment partials
+// P_s summed by the tile's last CTA, then p = sigmoid(logit)) and route_kernel (bias, then the
+// routing of one block per CTA).
 #include "dmoe_internal.h"
 #include "sm100.cuh"
 
@@ -55,20 +59,28 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Router logits: one CTA = 64 threads computing a 32-token x 64-expert tile; thread (ty, tx)
-// owns tokens 4 ty .. 4 ty + 3 and experts {4 tx .. 4 tx + 3} u {32 + 4 tx .. 32 + 4 tx + 3}.
-// Tiles of x [token][k] and of the transposed router weight wrt [k][expert] (transposed once at
-// bind time) arrive by cp.async into a double-buffered shared-memory ring.
-//   SPLIT = false: one CTA runs every segment, keeping tot = P_0 + P_1 + ... (large N).
-//   SPLIT = true:  one CTA per (tile, segment) writes its segment partial P_s, and
-//                  router_finish_kernel sums P_0 .. P_{S-1} left to right (small N, where the
-//                  tiles alone cannot fill the GPU).
-// Both produce the canonical logits, turned into probs = sigmoid(logit) and selection scores
-// sel = probs + bias (src/diffuse-moe-graph.cpp:204-210).
+// Router logits. CTA = 128 threads on a (16 TM) token x 64 expert tile; thread (ty, tx) =
+// (tid / 8, tid % 8) owns tokens TM ty .. TM ty + TM - 1 and experts {4 tx .. 4 tx + 3} u
+// {32 + 4 tx .. 32 + 4 tx + 3}: TM x 8 independent fma chains. x [token][k] and the transposed
+// router weight wrt [k][expert] (transposed once at bind time) arrive in 32-k chunks through a
+// 3-deep cp.async ring.
+//   SPLIT = false: the CTA runs every 256-k segment and keeps tot = P_0 + P_1 + ...; writes
+//                  p = sigmoid(logit) to part[0].
+//   SPLIT = true:  one CTA per (tile, segment) writes its partial P_s to part[s]; the last CTA
+//                  of a tile to finish (per-tile arrival counter) adds P_0 .. P_{S-1} left to
+//                  right, writes p to part[0] and re-arms the counter (small N, where whole-K
+//                  tiles cannot fill the GPU).
+// TM = 4 for large N (fewer shared-memory reads per fma), TM = 2 for small N (more CTAs).
 // ------------------------------------------------------------------------------------------
-constexpr int RL_TOK = 32, RL_EXP = 64, RL_KC = 64, RL_THREADS = 64;
+constexpr int RL_EXP = 64, RL_KC = 32, RL_THREADS = 128, RL_STAGES = 3;
 constexpr int RL_XP = RL_KC + 4;  // x tile row pitch (floats)
-constexpr int RL_SMEM = 2 * (RL_TOK * RL_XP + RL_KC * RL_EXP) * 4;
+
+template <int TM>
+constexpr int rl_tok() { return 16 * TM; }
+template <int TM>
+constexpr int rl_stage_floats() { return rl_tok<TM>() * RL_XP + RL_KC * RL_EXP; }
+template <int TM>
+constexpr int rl_smem() { return RL_STAGES * rl_stage_floats<TM>() * 4; }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
@@ -79,136 +91,169 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <bool SPLIT>
-__global__ void __launch_bounds__(RL_THREADS) router_logits_kernel(const float* __restrict__ x,
+// d = a * b + d on two fp32 lanes at once (sm_100 fma.rn.f32x2): each lane is an IEEE
+// round-to-nearest fma, bitwise the same as fmaf, at half the issue slots.
+__device__ __forceinline__ void ffma2(float2& d, float2 a, float2 b) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d.x), "+f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+}
+
+template <int TM, bool SPLIT>
+__global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const float* __restrict__ x,
                                                                    const float* __restrict__ wrt,
-                                                                   const float* __restrict__ bias,
-                                                                   float* __restrict__ part, float* __restrict__ probs,
-                                                                   float* __restrict__ sel, int64_t n, int h,
-                                                                   int e) {
-  extern __shared__ __align__(16) float rl_smem[];
-  const uint32_t xs0 = smem_u32(rl_smem);                     // [2][32][RL_XP]
-  const uint32_t ws0 = xs0 + 2 * RL_TOK * RL_XP * 4;          // [2][64 k][64 e]
+                                                                   float* __restrict__ part, int64_t n, int h, int e,
+                                                                   int32_t* __restrict__ arrivals) {
+  extern __shared__ __align__(16) float rl_smem_f[];
+  constexpr int TT = rl_tok<TM>();
+  const uint32_t sm0 = smem_u32(rl_smem_f);
   const int tid = threadIdx.x;
   const int ty = tid >> 3, tx = tid & 7;
-  const int64_t t0 = (int64_t)blockIdx.x * RL_TOK;
+  const int64_t t0 = (int64_t)blockIdx.x * TT;
   const int e0 = blockIdx.y * RL_EXP;
   const int nseg = h / kRouterSeg;
   const int s_begin = SPLIT ? (int)blockIdx.z : 0;
   const int s_end = SPLIT ? s_begin + 1 : nseg;
-  const int kc0 = s_begin * kRouterSeg, nchunks = (s_end - s_begin) * (kRouterSeg / RL_KC);
+  constexpr int CH_PER_SEG = kRouterSeg / RL_KC;
+  const int kc0 = s_begin * kRouterSeg, nchunks = (s_end - s_begin) * CH_PER_SEG;
 
+  auto xs_of = [&](int buf) { return sm0 + buf * rl_stage_floats<TM>() * 4; };
+  auto ws_of = [&](int buf) { return xs_of(buf) + TT * RL_XP * 4; };
   auto load_chunk = [&](int c, int buf) {
     const int kc = kc0 + c * RL_KC;
-    const uint32_t xs = xs0 + buf * RL_TOK * RL_XP * 4, ws = ws0 + buf * RL_KC * RL_EXP * 4;
-#pragma unroll
-    for (int r = 0; r < (RL_TOK * RL_KC / 4) / RL_THREADS; ++r) {  // 8 per thread
-      const int q = tid + r * RL_THREADS, t = q >> 4, k4 = q & 15;
+    const uint32_t xs = xs_of(buf), ws = ws_of(buf);
+    for (int q = tid; q < TT * (RL_KC / 4); q += RL_THREADS) {
+      const int t = q / (RL_KC / 4), k4 = q % (RL_KC / 4);
       const bool ok = t0 + t < n;
       const float* src = ok ? x + (t0 + t) * h + kc + 4 * k4 : x;
       cp_async16(xs + (t * RL_XP + 4 * k4) * 4, src, ok);
     }
 #pragma unroll
-    for (int r = 0; r < (RL_KC * RL_EXP / 4) / RL_THREADS; ++r) {  // 16 per thread
+    for (int r = 0; r < (RL_KC * RL_EXP / 4) / RL_THREADS; ++r) {
       const int q = tid + r * RL_THREADS, k = q >> 4, e4 = q & 15;
       const bool ok = e0 + 4 * e4 < e;
       const float* src = ok ? wrt + (int64_t)(kc + k) * e + e0 + 4 * e4 : wrt;
       cp_async16(ws + (k * RL_EXP + 4 * e4) * 4, src, ok);
     }
-    cp_async_commit();
   };
 
-  float tot[4][8], acc[4][8];
+  float tot[TM][8];
+  float2 acc[TM][4];  // experts (2 jp, 2 jp + 1) of the thread's 8
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < TM; ++i) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) tot[i][j] = acc[i][j] = 0.0f;
+    for (int j = 0; j < 8; ++j) tot[i][j] = 0.0f;
+#pragma unroll
+    for (int jp = 0; jp < 4; ++jp) acc[i][jp] = make_float2(0.0f, 0.0f);
+  }
 
-  load_chunk(0, 0);
+#pragma unroll
+  for (int c = 0; c < RL_STAGES - 1; ++c) {
+    if (c < nchunks) load_chunk(c, c);
+    cp_async_commit();
+  }
   for (int c = 0; c < nchunks; ++c) {
-    const int buf = c & 1;
-    if (c + 1 < nchunks) {
-      load_chunk(c + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint32_t xs = xs0 + buf * RL_TOK * RL_XP * 4, ws = ws0 + buf * RL_KC * RL_EXP * 4;
+    const int buf = c % RL_STAGES;
+    cp_async_wait<RL_STAGES - 2>();
+    __syncthreads();  // chunk c landed for every thread; chunk c - 1's buffer is free
+    if (c + RL_STAGES - 1 < nchunks) load_chunk(c + RL_STAGES - 1, (c + RL_STAGES - 1) % RL_STAGES);
+    cp_async_commit();
+    const uint32_t xs = xs_of(buf), ws = ws_of(buf);
 #pragma unroll 2
     for (int k4 = 0; k4 < RL_KC / 4; ++k4) {
-      float4 xv[4];
+      float4 xv[TM];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) xv[i] = lds128f(xs + ((4 * ty + i) * RL_XP + 4 * k4) * 4);
+      for (int i = 0; i < TM; ++i) xv[i] = lds128f(xs + ((TM * ty + i) * RL_XP + 4 * k4) * 4);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t wrow = ws + ((4 * k4 + kk) * RL_EXP) * 4;
         const float4 wa = lds128f(wrow + (4 * tx) * 4), wb = lds128f(wrow + (32 + 4 * tx) * 4);
-        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const float2 wp[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
+                              make_float2(wb.z, wb.w)};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < TM; ++i) {
           const float xi = kk == 0 ? xv[i].x : kk == 1 ? xv[i].y : kk == 2 ? xv[i].z : xv[i].w;
+          const float2 xx = make_float2(xi, xi);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xi, wv[j], acc[i][j]);
+          for (int jp = 0; jp < 4; ++jp) ffma2(acc[i][jp], xx, wp[jp]);
         }
       }
     }
-    __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
-    if (((c + 1) % (kRouterSeg / RL_KC)) == 0) {  // end of a segment: fold its partial in order
-      const bool first = (c + 1) == (kRouterSeg / RL_KC);
+    if (((c + 1) % CH_PER_SEG) == 0) {  // end of a segment: fold its partial in order
+      const bool first = (c + 1) == CH_PER_SEG;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          tot[i][j] = first ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
-          acc[i][j] = 0.0f;
+        for (int jp = 0; jp < 4; ++jp) {
+          tot[i][2 * jp] = first ? acc[i][jp].x : __fadd_rn(tot[i][2 * jp], acc[i][jp].x);
+          tot[i][2 * jp + 1] = first ? acc[i][jp].y : __fadd_rn(tot[i][2 * jp + 1], acc[i][jp].y);
+          acc[i][jp] = make_float2(0.0f, 0.0f);
         }
     }
   }
+  cp_async_wait<0>();
+  float* dst = part + (SPLIT ? (int64_t)s_begin * n * e : 0);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t tok = t0 + 4 * ty + i;
+  for (int i = 0; i < TM; ++i) {
+    const int64_t tok = t0 + TM * ty + i;
     if (tok >= n) continue;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int ee = e0 + (j < 4 ? 4 * tx + j : 32 + 4 * tx + (j - 4));
+    for (int j = 0; j < 8; j += 4) {
+      const int ee = e0 + (j == 0 ? 4 * tx : 32 + 4 * tx);
       if (ee >= e) continue;
       if constexpr (SPLIT) {
-        part[(int64_t)s_begin * n * e + tok * e + ee] = tot[i][j];
+        *reinterpret_cast<float4*>(dst + tok * e + ee) = make_float4(tot[i][j], tot[i][j + 1], tot[i][j + 2], tot[i][j + 3]);
       } else {
-        const float pv = sigmoid_canonical(tot[i][j]);
-        probs[tok * e + ee] = pv;
-        sel[tok * e + ee] = bias ? __fadd_rn(pv, bias[ee]) : pv;
+        *reinterpret_cast<float4*>(dst + tok * e + ee) =
+            make_float4(sigmoid_canonical(tot[i][j]), sigmoid_canonical(tot[i][j + 1]),
+                        sigmoid_canonical(tot[i][j + 2]), sigmoid_canonical(tot[i][j + 3]));
       }
     }
   }
-}
-
-// Small-N finish: one thread per (token, expert) logit; all segment partials are loaded before
-// the left-to-right sum.
-__global__ void __launch_bounds__(256) router_finish_kernel(const float* __restrict__ part,
-                                                            const float* __restrict__ bias, float* __restrict__ probs,
-                                                            float* __restrict__ sel, int64_t n, int e, int nseg) {
-  const int64_t off = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (off >= n * e) return;
-  const int64_t ps = n * e;
-  float pp[16];
-  float l = __ldcs(part + off);
-  for (int s0 = 1; s0 < nseg; s0 += 16) {
+  if constexpr (SPLIT) {
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    if (tid == 0) s_last = atomicAdd(&arrivals[tile], 1) == nseg - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // this tile's logits = P_0 + P_1 + ... in segment order; p = sigmoid(logit) into part[0]
+    const int64_t ps = n * e;
+    for (int q = tid; q < TT * (RL_EXP / 4); q += RL_THREADS) {
+      const int t = q / (RL_EXP / 4), e4 = q % (RL_EXP / 4);
+      const int64_t tok = t0 + t;
+      const int ee = e0 + 4 * e4;
+      if (tok >= n || ee >= e) continue;
+      const float4* src = reinterpret_cast<const float4*>(part + tok * e + ee);
+      float4 l = __ldcg(src);
+      for (int s0 = 1; s0 < nseg; s0 += 8) {
+        float4 v[8];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) pp[u] = (s0 + u < nseg) ? __ldcs(part + (int64_t)(s0 + u) * ps + off) : 0.0f;
+        for (int u = 0; u < 8; ++u)
+          if (s0 + u < nseg) v[u] = __ldcg(src + (int64_t)(s0 + u) * (ps / 4));
 #pragma unroll
-    for (int u = 0; u < 16; ++u)
-      if (s0 + u < nseg) l = __fadd_rn(l, pp[u]);
+        for (int u = 0; u < 8; ++u)
+          if (s0 + u < nseg) {
+            l.x = __fadd_rn(l.x, v[u].x);
+            l.y = __fadd_rn(l.y, v[u].y);
+            l.z = __fadd_rn(l.z, v[u].z);
+            l.w = __fadd_rn(l.w, v[u].w);
+          }
+      }
+      *reinterpret_cast<float4*>(part + tok * e + ee) =
+          make_float4(sigmoid_canonical(l.x), sigmoid_canonical(l.y), sigmoid_canonical(l.z), sigmoid_canonical(l.w));
+    }
+    if (tid == 0) arrivals[tile] = 0;  // re-armed for the next launch on this stream
   }
-  const float pv = sigmoid_canonical(l);
-  probs[off] = pv;
-  sel[off] = bias ? __fadd_rn(pv, bias[off % e]) : pv;
 }
 
 // ------------------------------------------------------------------------------------------
 // Routing: one CTA of 1024 threads per block of `blk` tokens (32 tokens when block routing is
-// off), from the probs / selection scores of the logits kernel.
+// off), from p = sigmoid(logit); the block's p stays in shared memory for the gate weights.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
@@ -219,42 +264,38 @@ constexpr int RT_THREADS = 1024;
 __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
   extern __shared__ float rsm[];
   const int tpb = a.use_block ? a.blk : 32;  // tokens per CTA
-  float* ss = rsm;                           // [tpb][e] selection scores (masked in place)
-  float* bmax = ss + tpb * a.e;              // [e] block max of the selection scores
-  float* addv = bmax + a.e;                  // [e] 0 or -1e30
-  int* gt_s = reinterpret_cast<int*>(addv + a.e);  // [e]
-  int* eq_s = gt_s + a.e;                          // [e]
+  const int E = a.e;
+  float* ss = rsm;                                 // [tpb][E] selection scores (masked in place)
+  float* pp = ss + tpb * E;                        // [tpb][E] probabilities
+  float* bmax = pp + tpb * E;                      // [E] block max of the selection scores
+  float* addv = bmax + E;                          // [E] 0 or -1e30
+  int* gt_s = reinterpret_cast<int*>(addv + E);    // [E]
+  int* eq_s = gt_s + E;                            // [E]
+  int* cnt_s = eq_s + E;                           // [E] pairs per expert in this CTA
   __shared__ float thr_s;
   const int tid = threadIdx.x;
   const int64_t t0 = (int64_t)blockIdx.x * tpb;
   const int ntok = (int)min((int64_t)tpb, a.n - t0);
-  const int cnt = ntok * a.e;
-  // stage the block's selection scores (coalesced, 4 loads in flight per thread)
-  const float* sg = a.sel + t0 * a.e;
-  for (int base = 0; base < cnt; base += 4 * RT_THREADS) {
-    float v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int idx = base + u * RT_THREADS + tid;
-      v[u] = idx < cnt ? sg[idx] : 0.0f;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int idx = base + u * RT_THREADS + tid;
-      if (idx < cnt) ss[idx] = v[u];
-    }
+  const int cnt = ntok * E;
+  // p and sel = p + bias (:204-210)
+  const float* pg = a.probs + t0 * E;
+  for (int i = tid; i < cnt; i += RT_THREADS) {
+    const float pv = pg[i];
+    pp[i] = pv;
+    ss[i] = a.bias ? __fadd_rn(pv, a.bias[i % E]) : pv;
   }
-  for (int ee = tid; ee < a.e; ee += RT_THREADS) {
+  for (int ee = tid; ee < E; ee += RT_THREADS) {
     gt_s[ee] = 0;
     eq_s[ee] = 0;
+    cnt_s[ee] = 0;
   }
   __syncthreads();
   if (a.use_block) {
     // block max by the fold m = s_t + relu(m - s_t), t = 1 .. blk-1 in order (:223-229)
-    for (int ee = tid; ee < a.e; ee += RT_THREADS) {
+    for (int ee = tid; ee < E; ee += RT_THREADS) {
       float m = ss[ee];
       for (int t = 1; t < tpb; ++t) {
-        const float st = ss[t * a.e + ee];
+        const float st = ss[t * E + ee];
         const float d = __fsub_rn(m, st);
         const float rl = d > 0.0f ? d : 0.0f;
         m = __fadd_rn(st, rl);
@@ -264,13 +305,13 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
     __syncthreads();
     // thr = value at position cap-1 of bmax sorted descending (:231-236): rank counts split
     // over `nsp` threads per expert
-    const int nsp = max(1, RT_THREADS / a.e);
-    const int chunk = (a.e + nsp - 1) / nsp;
-    if (tid < nsp * a.e) {
-      const int ee = tid % a.e, q = tid / a.e;
+    const int nsp = max(1, RT_THREADS / E);
+    const int chunk = (E + nsp - 1) / nsp;
+    if (tid < nsp * E) {
+      const int ee = tid % E, q = tid / E;
       const float v = bmax[ee];
       int gt = 0, eq = 0;
-      const int j1 = min(a.e, (q + 1) * chunk);
+      const int j1 = min(E, (q + 1) * chunk);
       for (int j = q * chunk; j < j1; ++j) {
         const float u = bmax[j];
         gt += u > v;
@@ -280,41 +321,51 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
       atomicAdd(&eq_s[ee], eq);
     }
     __syncthreads();
-    for (int ee = tid; ee < a.e; ee += RT_THREADS) {
+    for (int ee = tid; ee < E; ee += RT_THREADS) {
       const int gt = gt_s[ee], eq = eq_s[ee];
       if (gt <= a.cap - 1 && a.cap - 1 < gt + eq) thr_s = bmax[ee];  // all writers store the same value
     }
     __syncthreads();
     // keep = step(bmax - (thr - 1e-6)); masked scores += -1e30 (:238-248)
     const float thr_m = __fadd_rn(__fmul_rn(thr_s, 1.0f), -1e-6f);
-    for (int ee = tid; ee < a.e; ee += RT_THREADS) {
+    for (int ee = tid; ee < E; ee += RT_THREADS) {
       const float dlt = __fsub_rn(bmax[ee], thr_m);
       const bool keep = dlt > 0.0f;
-      if (a.allowed) a.allowed[(int64_t)blockIdx.x * a.e + ee] = keep ? 1 : 0;
+      if (a.allowed) a.allowed[(int64_t)blockIdx.x * E + ee] = keep ? 1 : 0;
       addv[ee] = keep ? 0.0f : -1e30f;
     }
     __syncthreads();
-    for (int idx = tid; idx < cnt; idx += RT_THREADS) ss[idx] = __fadd_rn(ss[idx], addv[idx % a.e]);
+    for (int i = tid; i < cnt; i += RT_THREADS) ss[i] = __fadd_rn(ss[i], addv[i % E]);
     __syncthreads();
   }
-  // per-token top-k (:252): one warp per token, ties to the lower expert id
+  // per-token top-k (:252): one warp per token, ties to the lower expert id. Each lane keeps
+  // the best of its candidates (experts lane, lane + 32, ...); every round the warp reduces the
+  // lanes' bests, and only the winning lane marks its candidate taken and rescans.
   const int warp = tid >> 5, lane = tid & 31;
+  const int ncand = (E - lane + 31) / 32;  // this lane's candidates (<= 32)
   for (int t = warp; t < ntok; t += RT_THREADS / 32) {
-    const float* st = ss + t * a.e;
-    uint32_t taken = 0;  // bit j: candidate lane + 32 j already selected (e <= 1024)
-    int sel_idx[16];
-    for (int s = 0; s < a.top_k; ++s) {
-      float bv = 0.0f;
-      int bi = -1;
-      for (int j = 0; j * 32 + lane < a.e; ++j) {
+    const float* st = ss + t * E;
+    uint32_t taken = 0;
+    float hv = 0.0f;
+    int hi = -1;
+    auto rescan = [&]() {
+      hv = 0.0f;
+      hi = -1;
+      for (int j = 0; j < ncand; ++j) {
         if (taken & (1u << j)) continue;
         const int ee = j * 32 + lane;
         const float v = st[ee];
-        if (bi < 0 || better(v, ee, bv, bi)) {
-          bv = v;
-          bi = ee;
+        if (hi < 0 || better(v, ee, hv, hi)) {
+          hv = v;
+          hi = ee;
         }
       }
+    };
+    rescan();
+    int sel_idx = -1;  // lane s < top_k keeps slot s
+    for (int s = 0; s < a.top_k; ++s) {
+      float bv = hv;
+      int bi = hi;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -324,57 +375,67 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
           bi = oi;
         }
       }
-      if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-      sel_idx[s] = bi;
+      if (lane == s) sel_idx = bi;
+      if (bi >= 0 && (bi & 31) == lane) {
+        taken |= 1u << (bi >> 5);
+        rescan();
+      }
     }
-    // gates from the unbiased probs, renormalised (sum in double) and scaled (:253-262)
-    if (lane == 0) {
-      const int64_t tok = t0 + t;
-      float wv[16];
-      double sum = 0.0;
-      for (int s = 0; s < a.top_k; ++s) {
-        wv[s] = a.probs[tok * a.e + sel_idx[s]];
-        sum = __dadd_rn(sum, (double)wv[s]);
-      }
+    // gates from the unbiased probs, renormalised (sum in double, slot order) and scaled (:253-262)
+    const float pv = lane < a.top_k ? pp[t * E + sel_idx] : 0.0f;
+    double sum = 0.0;
+    for (int s = 0; s < a.top_k; ++s) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, pv, s));
+    if (lane < a.top_k) {
       const float fs = __double2float_rn(sum);
-      for (int s = 0; s < a.top_k; ++s) {
-        float v = wv[s];
-        if (a.norm_topk) v = __fdiv_rn(v, fs);
-        if (a.scale != 1.0f) v = __fmul_rn(v, a.scale);
-        a.idx[tok * a.top_k + s] = sel_idx[s];
-        a.w[tok * a.top_k + s] = v;
-        atomicAdd(&a.counts[sel_idx[s]], 1);
-      }
+      float v = pv;
+      if (a.norm_topk) v = __fdiv_rn(v, fs);
+      if (a.scale != 1.0f) v = __fmul_rn(v, a.scale);
+      const int64_t tok = t0 + t;
+      a.idx[tok * a.top_k + lane] = sel_idx;
+      a.w[tok * a.top_k + lane] = v;
+      atomicAdd(&cnt_s[sel_idx], 1);
     }
   }
+  __syncthreads();
+  for (int ee = tid; ee < E; ee += RT_THREADS)
+    if (cnt_s[ee]) atomicAdd(&a.counts[ee], cnt_s[ee]);
 }
 
-// Fills probs and sel [n][e]. split = true: one CTA per (tile, segment) with partials in `part`
-// [h / 256][n][e], then the elementwise finish.
-cudaError_t launch_router(const float* x, const float* wrt, const float* bias, float* part, float* probs, float* sel,
-                          int64_t n, int h, int e, bool split, cudaStream_t st) {
+// p = sigmoid(logit) into part[0] ([n][e]); the split path also uses part[1 .. h/256 - 1] for
+// partials and `arrivals` (router_arrivals(n, e) zeroed ints, left zeroed again).
+cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, bool split,
+                          int32_t* arrivals, cudaStream_t st) {
   if (h % kRouterSeg) return cudaErrorInvalidValue;
   const int nseg = h / kRouterSeg;
-  dim3 grid((unsigned)((n + RL_TOK - 1) / RL_TOK), (unsigned)((e + RL_EXP - 1) / RL_EXP), split ? (unsigned)nseg : 1u);
+  const unsigned gy = (unsigned)((e + RL_EXP - 1) / RL_EXP);
   if (split) {
-    cudaFuncSetAttribute(router_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, RL_SMEM);
-    router_logits_kernel<true><<<grid, RL_THREADS, RL_SMEM, st>>>(x, wrt, bias, part, probs, sel, n, h, e);
-    cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
-    const int64_t cnt = n * e;
-    router_finish_kernel<<<(unsigned)((cnt + 255) / 256), 256, 0, st>>>(part, bias, probs, sel, n, e, nseg);
+    dim3 grid((unsigned)((n + rl_tok<2>() - 1) / rl_tok<2>()), gy, (unsigned)nseg);
+    cudaFuncSetAttribute(router_logits_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, rl_smem<2>());
+    if (!arrivals) return cudaErrorInvalidValue;
+    router_logits_kernel<2, true><<<grid, RL_THREADS, rl_smem<2>(), st>>>(x, wrt, part, n, h, e, arrivals);
   } else {
-    cudaFuncSetAttribute(router_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, RL_SMEM);
-    router_logits_kernel<false><<<grid, RL_THREADS, RL_SMEM, st>>>(x, wrt, bias, part, probs, sel, n, h, e);
+    dim3 grid((unsigned)((n + rl_tok<4>() - 1) / rl_tok<4>()), gy, 1u);
+    cudaFuncSetAttribute(router_logits_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, rl_smem<4>());
+    router_logits_kernel<4, false><<<grid, RL_THREADS, rl_smem<4>(), st>>>(x, wrt, part, n, h, e, nullptr);
   }
   return cudaGetLastError();
 }
 
+// Splitting by segment pays when the whole-K tiles cannot fill the GPU twice over.
+bool router_split(int64_t n, int e, int sms) {
+  const int64_t tiles = ((n + rl_tok<4>() - 1) / rl_tok<4>()) * ((e + RL_EXP - 1) / RL_EXP);
+  return tiles < 2LL * sms;
+}
+
+int64_t router_arrivals(int64_t n, int e) { return ((n + rl_tok<2>() - 1) / rl_tok<2>()) * ((e + RL_EXP - 1) / RL_EXP); }
+
+size_t route_smem_bytes(int64_t tpb, int64_t e) { return sizeof(float) * (size_t)((2 * tpb + 5) * e); }
+
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
   const int tpb = a.use_block ? a.blk : 32;
   const int64_t nblocks = (a.n + tpb - 1) / tpb;
-  const size_t smem = sizeof(float) * ((size_t)tpb * a.e + 4 * (size_t)a.e);
-  cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  const size_t smem = route_smem_bytes(tpb, a.e);
+  cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRouteSmemMax);
   route_kernel<<<(unsigned)nblocks, RT_THREADS, smem, st>>>(a);
   return cudaGetLastError();
 }

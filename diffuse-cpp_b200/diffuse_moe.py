@@ -25,7 +25,7 @@ LIB_PATH = os.path.join(_HERE, "libdiffuse_moe.so")
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K = 0, 1, 8, 12
 TYPE_NAMES = {TYPE_F32: "f32", TYPE_F16: "f16", TYPE_Q8_0: "q8_0", TYPE_Q4_K: "q4_K"}
 
-F_HOST_PTRS, F_ROUTE_ONLY, F_PROFILE = 1, 2, 4
+F_HOST_PTRS, F_ROUTE_ONLY, F_PROFILE, F_DETERMINISTIC = 1, 2, 4, 8
 
 STATUS_NAMES = {
     0: "DMOE_OK",
@@ -220,9 +220,10 @@ class MoELayer:
         self._keep.clear()  # weights are on the device now
 
     def forward(self, x, out=None, route: bool = False, route_only: bool = False, profile: bool = False,
-                stream: Optional[int] = None):
+                stream: Optional[int] = None, deterministic: bool = False):
         """x: numpy [n, H] float32 (host mode) or torch CUDA float32 tensor (device mode).
-        Returns out (and (idx, weights, allowed) when route=True)."""
+        Returns out (and (idx, weights, allowed) when route=True). deterministic=True selects the
+        bitwise-reproducible slot-order sum (DMOE_F_DETERMINISTIC)."""
         lib = load()
         H = self.hp["n_embd"]
         K = self.hp["n_expert_used"]
@@ -230,7 +231,8 @@ class MoELayer:
         blk = self.hp.get("moe_block_size", 32)
         is_np = isinstance(x, np.ndarray)
         n = int(x.shape[0])
-        flags = (F_HOST_PTRS if is_np else 0) | (F_ROUTE_ONLY if route_only else 0) | (F_PROFILE if profile else 0)
+        flags = ((F_HOST_PTRS if is_np else 0) | (F_ROUTE_ONLY if route_only else 0) | (F_PROFILE if profile else 0)
+                 | (F_DETERMINISTIC if deterministic else 0))
         if is_np:
             x = np.ascontiguousarray(x, dtype=np.float32)
             if out is None and not route_only:

@@ -119,6 +119,11 @@ typedef struct dmoe_stats {
                                  returns after the result is on the host */
 #define DMOE_F_ROUTE_ONLY 2u  /* run the router only (out is not touched) */
 #define DMOE_F_PROFILE 4u     /* record CUDA events around each stage (dmoe_get_stats) */
+#define DMOE_F_DETERMINISTIC 8u /* bitwise-reproducible output: every (token, slot) row of the down
+                                   projection is stored and summed per token in slot order, then
+                                   the shared expert added (the order of diffuse-moe-graph.cpp:
+                                   273-286); without it rows are reduced with fp32 atomics, which
+                                   is faster but leaves the summation order to the hardware */
 
 /* Binds one layer: validates the shapes, uploads router, bias and expert weights to the device
  * once (library-owned), prepares the TMA descriptors. Replaces the per-forward weight binding
@@ -177,7 +182,7 @@ size_t dmoe_quantized_size(int32_t type, int64_t nrows, int64_t n_per_row);
 #define DMOE_STATIC_MAX_EXPERTS 256
 #define DMOE_STATIC_MAX_EMBD 8192
 #define DMOE_STATIC_SCRATCH_BYTES                                                                  \
-  (4ull * (2ull * DMOE_STATIC_MAX_TOKENS * DMOE_STATIC_MAX_EXPERTS +                                \
+  (4ull * (1ull * DMOE_STATIC_MAX_TOKENS * DMOE_STATIC_MAX_EXPERTS +                                \
            (unsigned long long)DMOE_STATIC_MAX_EMBD * DMOE_STATIC_MAX_EXPERTS + DMOE_STATIC_MAX_EXPERTS))
 dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64_t n_embd, const float* w_router,
                               const float* b_router, int64_t n_expert, int64_t n_expert_used,
