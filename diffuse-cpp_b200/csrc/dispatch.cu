@@ -132,7 +132,6 @@ __global__ void swiglu_finish_kernel(const float* __restrict__ gu, int64_t gu_ha
 
 // One CTA per token. y holds the weighted routed rows (row r of the gathered layout at
 // y + (r - n) * y_ld); out holds the shared expert's rows when add_out is set.
-constexpr int kMaxTopK = 16;
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, int64_t y_ld, int64_t n,
                                                       const int32_t* __restrict__ pair_row, int top_k,
                                                       float* __restrict__ out, int64_t h, int add_out) {

@@ -16,12 +16,15 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <chrono>
 #include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 
 #include "../../include/diffuse_moe.h"
 #include "dmoe_internal.h"
+#include "nccl_dyn.h"
 
 using namespace dmoe;
 
@@ -192,6 +195,22 @@ struct dmoe_layer {
   float* xdev = nullptr; size_t xdev_cap = 0;
   float* odev = nullptr; size_t odev_cap = 0;
   uint32_t* err = nullptr;
+  // expert parallelism: this rank owns experts [rank * e_local, (rank + 1) * e_local)
+  int world = 1, rank = 0;
+  int64_t e_local = 0;
+  int timeout_ms = 60000;
+  ncclComm_t comm = nullptr;
+  bool broken = false;  // a collective failed or timed out; the communicator was aborted
+  uint32_t* ep_mask = nullptr; size_t ep_mask_cap = 0;
+  int32_t* ep_pos = nullptr; size_t ep_pos_cap = 0;
+  int32_t* ep_cnt = nullptr; size_t ep_cnt_cap = 0;  // [send counts W][recv counts W]
+  __half* ep_xs = nullptr; size_t ep_xs_cap = 0;     // rows sent, [S][H]
+  int32_t* ep_ms = nullptr; size_t ep_ms_cap = 0;    // slot lists sent, [S][2 top_k]
+  __half* ep_xr = nullptr; size_t ep_xr_cap = 0;     // rows received, [R][H]
+  int32_t* ep_mr = nullptr; size_t ep_mr_cap = 0;    // slot lists received
+  float* ep_part = nullptr; size_t ep_part_cap = 0;  // partial rows computed here for others, [R][H]
+  float* ep_back = nullptr; size_t ep_back_cap = 0;  // partial rows returned to this rank, [S][H]
+  int32_t* ep_host = nullptr;                        // pinned: the 2W counts
   // statistics
   dmoe_stats stats{};
   int32_t* host_counters = nullptr;  // pinned: n_tiles, n_active
@@ -243,13 +262,15 @@ int pick_nt(const dmoe_layer* L, int64_t n) {
   const int forced = env_int("DMOE_NT", 0);
   if (forced == 32 || forced == 64 || forced == 128) return forced;
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < L->E && n % L->blk == 0;
+  // pairs computed here: n * top_k on one GPU, and the same on average per rank with expert
+  // parallelism (every rank sends n * top_k (token, slot) pairs, spread over the ranks)
   const int64_t pairs = n * L->K;
-  int64_t active = std::min<int64_t>(L->E, pairs);
-  if (use_block) active = std::min<int64_t>(active, L->cap * (n / L->blk));
+  int64_t active = std::min<int64_t>(L->world > 1 ? L->e_local : L->E, pairs);
+  if (use_block && L->world == 1) active = std::min<int64_t>(active, L->cap * (n / L->blk));
   // weights are streamed once per token tile: size the tile for the busiest expert, whose
-  // count is at most n (each token picks an expert once) and is estimated as 3x the mean + 8
+  // count is at most the number of tokens that can reach it and is estimated as 3x the mean + 8
   const double avg = active > 0 ? (double)pairs / (double)active : 0.0;
-  const double busiest = std::min((double)n, 3.0 * avg + 8.0);
+  const double busiest = std::min((double)n * L->world, 3.0 * avg + 8.0);
   if (busiest <= 32.0) return 32;
   if (busiest <= 64.0) return 64;
   return 128;
@@ -284,6 +305,346 @@ void fill_group(GemmGroup& g, const DevWeight& w, int32_t type, int64_t rows_per
   g.present = 1;
 }
 
+
+// ------------------------------------------------------------------------------------------
+// expert stage: gate/up GEMM (+ SwiGLU) and down GEMM over the gathered layout (rows [0, n_sh)
+// shared expert, then routed pairs), src/diffuse-moe-graph.cpp:264-286
+// ------------------------------------------------------------------------------------------
+// out_sh: shared rows' output [n_sh][H]; out_rt: routed rows' reduction target (pair_tok[r]
+// indexes it), rt_rows of it zeroed here when it is not out_sh. combine = deterministic path
+// (single GPU only): routed rows stored to ybuf, then summed per token in slot order.
+dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t rows, int nt, int32_t* n_tiles,
+                        float* out_sh, float* out_rt, int64_t rt_rows, bool combine, bool prof, int& kernels) {
+  const int64_t H = L->H, K = L->K;
+  const int64_t Imax = std::max(L->I, L->Is);
+  const int64_t E_here = L->world > 1 ? L->e_local : L->E;
+  dmoe_status s;
+  CUtensorMap tm_x, tm_h;
+  if ((s = make_map(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->xg, (uint64_t)H, (uint64_t)rows, (uint64_t)H * 2, 64,
+                    (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+    return s;
+  if ((s = make_map(&tm_h, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->hbuf, (uint64_t)Imax, (uint64_t)rows,
+                    (uint64_t)Imax * 2, 64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+    return s;
+  const int64_t pairs = rows - n_sh;
+  const int64_t tt_est = std::min<int64_t>(E_here, pairs) + pairs / nt;
+  const int64_t sh_tt = L->has_shared ? (n_sh + nt - 1) / nt : 0;
+  const bool same_type = !L->has_shared || L->stype == L->etype;
+  const int gu_stage_r = gemm_stage_k(L->etype), gu_stage_s = gemm_stage_k(L->stype);
+  const int64_t gu_tiles = tt_est * (L->I / kMTile) + sh_tt * (L->Is / kMTile);
+  int ks_gu = pick_ksplit(gu_tiles, L->sms,
+                          {(int)(H / gu_stage_r), L->has_shared ? (int)(H / gu_stage_s) : (int)(H / gu_stage_r)});
+  if ((size_t)rows * 2 * Imax * 4 > (256ull << 20)) ks_gu = 1;
+  const int64_t dn_tiles = (tt_est + sh_tt) * (H / kMTile);
+  int ks_dn = pick_ksplit(dn_tiles, L->sms,
+                          {(int)(L->I / gu_stage_r), L->has_shared ? (int)(L->Is / gu_stage_s) : (int)(L->I / gu_stage_r)});
+  {
+    const int f_gu = env_int("DMOE_KSPLIT_GU", 0), f_dn = env_int("DMOE_KSPLIT_DN", 0);
+    auto divides = [&](int ks, int64_t k_r, int64_t k_s) {
+      return ks >= 1 && ks <= 8 && (ks & (ks - 1)) == 0 && k_r % ks == 0 && k_s % ks == 0;
+    };
+    const int64_t gr = H / gu_stage_r, gs = L->has_shared ? H / gu_stage_s : gr;
+    const int64_t dr = L->I / gu_stage_r, ds = L->has_shared ? L->Is / gu_stage_s : dr;
+    if (divides(f_gu, gr, gs) && (size_t)rows * 2 * Imax * 4 <= (256ull << 20)) ks_gu = f_gu;
+    if (divides(f_dn, dr, ds)) ks_dn = f_dn;
+  }
+  if (ks_gu > 1) {
+    if ((s = grow(L->gu, L->gu_cap, (size_t)rows * 2 * Imax)) != DMOE_OK) return s;
+    DMOE_CUDA(cudaMemsetAsync(L->gu, 0, (size_t)rows * 2 * Imax * 4, st));
+  }
+  GemmParams gp;
+  std::memset(&gp, 0, sizeof(gp));
+  gp.tm_b = tm_x;
+  gp.tiles = L->tiles;
+  gp.n_tiles = n_tiles;
+  gp.n_shared_tt = (int32_t)sh_tt;
+  gp.ksplit = ks_gu;
+  gp.n_tokens = n_sh;
+  gp.hbuf = L->hbuf;
+  gp.h_ld = Imax;
+  gp.h_quad_swap = (L->stype == DMOE_TYPE_Q4_K ? 1 : 0) | (L->etype == DMOE_TYPE_Q4_K ? 2 : 0);
+  gp.gu_acc = ks_gu > 1 ? L->gu : nullptr;
+  gp.gu_half = Imax;
+  gp.err = L->err;
+  if (L->has_shared) {
+    gp.tm_w[0][0] = L->sgate.tm_q;
+    gp.tm_w[0][1] = L->sup.tm_q;
+    gp.tm_s[0][0] = L->sgate.tm_s;
+    gp.tm_s[0][1] = L->sup.tm_s;
+    fill_group(gp.grp[0], L->sgate, L->stype, L->Is, L->Is);
+  }
+  gp.tm_w[1][0] = L->gate.tm_q;
+  gp.tm_w[1][1] = L->up.tm_q;
+  gp.tm_s[1][0] = L->gate.tm_s;
+  gp.tm_s[1][1] = L->up.tm_s;
+  fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I);
+  const int grid = L->sms;
+  const int ndq = env_int("DMOE_NDQ", 2);  // dequant warpgroups per CTA (2, 3 or 4)
+  if (same_type) {
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, gp, grid, st));
+    ++kernels;
+  } else {
+    GemmParams g0 = gp, g1 = gp;
+    g0.grp[1].present = 0;
+    g1.grp[0].present = 0;
+    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, ndq, g0, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, g1, grid, st));
+    kernels += 2;
+  }
+  if (ks_gu > 1) {
+    DMOE_CUDA(launch_swiglu_finish(L->gu, Imax, rows, n_sh, (int)L->Is, (int)L->I, L->hbuf, Imax,
+                                   L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, st));
+    ++kernels;
+  }
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[3], st));
+
+  // ---- down GEMM (+ gate weights, slot sum, shared expert)
+  // Deterministic path: routed rows are stored to y and summed per token in slot order by
+  // combine_kernel, the shared rows stored straight into out. Otherwise the epilogue reduces
+  // every row into zeroed outputs with fp32 atomics (measured faster at every size: the y
+  // round trip costs more than the reductions).
+  combine = combine && ks_dn == 1 && out_rt == out_sh;
+  if (combine) {
+    if ((s = grow(L->ybuf, L->ybuf_cap, (size_t)pairs * H)) != DMOE_OK) return s;
+  }
+  if (!combine || !L->has_shared) DMOE_CUDA(cudaMemsetAsync(out_sh, 0, (size_t)n_sh * H * 4, st));
+  if (out_rt != out_sh && rt_rows > 0) DMOE_CUDA(cudaMemsetAsync(out_rt, 0, (size_t)rt_rows * H * 4, st));
+  GemmParams dp = gp;
+  dp.tm_b = tm_h;
+  dp.ksplit = ks_dn;
+  dp.gu_acc = nullptr;
+  dp.out = out_sh;
+  dp.out_ld = H;
+  dp.out_routed = out_rt;
+  dp.y = combine ? L->ybuf : nullptr;
+  dp.y_ld = H;
+  dp.pair_tok = L->pair_tok;
+  dp.pair_w = L->pair_w;
+  std::memset(&dp.grp, 0, sizeof(dp.grp));
+  if (L->has_shared) {
+    dp.tm_w[0][0] = L->sdown.tm_q;
+    dp.tm_s[0][0] = L->sdown.tm_s;
+    fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H);
+  }
+  dp.tm_w[1][0] = L->down.tm_q;
+  dp.tm_s[1][0] = L->down.tm_s;
+  fill_group(dp.grp[1], L->down, L->etype, L->H, L->H);
+  if (same_type) {
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, dp, grid, st));
+    ++kernels;
+  } else {
+    GemmParams d0 = dp, d1 = dp;
+    d0.grp[1].present = 0;
+    d1.grp[0].present = 0;
+    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, d0, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, d1, grid, st));
+    kernels += 2;
+  }
+  if (combine) {
+    DMOE_CUDA(launch_combine(L->ybuf, H, n_sh, L->pair_row, (int)K, out_sh, H, L->has_shared ? 1 : 0, st));
+    ++kernels;
+  }
+  L->stats.token_tile = nt;
+  L->stats.ksplit_gateup = ks_gu;
+  L->stats.ksplit_down = ks_dn;
+  return DMOE_OK;
+}
+
+dmoe_status single_gpu_experts(dmoe_layer* L, cudaStream_t st, const float* xd, int64_t n, const int32_t* idx,
+                               const float* w, const int32_t* counts, float* od, uint32_t flags, int& kernels) {
+  const int64_t H = L->H, E = L->E, K = L->K;
+  const int64_t rows = n * (1 + K);  // shared segment [0, n) + routed pairs
+  const int64_t Imax = std::max(L->I, L->Is);
+  const bool prof = flags & DMOE_F_PROFILE;
+  const int nt = pick_nt(L, n);
+  int32_t* fill = L->ints + E;
+  int32_t* off = L->ints + 2 * E;
+  int32_t* n_tiles = L->ints + 3 * E;
+  int32_t* n_active = n_tiles + 1;
+  dmoe_status s;
+  // ---- dispatch: offsets, token tiles, gathered fp16 rows
+  if ((s = grow(L->tiles, L->tiles_cap, (size_t)(n * K / 32 + E + 2))) != DMOE_OK) return s;
+  if ((s = grow(L->xg, L->xg_cap, (size_t)rows * H)) != DMOE_OK) return s;
+  if ((s = grow(L->hbuf, L->hbuf_cap, (size_t)rows * Imax)) != DMOE_OK) return s;
+  if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows)) != DMOE_OK) return s;
+  if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
+  if ((s = grow(L->pair_row, L->pair_row_cap, (size_t)n * K)) != DMOE_OK) return s;
+  DMOE_CUDA(launch_scan_tiles(counts, (int)E, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
+  DMOE_CUDA(launch_gather(xd, n, (int)H, (int)K, idx, w, off, fill, L->xg, L->pair_tok, L->pair_w, L->pair_row,
+                          L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, L->has_shared ? 1 : 0, st));
+  kernels += 2;
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
+  const bool det = (flags & DMOE_F_DETERMINISTIC) || n >= env_int("DMOE_COMBINE_MIN", 1 << 30);
+  if ((s = run_experts(L, st, n, rows, nt, n_tiles, od, od, 0, det, prof, kernels)) != DMOE_OK) return s;
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));
+  DMOE_CUDA(cudaMemcpyAsync(L->host_counters, n_tiles, 8, cudaMemcpyDeviceToHost, st));
+  return DMOE_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// expert parallelism (NCCL over NVLink; one process per GPU)
+// ---------------------------------------------------------------------------------------------
+const char* nccl_err(ncclResult_t r) { return nccl().GetErrorString ? nccl().GetErrorString(r) : "?"; }
+
+void ep_abort(dmoe_layer* L) {
+  if (L->comm) nccl().CommAbort(L->comm);
+  L->comm = nullptr;
+  L->broken = true;
+}
+
+// Settles a call on the non-blocking communicator: polls its state until the call completed,
+// failed, or the layer's deadline passed (then the communicator is aborted).
+dmoe_status nccl_settle(dmoe_layer* L, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return DMOE_OK;
+  if (r != ncclInProgress) {
+    ep_abort(L);
+    return fail(DMOE_ERR_NCCL, "%s: %s", what, nccl_err(r));
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    ncclResult_t a = ncclInProgress;
+    nccl().CommGetAsyncError(L->comm, &a);
+    if (a == ncclSuccess) return DMOE_OK;
+    if (a != ncclInProgress) {
+      ep_abort(L);
+      return fail(DMOE_ERR_NCCL, "%s: %s", what, nccl_err(a));
+    }
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(L->timeout_ms)) {
+      ep_abort(L);
+      return fail(DMOE_ERR_TIMEOUT, "%s did not complete within %d ms; communicator aborted", what, L->timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+// Waits for `st` to drain while watching the communicator; the deadline aborts it.
+dmoe_status ep_wait(dmoe_layer* L, cudaStream_t st, const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    const cudaError_t q = cudaStreamQuery(st);
+    if (q == cudaSuccess) return DMOE_OK;
+    if (q != cudaErrorNotReady) return fail(DMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(q));
+    if (L->comm) {
+      ncclResult_t a = ncclSuccess;
+      nccl().CommGetAsyncError(L->comm, &a);
+      if (a != ncclSuccess && a != ncclInProgress) {
+        ep_abort(L);
+        return fail(DMOE_ERR_NCCL, "%s: %s", what, nccl_err(a));
+      }
+    }
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(L->timeout_ms)) {
+      ep_abort(L);
+      return fail(DMOE_ERR_TIMEOUT, "%s did not complete within %d ms; communicator aborted", what, L->timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+#define DMOE_NCCL(call, what)                                               \
+  do {                                                                      \
+    dmoe_status s_ = nccl_settle(L, (call), what);                          \
+    if (s_ != DMOE_OK) return s_;                                           \
+  } while (0)
+
+dmoe_status ep_experts(dmoe_layer* L, cudaStream_t st, const float* xd, int64_t n, const int32_t* idx,
+                       const float* w, float* od, uint32_t flags, int& kernels) {
+  const NcclApi& api = nccl();
+  const int W = L->world;
+  const int64_t H = L->H, K = L->K, El = L->e_local;
+  const int64_t Imax = std::max(L->I, L->Is);
+  const bool prof = flags & DMOE_F_PROFILE;
+  if (flags & DMOE_F_DETERMINISTIC)
+    return fail(DMOE_ERR_UNSUPPORTED, "DMOE_F_DETERMINISTIC is single-GPU only");
+  dmoe_status s;
+  if ((s = grow(L->ep_mask, L->ep_mask_cap, (size_t)n)) != DMOE_OK) return s;
+  if ((s = grow(L->ep_pos, L->ep_pos_cap, (size_t)W * n)) != DMOE_OK) return s;
+  if ((s = grow(L->ep_cnt, L->ep_cnt_cap, (size_t)2 * W)) != DMOE_OK) return s;
+  int32_t* cnt_send = L->ep_cnt;
+  int32_t* cnt_recv = L->ep_cnt + W;
+  // ---- plan and count exchange
+  DMOE_CUDA(launch_ep_plan(idx, n, (int)K, (int)El, W, L->ep_mask, L->ep_pos, cnt_send, st));
+  kernels += 2;
+  DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
+  for (int p = 0; p < W; ++p) {
+    DMOE_NCCL(api.Send(cnt_send + p, 1, ncclInt32, p, L->comm, st), "ncclSend(counts)");
+    DMOE_NCCL(api.Recv(cnt_recv + p, 1, ncclInt32, p, L->comm, st), "ncclRecv(counts)");
+  }
+  DMOE_NCCL(api.GroupEnd(), "count exchange");
+  DMOE_CUDA(cudaMemcpyAsync(L->ep_host, L->ep_cnt, sizeof(int32_t) * 2 * W, cudaMemcpyDeviceToHost, st));
+  if ((s = ep_wait(L, st, "count exchange")) != DMOE_OK) return s;
+  RankOffsets soff{}, roff{};
+  int64_t S = 0, R = 0;
+  for (int p = 0; p < W; ++p) {
+    soff.v[p] = (int32_t)S;
+    roff.v[p] = (int32_t)R;
+    S += L->ep_host[p];
+    R += L->ep_host[W + p];
+  }
+  const int64_t P = R * K;       // upper bound of the local (row, expert) pairs
+  const int64_t rows = n + P;    // gathered layout: shared rows [0, n), then pairs
+  if ((s = grow(L->ep_xs, L->ep_xs_cap, (size_t)std::max<int64_t>(S, 1) * H)) != DMOE_OK) return s;
+  if ((s = grow(L->ep_ms, L->ep_ms_cap, (size_t)std::max<int64_t>(S, 1) * 2 * K)) != DMOE_OK) return s;
+  if ((s = grow(L->ep_xr, L->ep_xr_cap, (size_t)std::max<int64_t>(R, 1) * H)) != DMOE_OK) return s;
+  if ((s = grow(L->ep_mr, L->ep_mr_cap, (size_t)std::max<int64_t>(R, 1) * 2 * K)) != DMOE_OK) return s;
+  if ((s = grow(L->ep_part, L->ep_part_cap, (size_t)std::max<int64_t>(R, 1) * H)) != DMOE_OK) return s;
+  if ((s = grow(L->ep_back, L->ep_back_cap, (size_t)std::max<int64_t>(S, 1) * H)) != DMOE_OK) return s;
+  // ---- dispatch: one fp16 row + slot list per (token, destination)
+  DMOE_CUDA(launch_ep_pack(xd, n, (int)H, (int)K, idx, w, (int)El, L->ep_mask, L->ep_pos, soff,
+                           L->etype == DMOE_TYPE_Q4_K, L->ep_xs, L->ep_ms, st));
+  ++kernels;
+  DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
+  for (int p = 0; p < W; ++p) {
+    const int64_t cs = L->ep_host[p], cr = L->ep_host[W + p];
+    if (cs) {
+      DMOE_NCCL(api.Send(L->ep_xs + (int64_t)soff.v[p] * H, (size_t)(cs * H), ncclFloat16, p, L->comm, st), "ncclSend(rows)");
+      DMOE_NCCL(api.Send(L->ep_ms + (int64_t)soff.v[p] * 2 * K, (size_t)(cs * 2 * K), ncclInt32, p, L->comm, st), "ncclSend(slots)");
+    }
+    if (cr) {
+      DMOE_NCCL(api.Recv(L->ep_xr + (int64_t)roff.v[p] * H, (size_t)(cr * H), ncclFloat16, p, L->comm, st), "ncclRecv(rows)");
+      DMOE_NCCL(api.Recv(L->ep_mr + (int64_t)roff.v[p] * 2 * K, (size_t)(cr * 2 * K), ncclInt32, p, L->comm, st), "ncclRecv(slots)");
+    }
+  }
+  DMOE_NCCL(api.GroupEnd(), "dispatch exchange");
+  // ---- local experts over the received rows
+  const int nt = pick_nt(L, n);
+  int32_t* counts = L->ints;  // [e_local] (the router's global counts are not needed any more)
+  int32_t* fill = L->ints + L->E;
+  int32_t* off = L->ints + 2 * L->E;
+  int32_t* n_tiles = L->ints + 3 * L->E;
+  int32_t* n_active = n_tiles + 1;
+  if ((s = grow(L->tiles, L->tiles_cap, (size_t)(P / 32 + El + 2))) != DMOE_OK) return s;
+  if ((s = grow(L->xg, L->xg_cap, (size_t)rows * H)) != DMOE_OK) return s;
+  if ((s = grow(L->hbuf, L->hbuf_cap, (size_t)rows * Imax)) != DMOE_OK) return s;
+  if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows)) != DMOE_OK) return s;
+  if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
+  DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)El, st));
+  DMOE_CUDA(launch_ep_count(L->ep_mr, R, (int)K, counts, st));
+  DMOE_CUDA(launch_scan_tiles(counts, (int)El, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
+  if (L->has_shared) {
+    DMOE_CUDA(launch_gather_shared(xd, n, (int)H, L->stype == DMOE_TYPE_Q4_K, L->xg, st));
+    ++kernels;
+  }
+  DMOE_CUDA(launch_gather_rows(L->ep_xr, R, (int)H, (int)K, L->ep_mr, off, fill, L->xg, L->pair_tok, L->pair_w, st));
+  kernels += 3;
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
+  if ((s = run_experts(L, st, n, rows, nt, n_tiles, od, L->ep_part, R, false, prof, kernels)) != DMOE_OK) return s;
+  // ---- combine: partial rows back to their owners, then the owner's sum
+  DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
+  for (int p = 0; p < W; ++p) {
+    const int64_t cs = L->ep_host[p], cr = L->ep_host[W + p];
+    if (cr) DMOE_NCCL(api.Send(L->ep_part + (int64_t)roff.v[p] * H, (size_t)(cr * H), ncclFloat32, p, L->comm, st), "ncclSend(partials)");
+    if (cs) DMOE_NCCL(api.Recv(L->ep_back + (int64_t)soff.v[p] * H, (size_t)(cs * H), ncclFloat32, p, L->comm, st), "ncclRecv(partials)");
+  }
+  DMOE_NCCL(api.GroupEnd(), "combine exchange");
+  DMOE_CUDA(launch_ep_final(od, L->ep_back, n, (int)H, L->ep_mask, L->ep_pos, soff, st));
+  ++kernels;
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));
+  DMOE_CUDA(cudaMemcpyAsync(L->host_counters, n_tiles, 8, cudaMemcpyDeviceToHost, st));
+  L->stats.ep_rows_sent = S;
+  L->stats.ep_rows_received = R;
+  return DMOE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -304,9 +665,15 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
   *out = nullptr;
   dmoe_status st = validate(d);
   if (st != DMOE_OK) return st;
-  if (dist && dist->world_size > 1)
-    return fail(DMOE_ERR_UNSUPPORTED, "expert parallelism (world_size %d) is not available in this build",
-                dist->world_size);
+  const int world = dist ? std::max(1, dist->world_size) : 1;
+  if (world > 1) {
+    if (world > kMaxRanks) return fail(DMOE_ERR_UNSUPPORTED, "world_size %d > %d", world, kMaxRanks);
+    if (dist->rank < 0 || dist->rank >= world) return fail(DMOE_ERR_INVALID_ARG, "rank %d of %d", dist->rank, world);
+    if (d->n_expert % world) return fail(DMOE_ERR_UNSUPPORTED, "n_expert %lld not divisible by world_size %d",
+                                         (long long)d->n_expert, world);
+    if (!dist->nccl_id) return fail(DMOE_ERR_INVALID_ARG, "expert parallelism needs dist->nccl_id");
+    if (!nccl().ok) return fail(DMOE_ERR_NCCL, "NCCL unavailable: %s", nccl().why);
+  }
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
     cudaGetLastError();
@@ -340,6 +707,10 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
   L->stype = d->shared_type;
   L->has_shared = d->n_ff_shexp > 0;
   L->has_bias = d->b_router != nullptr;
+  L->world = world;
+  L->rank = world > 1 ? dist->rank : 0;
+  L->e_local = L->E / world;
+  L->timeout_ms = (dist && dist->timeout_ms > 0) ? dist->timeout_ms : 60000;
   if (cudaStreamCreateWithFlags(&L->own_stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(fail(DMOE_ERR_CUDA, "stream create"));
   for (auto& e : L->ev)
@@ -358,9 +729,16 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
     if (cudaMemcpy(L->br, d->b_router, (size_t)L->E * 4, cudaMemcpyHostToDevice) != cudaSuccess)
       return bail(fail(DMOE_ERR_CUDA, "bias upload"));
   }
-  if ((st = upload_weight(L->gate, L->etype, d->w_gate, L->E * L->I, L->H)) != DMOE_OK) return bail(st);
-  if ((st = upload_weight(L->up, L->etype, d->w_up, L->E * L->I, L->H)) != DMOE_OK) return bail(st);
-  if ((st = upload_weight(L->down, L->etype, d->w_down, L->E * L->H, L->I)) != DMOE_OK) return bail(st);
+  {
+    // this rank's experts: a contiguous slice of each [E][rows][k] GGUF tensor
+    const int64_t e0 = (int64_t)L->rank * L->e_local;
+    const uint8_t* g = static_cast<const uint8_t*>(d->w_gate) + (size_t)e0 * L->I * row_size(L->etype, L->H);
+    const uint8_t* u = static_cast<const uint8_t*>(d->w_up) + (size_t)e0 * L->I * row_size(L->etype, L->H);
+    const uint8_t* dn = static_cast<const uint8_t*>(d->w_down) + (size_t)e0 * L->H * row_size(L->etype, L->I);
+    if ((st = upload_weight(L->gate, L->etype, g, L->e_local * L->I, L->H)) != DMOE_OK) return bail(st);
+    if ((st = upload_weight(L->up, L->etype, u, L->e_local * L->I, L->H)) != DMOE_OK) return bail(st);
+    if ((st = upload_weight(L->down, L->etype, dn, L->e_local * L->H, L->I)) != DMOE_OK) return bail(st);
+  }
   if (L->has_shared) {
     if ((st = upload_weight(L->sgate, L->stype, d->sw_gate, L->Is, L->H)) != DMOE_OK) return bail(st);
     if ((st = upload_weight(L->sup, L->stype, d->sw_up, L->Is, L->H)) != DMOE_OK) return bail(st);
@@ -370,13 +748,45 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
   if (cudaMemset(L->err, 0, 64) != cudaSuccess) return bail(fail(DMOE_ERR_CUDA, "err memset"));
   if (cudaMallocHost(&L->host_counters, 64) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "pinned alloc"));
   std::memset(L->host_counters, 0, 64);
+  if (world > 1) {
+    if (cudaMallocHost(&L->ep_host, sizeof(int32_t) * 2 * kMaxRanks) != cudaSuccess)
+      return bail(fail(DMOE_ERR_OOM, "pinned alloc"));
+    // non-blocking communicator: init and every group are polled against the layer's deadline
+    ncclUniqueId id;
+    std::memcpy(&id, dist->nccl_id, sizeof(id));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t r = nccl().CommInitRankConfig(&L->comm, world, id, L->rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+      L->comm = nullptr;
+      return bail(fail(DMOE_ERR_NCCL, "ncclCommInitRankConfig: %s", nccl().GetErrorString(r)));
+    }
+    if ((st = nccl_settle(L, r, "communicator init (all ranks must call dmoe_create)")) != DMOE_OK) return bail(st);
+  }
   *out = L;
+  return DMOE_OK;
+}
+
+dmoe_status dmoe_nccl_unique_id(void* id128) {
+  if (!id128) return fail(DMOE_ERR_INVALID_ARG, "null id buffer");
+  if (!nccl().ok) return fail(DMOE_ERR_NCCL, "NCCL unavailable: %s", nccl().why);
+  ncclUniqueId id;
+  const ncclResult_t r = nccl().GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(DMOE_ERR_NCCL, "ncclGetUniqueId: %s", nccl().GetErrorString(r));
+  std::memcpy(id128, &id, sizeof(id));
   return DMOE_OK;
 }
 
 void dmoe_destroy(dmoe_layer* L) {
   if (!L) return;
   cudaSetDevice(L->device);
+  if (L->comm) {
+    // drain this rank's work (bounded by the deadline), then release the communicator without
+    // waiting on the other ranks: destroy never blocks on a peer that is gone
+    ep_wait(L, L->last_stream, "destroy");
+    if (L->comm) nccl().CommAbort(L->comm);
+    L->comm = nullptr;
+  }
   if (L->own_stream) cudaStreamSynchronize(L->own_stream);
   cudaStreamSynchronize(L->last_stream);
   cudaFree(L->wr);
@@ -399,6 +809,10 @@ void dmoe_destroy(dmoe_layer* L) {
   cudaFree(L->xdev);
   cudaFree(L->odev);
   cudaFree(L->err);
+  for (void* p : {(void*)L->ep_mask, (void*)L->ep_pos, (void*)L->ep_cnt, (void*)L->ep_xs, (void*)L->ep_ms,
+                  (void*)L->ep_xr, (void*)L->ep_mr, (void*)L->ep_part, (void*)L->ep_back})
+    cudaFree(p);
+  if (L->ep_host) cudaFreeHost(L->ep_host);
   if (L->host_counters) cudaFreeHost(L->host_counters);
   for (auto& e : L->ev)
     if (e) cudaEventDestroy(e);
@@ -409,6 +823,7 @@ void dmoe_destroy(dmoe_layer* L) {
 dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, const dmoe_route_out* route,
                          void* stream, uint32_t flags) {
   if (!L) return fail(DMOE_ERR_INVALID_ARG, "null layer");
+  if (L->broken) return fail(DMOE_ERR_NCCL, "a collective of this layer failed earlier; re-create it on every rank");
   if (n < 0 || (n > 0 && !x)) return fail(DMOE_ERR_INVALID_ARG, "bad input");
   const bool route_only = flags & DMOE_F_ROUTE_ONLY;
   const bool host = flags & DMOE_F_HOST_PTRS;
@@ -426,14 +841,11 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if (n == 0) return DMOE_OK;
 
   const int64_t H = L->H, E = L->E, K = L->K;
-  const int64_t rows = n * (1 + K);  // shared segment [0, n) + routed pairs
-  const int64_t Imax = std::max(L->I, L->Is);
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;
   const int nseg = (int)((H + kRouterSeg - 1) / kRouterSeg);
   bool rl_split = router_split(n, (int)E, L->sms);  // too few whole-K tiles: split by segment
   if (const int f = env_int("DMOE_ROUTER_SPLIT", -1); f == 0 || f == 1) rl_split = f == 1;
   const int nparts = rl_split ? nseg : 1;
-  const int nt = pick_nt(L, n);
 
   dmoe_status s;
   size_t dummy_cap;
@@ -455,10 +867,6 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if ((s = grow(L->ints, L->ints_cap, (size_t)3 * E + 8)) != DMOE_OK) return s;
   if (use_block && (s = grow(L->allowed, L->allowed_cap, (size_t)(n / L->blk) * E)) != DMOE_OK) return s;
   int32_t* counts = L->ints;
-  int32_t* fill = L->ints + E;
-  int32_t* off = L->ints + 2 * E;
-  int32_t* n_tiles = L->ints + 3 * E;
-  int32_t* n_active = n_tiles + 1;
 
   const float* xd = x;
   float* od = out;
@@ -498,149 +906,9 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[1], st));
 
   if (!route_only) {
-    // ---- dispatch: offsets, token tiles, gathered fp16 rows
-    if ((s = grow(L->tiles, L->tiles_cap, (size_t)(n * K / 32 + E + 2))) != DMOE_OK) return s;
-    if ((s = grow(L->xg, L->xg_cap, (size_t)rows * H)) != DMOE_OK) return s;
-    if ((s = grow(L->hbuf, L->hbuf_cap, (size_t)rows * Imax)) != DMOE_OK) return s;
-    if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows)) != DMOE_OK) return s;
-    if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
-    if ((s = grow(L->pair_row, L->pair_row_cap, (size_t)n * K)) != DMOE_OK) return s;
-    DMOE_CUDA(launch_scan_tiles(counts, (int)E, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
-    DMOE_CUDA(launch_gather(xd, n, (int)H, (int)K, ra.idx, ra.w, off, fill, L->xg, L->pair_tok, L->pair_w, L->pair_row,
-                            L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, L->has_shared ? 1 : 0, st));
-    kernels += 2;
-    if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
-
-    // ---- gate/up GEMM (+ SwiGLU)
-    CUtensorMap tm_x, tm_h;
-    if ((s = make_map(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->xg, (uint64_t)H, (uint64_t)rows, (uint64_t)H * 2, 64,
-                      (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
-      return s;
-    if ((s = make_map(&tm_h, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->hbuf, (uint64_t)Imax, (uint64_t)rows,
-                      (uint64_t)Imax * 2, 64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
-      return s;
-    int64_t active_est = std::min<int64_t>(E, n * K);
-    if (use_block) active_est = std::min<int64_t>(active_est, L->cap * (n / L->blk));
-    const int64_t tt_est = active_est + (n * K) / nt;
-    const int64_t sh_tt = L->has_shared ? (n + nt - 1) / nt : 0;
-    const bool same_type = !L->has_shared || L->stype == L->etype;
-    const int gu_stage_r = gemm_stage_k(L->etype), gu_stage_s = gemm_stage_k(L->stype);
-    const int64_t gu_tiles = tt_est * (L->I / kMTile) + sh_tt * (L->Is / kMTile);
-    int ks_gu = pick_ksplit(gu_tiles, L->sms,
-                            {(int)(H / gu_stage_r), L->has_shared ? (int)(H / gu_stage_s) : (int)(H / gu_stage_r)});
-    if ((size_t)rows * 2 * Imax * 4 > (256ull << 20)) ks_gu = 1;
-    const int64_t dn_tiles = (tt_est + sh_tt) * (H / kMTile);
-    int ks_dn = pick_ksplit(dn_tiles, L->sms,
-                            {(int)(L->I / gu_stage_r), L->has_shared ? (int)(L->Is / gu_stage_s) : (int)(L->I / gu_stage_r)});
-    {
-      const int f_gu = env_int("DMOE_KSPLIT_GU", 0), f_dn = env_int("DMOE_KSPLIT_DN", 0);
-      auto divides = [&](int ks, int64_t k_r, int64_t k_s) {
-        return ks >= 1 && ks <= 8 && (ks & (ks - 1)) == 0 && k_r % ks == 0 && k_s % ks == 0;
-      };
-      const int64_t gr = H / gu_stage_r, gs = L->has_shared ? H / gu_stage_s : gr;
-      const int64_t dr = L->I / gu_stage_r, ds = L->has_shared ? L->Is / gu_stage_s : dr;
-      if (divides(f_gu, gr, gs) && (size_t)rows * 2 * Imax * 4 <= (256ull << 20)) ks_gu = f_gu;
-      if (divides(f_dn, dr, ds)) ks_dn = f_dn;
-    }
-    if (ks_gu > 1) {
-      if ((s = grow(L->gu, L->gu_cap, (size_t)rows * 2 * Imax)) != DMOE_OK) return s;
-      DMOE_CUDA(cudaMemsetAsync(L->gu, 0, (size_t)rows * 2 * Imax * 4, st));
-    }
-    GemmParams gp;
-    std::memset(&gp, 0, sizeof(gp));
-    gp.tm_b = tm_x;
-    gp.tiles = L->tiles;
-    gp.n_tiles = n_tiles;
-    gp.n_shared_tt = (int32_t)sh_tt;
-    gp.ksplit = ks_gu;
-    gp.n_tokens = n;
-    gp.hbuf = L->hbuf;
-    gp.h_ld = Imax;
-    gp.h_quad_swap = (L->stype == DMOE_TYPE_Q4_K ? 1 : 0) | (L->etype == DMOE_TYPE_Q4_K ? 2 : 0);
-    gp.gu_acc = ks_gu > 1 ? L->gu : nullptr;
-    gp.gu_half = Imax;
-    gp.err = L->err;
-    if (L->has_shared) {
-      gp.tm_w[0][0] = L->sgate.tm_q;
-      gp.tm_w[0][1] = L->sup.tm_q;
-      gp.tm_s[0][0] = L->sgate.tm_s;
-      gp.tm_s[0][1] = L->sup.tm_s;
-      fill_group(gp.grp[0], L->sgate, L->stype, L->Is, L->Is);
-    }
-    gp.tm_w[1][0] = L->gate.tm_q;
-    gp.tm_w[1][1] = L->up.tm_q;
-    gp.tm_s[1][0] = L->gate.tm_s;
-    gp.tm_s[1][1] = L->up.tm_s;
-    fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I);
-    const int grid = L->sms;
-    const int ndq = env_int("DMOE_NDQ", 2);  // dequant warpgroups per CTA (2, 3 or 4)
-    if (same_type) {
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, gp, grid, st));
-      ++kernels;
-    } else {
-      GemmParams g0 = gp, g1 = gp;
-      g0.grp[1].present = 0;
-      g1.grp[0].present = 0;
-      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, ndq, g0, grid, st));
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, g1, grid, st));
-      kernels += 2;
-    }
-    if (ks_gu > 1) {
-      DMOE_CUDA(launch_swiglu_finish(L->gu, Imax, rows, n, (int)L->Is, (int)L->I, L->hbuf, Imax,
-                                     L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, st));
-      ++kernels;
-    }
-    if (prof) DMOE_CUDA(cudaEventRecord(L->ev[3], st));
-
-    // ---- down GEMM (+ gate weights, slot sum, shared expert)
-    // Deterministic path (DMOE_F_DETERMINISTIC): routed rows are stored to y and summed per
-    // token in slot order by combine_kernel, the shared rows stored straight into out.
-    // Otherwise the epilogue reduces every row into a zeroed out with fp32 atomics (measured
-    // faster at every size: the y round trip costs more than the reductions).
-    const bool combine = ks_dn == 1 && ((flags & DMOE_F_DETERMINISTIC) || n >= env_int("DMOE_COMBINE_MIN", 1 << 30));
-    if (combine) {
-      if ((s = grow(L->ybuf, L->ybuf_cap, (size_t)n * K * H)) != DMOE_OK) return s;
-    }
-    if (!combine || !L->has_shared) DMOE_CUDA(cudaMemsetAsync(od, 0, (size_t)n * H * 4, st));
-    GemmParams dp = gp;
-    dp.tm_b = tm_h;
-    dp.ksplit = ks_dn;
-    dp.gu_acc = nullptr;
-    dp.out = od;
-    dp.out_ld = H;
-    dp.y = combine ? L->ybuf : nullptr;
-    dp.y_ld = H;
-    dp.pair_tok = L->pair_tok;
-    dp.pair_w = L->pair_w;
-    std::memset(&dp.grp, 0, sizeof(dp.grp));
-    if (L->has_shared) {
-      dp.tm_w[0][0] = L->sdown.tm_q;
-      dp.tm_s[0][0] = L->sdown.tm_s;
-      fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H);
-    }
-    dp.tm_w[1][0] = L->down.tm_q;
-    dp.tm_s[1][0] = L->down.tm_s;
-    fill_group(dp.grp[1], L->down, L->etype, L->H, L->H);
-    if (same_type) {
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, dp, grid, st));
-      ++kernels;
-    } else {
-      GemmParams d0 = dp, d1 = dp;
-      d0.grp[1].present = 0;
-      d1.grp[0].present = 0;
-      DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, d0, grid, st));
-      DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, d1, grid, st));
-      kernels += 2;
-    }
-    if (combine) {
-      DMOE_CUDA(launch_combine(L->ybuf, H, n, L->pair_row, (int)K, od, H, L->has_shared ? 1 : 0, st));
-      ++kernels;
-    }
-    if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));
-    L->stats.token_tile = nt;
-    L->stats.ksplit_gateup = ks_gu;
-    L->stats.ksplit_down = ks_dn;
-    DMOE_CUDA(cudaMemcpyAsync(L->host_counters, n_tiles, 8, cudaMemcpyDeviceToHost, st));
+    s = L->world == 1 ? single_gpu_experts(L, st, xd, n, ra.idx, ra.w, counts, od, flags, kernels)
+                      : ep_experts(L, st, xd, n, ra.idx, ra.w, od, flags, kernels);
+    if (s != DMOE_OK) return s;
   }
   L->stats.router_parts = nparts;
   L->stats.kernels = kernels;
@@ -663,7 +931,12 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
 dmoe_status dmoe_sync(dmoe_layer* L) {
   if (!L) return fail(DMOE_ERR_INVALID_ARG, "null layer");
   DMOE_CUDA(cudaSetDevice(L->device));
-  DMOE_CUDA(cudaStreamSynchronize(L->last_stream));
+  if (L->comm) {
+    dmoe_status s = ep_wait(L, L->last_stream, "forward");
+    if (s != DMOE_OK) return s;
+  } else {
+    DMOE_CUDA(cudaStreamSynchronize(L->last_stream));
+  }
   uint32_t e = 0;
   DMOE_CUDA(cudaMemcpy(&e, L->err, 4, cudaMemcpyDeviceToHost));
   L->stats.n_routed_tiles = L->host_counters[0];

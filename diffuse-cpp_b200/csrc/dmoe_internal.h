@@ -16,6 +16,13 @@ enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1 };
 
 constexpr int kRouterSeg = 256;  // canonical router segment length (fma chain per segment)
 constexpr int kMTile = 128;      // weight rows per MMA tile (tcgen05 M)
+constexpr int kMaxTopK = 16;     // n_expert_used limit
+constexpr int kMaxRanks = 32;    // expert-parallel world size limit (one mask bit per rank)
+
+// Per-rank row offsets, passed by value to the expert-parallel kernels.
+struct RankOffsets {
+  int32_t v[kMaxRanks];
+};
 
 // One token tile of one routed expert: rows [row0, row0 + nrows) of the gathered activation
 // buffer all belong to `expert`.
@@ -55,8 +62,9 @@ struct GemmParams {
   // down epilogue: with y == null every row is reduced into out (fp32 vector atomics);
   // otherwise shared rows store into out and routed row r stores w_r * (W_d h_r) into
   // y[r - n_tokens] for combine_kernel (deterministic slot-order sum)
-  float* out;
+  float* out;           // shared rows (group 0), token = row
   int64_t out_ld;
+  float* out_routed;    // routed rows (group 1) reduce into out_routed[pair_tok[r]] (atomic path)
   float* y;
   int64_t y_ld;
   const int32_t* pair_tok;
@@ -94,6 +102,19 @@ cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int
                           int32_t* pair_row, int swap_shared, int swap_routed, int with_shared, cudaStream_t st);
 cudaError_t launch_combine(const float* y, int64_t y_ld, int64_t n, const int32_t* pair_row, int top_k, float* out,
                            int64_t h, int add_out, cudaStream_t st);
+// expert parallelism (ep.cu)
+cudaError_t launch_ep_plan(const int32_t* idx, int64_t n, int top_k, int e_local, int world, uint32_t* mask,
+                           int32_t* pos, int32_t* cnt, cudaStream_t st);
+cudaError_t launch_ep_pack(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
+                           int e_local, const uint32_t* mask, const int32_t* pos, const RankOffsets& soff, int swap,
+                           __half* xs, int32_t* meta, cudaStream_t st);
+cudaError_t launch_ep_count(const int32_t* meta, int64_t rows, int top_k, int32_t* counts, cudaStream_t st);
+cudaError_t launch_gather_rows(const __half* xr, int64_t rows, int h, int top_k, const int32_t* meta,
+                               const int32_t* off, int32_t* fill, __half* xg, int32_t* pair_tok, float* pair_w,
+                               cudaStream_t st);
+cudaError_t launch_gather_shared(const float* x, int64_t n, int h, int swap, __half* xg, cudaStream_t st);
+cudaError_t launch_ep_final(float* out, const float* back, int64_t n, int h, const uint32_t* mask, const int32_t* pos,
+                            const RankOffsets& soff, cudaStream_t st);
 cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows, int64_t n, int is, int iw,
                                  __half* hbuf, int64_t h_ld, int swap_shared, int swap_routed, cudaStream_t st);
 cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st);

@@ -506,7 +506,8 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
               const int k = 16 * ch + c;
               const float wgt = __shfl_sync(0xffffffffu, wv[k >> 5], k & 31);
               const int tok = __shfl_sync(0xffffffffu, tv[k >> 5], k & 31);
-              if (c0 + c < ti.nrows) atomicAdd(p.out + (int64_t)tok * p.out_ld + obase + lane, __uint_as_float(acc0[c]) * wgt);
+              float* dst = ti.group == 0 ? p.out : p.out_routed;
+              if (c0 + c < ti.nrows) atomicAdd(dst + (int64_t)tok * p.out_ld + obase + lane, __uint_as_float(acc0[c]) * wgt);
             }
           }
         }

@@ -96,6 +96,8 @@ class Stats(ctypes.Structure):
         ("ms_gateup", ctypes.c_float),
         ("ms_down", ctypes.c_float),
         ("ms_total", ctypes.c_float),
+        ("ep_rows_sent", ctypes.c_int64),
+        ("ep_rows_received", ctypes.c_int64),
     ]
 
     def as_dict(self) -> dict:
@@ -141,8 +143,28 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.dmoe_route_static.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, P, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_int32, P, P, P]
     lib.dmoe_route_static.restype = ctypes.c_int
+    lib.dmoe_nccl_unique_id.argtypes = [P]
+    lib.dmoe_nccl_unique_id.restype = ctypes.c_int
     _lib = lib
     return lib
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id (dmoe_nccl_unique_id): make it on one rank, share it."""
+    buf = ctypes.create_string_buffer(128)
+    _check(load().dmoe_nccl_unique_id(buf))
+    return buf.raw
+
+
+def dist_cfg(rank: int, world_size: int, device: int, nccl_id: Optional[bytes] = None, timeout_ms: int = 0):
+    """dmoe_dist_cfg for one rank; the returned object keeps the id buffer alive."""
+    cfg = DistCfg(rank, world_size, device, timeout_ms, None)
+    if nccl_id is not None:
+        if len(nccl_id) != 128:
+            raise ValueError("nccl_id must be 128 bytes")
+        cfg._id = ctypes.create_string_buffer(nccl_id, 128)
+        cfg.nccl_id = ctypes.cast(cfg._id, ctypes.c_void_p)
+    return cfg
 
 
 def last_error() -> str:

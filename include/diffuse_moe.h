@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define DMOE_ABI_VERSION 1
+#define DMOE_ABI_VERSION 2
 
 /* Replaces the reference's bool returns + DIFFUSE_DIE/exit(1) (src/diffuse-common.h:22-27,
  * src/diffuse-moe-graph.cpp:325-329). */
@@ -33,7 +33,8 @@ typedef enum dmoe_status {
   DMOE_ERR_NO_DEVICE = 3,    /* no CUDA device (there is no CPU fallback) */
   DMOE_ERR_CUDA = 4,         /* CUDA runtime / driver error; see dmoe_last_error */
   DMOE_ERR_NCCL = 5,         /* expert-parallel communication error */
-  DMOE_ERR_TIMEOUT = 6,      /* a bounded device-side wait expired (kernel gave up, no hang) */
+  DMOE_ERR_TIMEOUT = 6,      /* a bounded wait expired: a device-side wait (the kernel gave up) or a
+                                collective past dmoe_dist_cfg.timeout_ms (communicator aborted) */
   DMOE_ERR_OOM = 7           /* device allocation failed */
 } dmoe_status;
 
@@ -81,8 +82,15 @@ typedef struct dmoe_layer_desc {
 } dmoe_layer_desc;
 
 /* Expert parallelism: one process per GPU; every rank calls dmoe_create and dmoe_forward
- * collectively with its own token shard. NULL (or world_size 1) = single GPU. Rank r owns
- * experts [r E / W, (r + 1) E / W); router and shared expert are replicated. */
+ * collectively with its own token shard (whole routing blocks). NULL (or world_size 1) = single
+ * GPU. Rank r owns experts [r E / W, (r + 1) E / W) (E % W == 0, W <= 32); router, bias and shared
+ * expert are replicated. Each forward routes locally, sends one fp16 row per (token, owning
+ * rank) with its slot list, computes the local experts' weighted partial rows, returns them to
+ * the token's rank and adds them to the shared expert's rows there (NCCL send / recv, loaded at
+ * run time from libnccl.so.2). Every collective wait has the host deadline timeout_ms; when it
+ * passes the call returns DMOE_ERR_TIMEOUT, the communicator is aborted and the layer refuses
+ * further forwards (destroy and re-create it on every rank). dmoe_create itself waits at most
+ * timeout_ms for all ranks to join. */
 typedef struct dmoe_dist_cfg {
   int32_t rank;
   int32_t world_size;
@@ -113,6 +121,8 @@ typedef struct dmoe_stats {
   float ms_gateup;
   float ms_down;
   float ms_total;
+  int64_t ep_rows_sent;     /* expert parallelism: (token, rank) rows sent / received */
+  int64_t ep_rows_received;
 } dmoe_stats;
 
 #define DMOE_F_HOST_PTRS 1u   /* x, out and route_out are host memory: the call copies them and
@@ -129,6 +139,10 @@ typedef struct dmoe_stats {
  * once (library-owned), prepares the TMA descriptors. Replaces the per-forward weight binding
  * and F32 casts of src/diffuse-moe-graph.cpp:8-12,203,282-284 (weights are never re-staged). */
 dmoe_status dmoe_create(const dmoe_layer_desc* desc, const dmoe_dist_cfg* dist, struct dmoe_layer** out);
+
+/* Writes a fresh 128-byte NCCL unique id for dmoe_dist_cfg.nccl_id (create it on one rank and
+ * share it with the others). No counterpart in the reference, which runs on one device. */
+dmoe_status dmoe_nccl_unique_id(void* id128);
 
 /* moe_out = MoE(x). Replaces src/diffuse-moe-graph.cpp:195-287 (router :203-262, experts
  * :264-278, shared expert :280-286). x and out are [n_tokens][n_embd] f32, row-major (ggml

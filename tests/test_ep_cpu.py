@@ -1,0 +1,114 @@
+"""Expert parallelism on CPU: the decomposition the library's EP path implements (ep.cu), run
+with real collectives (torch.distributed gloo, world size 2) around the oracle.
+
+Each rank routes its own whole token blocks, sends one row per (token, owning rank) with its
+slot list (rank-local expert id or -1, gate weight), computes the weighted partial rows of its
+own experts only (it is given only their weights), returns them, and the owner adds the
+partials in rank order to its shared-expert rows. The result must equal the single-process
+layer (oracle, double accumulation) on the same tokens, and routing needs no communication.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import diffuse_moe as dm
+import oracle
+import synth
+
+WORLD = 2
+
+
+def free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def spec():
+    return synth.LayerSpec(H=256, I=256, Is=256, E=8, top_k=3, cap=4, blk=32, expert_type=dm.TYPE_Q8_0, seed=21)
+
+
+def local_tensors(t, hp, rank, world):
+    """This rank's expert slice of each [E][rows][k] GGUF tensor (what dmoe_create uploads)."""
+    el = hp["n_expert"] // world
+    out = {}
+    for name, rows in (("w_gate", hp["n_ff_exp"]), ("w_up", hp["n_ff_exp"]), ("w_down", hp["n_embd"])):
+        a = np.asarray(t[name])
+        per = a.shape[0] // hp["n_expert"]
+        assert per == rows
+        out[name] = a[rank * el * per:(rank + 1) * el * per]
+    return out
+
+
+def exchange(objs_by_dest):
+    """all-to-all of python objects over gloo: returns the list received from each source."""
+    gathered = [None] * WORLD
+    dist.all_gather_object(gathered, objs_by_dest)
+    me = dist.get_rank()
+    return [gathered[src][me] for src in range(WORLD)]
+
+
+def worker(rank, port, ret):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        sp = spec()
+        hp = sp.hparams()
+        t = synth.make_layer(sp)
+        E, K, el = hp["n_expert"], hp["n_expert_used"], hp["n_expert"] // WORLD
+        x = synth.make_input(64, sp.H, 100 + rank)  # this rank's 2 blocks
+        # local routing (no communication)
+        lg = oracle.logits(x, t["w_router"])
+        idx, w, _, _, _ = oracle.route(lg, t["b_router"], K, hp["expert_capacity"], hp["moe_block_size"],
+                                       hp["norm_topk_prob"], hp["routed_scaling"])
+        # plan: one row per (token, owning rank), slot list with local ids (-1 elsewhere)
+        sends = [[] for _ in range(WORLD)]
+        for tok in range(x.shape[0]):
+            for d in sorted({int(e) // el for e in idx[tok]}):
+                slots = [(int(e) - d * el if int(e) // el == d else -1, float(w[tok, s])) for s, e in enumerate(idx[tok])]
+                sends[d].append((tok, x[tok], slots))
+        recv = exchange([[(x_row, slots) for _, x_row, slots in sends[d]] for d in range(WORLD)])
+        # partial rows with only this rank's experts
+        lt = local_tensors(t, hp, rank, WORLD)
+        hp_l = dict(hp, n_expert=el, n_ff_shexp=0)
+        parts = []
+        for src in range(WORLD):
+            rows = recv[src]
+            if not rows:
+                parts.append(np.zeros((0, sp.H), np.float32))
+                continue
+            xr = np.stack([r[0] for r in rows]).astype(np.float32)
+            li = np.array([[max(e, 0) for e, _ in r[1]] for r in rows], dtype=np.int32)
+            lw = np.array([[wv if e >= 0 else 0.0 for e, wv in r[1]] for r in rows], dtype=np.float32)
+            parts.append(oracle.experts(hp_l, lt, xr, li, lw, mode=0))
+        back = exchange(parts)
+        # owner: shared rows + partials in rank order
+        shared = oracle.experts(hp, t, x, np.zeros_like(idx), np.zeros_like(w), mode=0)
+        acc = np.zeros_like(shared)
+        for d in range(WORLD):
+            for j, (tok, _, _) in enumerate(sends[d]):
+                acc[tok] += back[d][j]
+        out = acc + shared
+        ref = oracle.layer(hp, t, x, mode=0)[0]
+        err = float(np.linalg.norm(out - ref) / np.linalg.norm(ref))
+        ret[rank] = err
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_expert_parallel_decomposition_gloo():
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    mp.start_processes(worker, args=(free_port(), ret), nprocs=WORLD, start_method="spawn")
+    assert sorted(ret.keys()) == list(range(WORLD))
+    for r in range(WORLD):
+        assert ret[r] < 1e-5, (r, ret[r])

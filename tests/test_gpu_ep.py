@@ -1,0 +1,117 @@
+"""Expert parallelism through the C ABI on 2 GPUs (one process per GPU, NCCL).
+
+Each rank binds its half of the experts, routes its own token blocks and runs dmoe_forward
+collectively. Its output rows must meet the oracle tolerance for its tokens, and its routing
+must stay bit-exact (routing is local). A rank that never joins must make the others' create
+return DMOE_ERR_TIMEOUT within the deadline instead of hanging. Skipped with fewer than 2 GPUs.
+NVLS is off for these child processes.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import diffuse_moe as dm
+import oracle
+import synth
+
+WORLD = 2
+
+
+def gpus() -> int:
+    import torch
+
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+needs2 = pytest.mark.skipif(gpus() < WORLD, reason="expert parallelism needs 2 GPUs")
+
+
+def layer_spec(kind: str) -> synth.LayerSpec:
+    if kind == "tiny":
+        return synth.LayerSpec(H=256, I=256, Is=256, E=16, top_k=4, cap=6, blk=32, expert_type=dm.TYPE_Q4_K, seed=31)
+    # S shape with q8_0 (c2-like), 256 experts over 2 ranks
+    return synth.LayerSpec(H=2048, I=512, Is=512, E=256, top_k=8, cap=48, blk=32, expert_type=dm.TYPE_Q8_0, seed=32)
+
+
+def worker(rank, kind, ntok, nccl_id, ret):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        sp = layer_spec(kind)
+        hp = sp.hparams()
+        t = synth.make_layer(sp)
+        x = synth.make_input(ntok, sp.H, 500 + rank)
+        cfg = dm.dist_cfg(rank, WORLD, rank, nccl_id, timeout_ms=60000)
+        L = dm.MoELayer(hp, t, dist=cfg)
+        out, (idx, w, allowed) = L.forward(x, route=True)
+        out2 = L.forward(x)  # a second call reuses the grown buffers and the communicator
+        st = L.stats()
+        L.close()
+        r_out, r_idx, r_w, r_allowed, used = oracle.layer(hp, t, x)
+        ok_route = bool(np.array_equal(idx, r_idx) and np.array_equal(w.view(np.uint32), r_w.view(np.uint32)))
+        err = float(np.linalg.norm(out.astype(np.float64) - r_out) / np.linalg.norm(r_out))
+        err2 = float(np.linalg.norm(out2.astype(np.float64) - r_out) / np.linalg.norm(r_out))
+        ret[rank] = (ok_route, err, err2, int(st["ep_rows_sent"]), int(st["ep_rows_received"]))
+    except Exception as e:  # reported to the parent
+        ret[rank] = ("error", repr(e))
+
+
+def run_world(kind, ntok):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    nccl_id = dm.nccl_unique_id()
+    procs = [ctx.Process(target=worker, args=(r, kind, ntok, nccl_id, ret)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(600)
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    return dict(ret)
+
+
+@pytest.mark.gpu
+@needs2
+@pytest.mark.parametrize("kind,ntok", [("tiny", 64), ("s_q8", 256)])
+def test_ep_two_ranks_match_oracle(kind, ntok):
+    ret = run_world(kind, ntok)
+    for r in range(WORLD):
+        v = ret[r]
+        assert v[0] != "error", v
+        ok_route, err, err2, sent, recvd = v
+        assert ok_route, f"rank {r}: routing differs from the oracle"
+        assert err <= 2e-3 and err2 <= 2e-3, (r, err, err2)
+        assert sent > 0 and recvd > 0
+
+
+def lonely_worker(nccl_id, ret):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import time
+
+    sp = layer_spec("tiny")
+    t = synth.make_layer(sp)
+    cfg = dm.dist_cfg(0, WORLD, 0, nccl_id, timeout_ms=3000)
+    t0 = time.time()
+    try:
+        dm.MoELayer(sp.hparams(), t, dist=cfg)
+        ret["status"] = 0
+    except dm.DmoeError as e:
+        ret["status"] = e.status
+        ret["msg"] = str(e)
+    ret["seconds"] = time.time() - t0
+
+
+@pytest.mark.gpu
+@needs2
+def test_ep_rank_that_never_joins_times_out():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    p = ctx.Process(target=lonely_worker, args=(dm.nccl_unique_id(), ret))  # rank 1 never starts
+    p.start()
+    p.join(120)
+    assert p.exitcode == 0
+    assert ret["status"] == 6, ret  # DMOE_ERR_TIMEOUT
+    assert ret["seconds"] < 30, ret
