@@ -9,8 +9,12 @@ the per-step activations exceed the 126 MB L2, so no extra flush is needed betwe
 
 One step = one dmoe_forward over the GPU's 8192 tokens. `value` is device-resident throughput
 (inputs already in HBM); `e2e` goes through the public C ABI with pinned host buffers (H2D of x,
-D2H of out inside the timed region). With N > 1 (torchrun), every rank runs its own token shard
-(weak scaling); the timing is the max over ranks.
+D2H of out inside the timed region). With N > 1 (torchrun) the layer is expert-parallel: rank r
+holds experts [256 r / N, 256 (r + 1) / N), routes its own 256 blocks and exchanges token rows and
+partial outputs with the other ranks over NCCL inside every step (weak scaling: 8192 tokens per
+GPU); the timing is the max over ranks. N > 1 also reports `c4`: the BASELINE c4 workload
+(16384 tokens in total, Zipf-skewed expert bias, expert-parallel over the N GPUs), as a strong-
+scaling measurement with per-rank expert loads.
 
 `--impl reference` times the reference's CPU algorithm on the host cores instead: the ggml CPU
 path cannot be built (its ggml submodule is empty), so this is the C restatement in oracle/
@@ -161,7 +165,9 @@ def main():
     cfg = {"workload": f"{args.config}: flash-shaped MoE layer H4096 E256 I1024 Is1024 top8 cap48 q4_K, "
                        f"{args.blocks} blocks x 32 tokens per GPU",
            "tokens_per_gpu": n_tok, "global_tokens": n_tok * args.gpus, "weights": "q4_K (synthetic F16 N(0,0.02))",
-           "l2": "working set > L2 (1.8 GB weights), no flush", "parallelism": f"token-sharded x{args.gpus}"}
+           "l2": "working set > L2 (1.8 GB weights), no flush",
+           "parallelism": "single GPU" if args.gpus == 1 else
+           f"expert-parallel x{args.gpus} ({256 // args.gpus} experts per GPU, NCCL dispatch/combine), token blocks sharded"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -191,8 +197,20 @@ def main():
     peaks = load_peaks()
     hp = spec.hparams()
     t = synth.make_layer(spec)
-    layer = dm.MoELayer(hp, t, dist=dm.DistCfg(0, 1, local_rank, 0, None))
     dev = torch.device("cuda", local_rank)
+    nccl_id = None
+    if world > 1:
+        # one NCCL unique id from rank 0 for the layer's own communicator
+        idt = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            idt.copy_(torch.frombuffer(bytearray(dm.nccl_unique_id()), dtype=torch.uint8).to(dev))
+        dist.broadcast(idt, 0)
+        nccl_id = bytes(idt.cpu().numpy().tobytes())
+
+    def make(sp, tt):
+        return dm.MoELayer(sp.hparams(), tt, dist=dm.dist_cfg(rank, world, local_rank, nccl_id, timeout_ms=120000))
+
+    layer = make(spec, t)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -280,6 +298,41 @@ def main():
     layer_roof = {"bytes": B, "flops": F, "hbm_gbs": B / (ms / 1e3) / 1e9, "tflops": F / (ms / 1e3) / 1e12,
                   "frac": t_roof / (ms / 1e3), "peak_source": peaks["source"]}
 
+    # ---- c4 (N > 1): 16384 tokens in total, Zipf-skewed bias, expert-parallel (strong scaling)
+    c4 = None
+    if world > 1:
+        layer.close()
+        del t
+        sp4 = synth.config("c4")
+        t4 = synth.make_layer(sp4)
+        nid = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            nid.copy_(torch.frombuffer(bytearray(dm.nccl_unique_id()), dtype=torch.uint8).to(dev))
+        dist.broadcast(nid, 0)
+        nccl_id = bytes(nid.cpu().numpy().tobytes())
+        layer = make(sp4, t4)
+        n4 = 16384 // world
+        x4 = torch.from_numpy(synth.make_input(n4, sp4.H, sp4.seed + 17 * rank)).to(dev)
+        o4 = torch.empty((n4, sp4.H), dtype=torch.float32, device=dev)
+        for _ in range(args.warmup):
+            layer.forward(x4, out=o4)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            layer.forward(x4, out=o4)
+        e1.record(stream)
+        barrier()
+        ms4 = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        layer.sync()
+        st4 = layer.stats()
+        loads = torch.tensor([float(st4["ep_rows_received"])], device=dev)
+        allv = [torch.zeros_like(loads) for _ in range(world)]
+        dist.all_gather(allv, loads)
+        c4 = {"tokens": 16384, "ms_per_step": ms4, "tokens_per_s": 16384 / (ms4 / 1e3),
+              "rows_received_per_rank": [int(v.item()) for v in allv], "scaling": "strong",
+              "bias": "0.5 log Zipf(1.1) over a random expert permutation"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, sample = run_cpu_reference(spec, t, n_tok)
@@ -294,6 +347,8 @@ def main():
                 "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": int(st["kernels"]) * args.steps,
                 "stages_ms": prof, "n_active": st["n_active"], "token_tile": st["token_tile"],
                 "ksplit": [st["ksplit_gateup"], st["ksplit_down"]], "sweep": sweep}
+        if c4 is not None:
+            line["c4"] = c4
         print(json.dumps(line))
     layer.close()
     if world > 1:
