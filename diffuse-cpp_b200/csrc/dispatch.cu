@@ -75,23 +75,22 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ x
                                                      __half* __restrict__ xg, int32_t* __restrict__ pair_tok,
                                                      float* __restrict__ pair_w, int32_t* __restrict__ pair_row,
                                                      int swap_shared, int swap_routed, int with_shared) {
-  __shared__ int64_t rows[17];
+  __shared__ int64_t rows[kMaxTopK + 1];
   const int64_t t = blockIdx.x;
   const int tid = threadIdx.x;
-  int nrows = 0;
-  if (tid == 0) {
-    if (with_shared) rows[nrows++] = t;
-    for (int s = 0; s < top_k; ++s) {
-      const int ee = idx[t * top_k + s];
-      const int64_t pos = off[ee] + atomicAdd(&fill[ee], 1);
-      pair_tok[pos] = (int32_t)t;
-      pair_w[pos] = w[t * top_k + s];
-      pair_row[t * top_k + s] = (int32_t)pos;
-      rows[nrows++] = pos;
-    }
+  const int r0 = with_shared ? 1 : 0;
+  if (tid == 0 && with_shared) rows[0] = t;
+  if (tid < top_k) {  // one lane per slot: the slots' atomics are in flight together
+    const int s = tid;
+    const int ee = idx[t * top_k + s];
+    const int64_t pos = off[ee] + atomicAdd(&fill[ee], 1);
+    pair_tok[pos] = (int32_t)t;
+    pair_w[pos] = w[t * top_k + s];
+    pair_row[t * top_k + s] = (int32_t)pos;
+    rows[r0 + s] = pos;
   }
   __syncthreads();
-  nrows = (with_shared ? 1 : 0) + top_k;
+  const int nrows = r0 + top_k;
   const float4* xr = reinterpret_cast<const float4*>(x + t * h);
   for (int q = tid; q < h / 4; q += blockDim.x) {
     const float4 v = xr[q];

@@ -85,6 +85,7 @@ struct RouteArgs {
   float* w;            // [n][top_k]
   uint8_t* allowed;    // [n / blk][e] or null
   int32_t* counts;     // [e] per-expert pair counts (atomics; zeroed by the caller)
+  int tok_split;       // CTAs per routing block (set by launch_route)
 };
 
 cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, bool split,

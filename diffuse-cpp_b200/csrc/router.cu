@@ -72,15 +72,19 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 //                  tiles cannot fill the GPU).
 // TM = 4 for large N (fewer shared-memory reads per fma), TM = 2 for small N (more CTAs).
 // ------------------------------------------------------------------------------------------
-constexpr int RL_EXP = 64, RL_KC = 32, RL_THREADS = 128, RL_STAGES = 3;
+constexpr int RL_EXP = 64, RL_KC = 32, RL_THREADS = 128;
 constexpr int RL_XP = RL_KC + 4;  // x tile row pitch (floats)
 
 template <int TM>
 constexpr int rl_tok() { return 16 * TM; }
 template <int TM>
 constexpr int rl_stage_floats() { return rl_tok<TM>() * RL_XP + RL_KC * RL_EXP; }
-template <int TM>
-constexpr int rl_smem() { return RL_STAGES * rl_stage_floats<TM>() * 4; }
+// ring depth: the split path prefetches its whole 256-k segment at once (one memory latency
+// instead of eight); the whole-K path keeps a 3-deep ring
+template <bool SPLIT>
+constexpr int rl_stages() { return SPLIT ? kRouterSeg / RL_KC : 3; }
+template <int TM, bool SPLIT>
+constexpr int rl_smem() { return rl_stages<SPLIT>() * rl_stage_floats<TM>() * 4; }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
@@ -108,6 +112,7 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
                                                                    int32_t* __restrict__ arrivals) {
   extern __shared__ __align__(16) float rl_smem_f[];
   constexpr int TT = rl_tok<TM>();
+  constexpr int RL_STAGES = rl_stages<SPLIT>();
   const uint32_t sm0 = smem_u32(rl_smem_f);
   const int tid = threadIdx.x;
   const int ty = tid >> 3, tx = tid & 7;
@@ -252,8 +257,11 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
 }
 
 // ------------------------------------------------------------------------------------------
-// Routing: one CTA of 1024 threads per block of `blk` tokens (32 tokens when block routing is
-// off), from p = sigmoid(logit); the block's p stays in shared memory for the gate weights.
+// Routing: `tok_split` CTAs of 1024 threads per block of `blk` tokens (32 tokens when block
+// routing is off), from p = sigmoid(logit). Every CTA of a block stages the block's p and derives
+// the block's capacity set (fold, threshold, mask: the same bits in each); CTA j then takes the
+// top-k of tokens [j tpb / tok_split, (j + 1) tpb / tok_split). Splitting spreads the per-token
+// work over more SMs when there are few blocks.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
@@ -274,15 +282,36 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
   int* cnt_s = eq_s + E;                           // [E] pairs per expert in this CTA
   __shared__ float thr_s;
   const int tid = threadIdx.x;
-  const int64_t t0 = (int64_t)blockIdx.x * tpb;
+  const int64_t blk_id = blockIdx.x / a.tok_split;
+  const int part = blockIdx.x % a.tok_split;
+  const int64_t t0 = blk_id * tpb;
   const int ntok = (int)min((int64_t)tpb, a.n - t0);
   const int cnt = ntok * E;
-  // p and sel = p + bias (:204-210)
-  const float* pg = a.probs + t0 * E;
-  for (int i = tid; i < cnt; i += RT_THREADS) {
-    const float pv = pg[i];
-    pp[i] = pv;
-    ss[i] = a.bias ? __fadd_rn(pv, a.bias[i % E]) : pv;
+  // p and sel = p + bias (:204-210); 16-byte loads, all issued before use
+  {
+    const float4* pg = reinterpret_cast<const float4*>(a.probs + t0 * E);
+    constexpr int PF = 4;
+    for (int base = 0; base < cnt / 4; base += PF * RT_THREADS) {
+      float4 v[PF], b[PF];
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        const int i4 = base + u * RT_THREADS + tid;
+        if (i4 < cnt / 4) {
+          v[u] = __ldcg(pg + i4);
+          b[u] = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias) + (4 * i4 % E) / 4) : make_float4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        const int i4 = base + u * RT_THREADS + tid;
+        if (i4 >= cnt / 4) continue;
+        reinterpret_cast<float4*>(pp)[i4] = v[u];
+        if (a.bias)
+          v[u] = make_float4(__fadd_rn(v[u].x, b[u].x), __fadd_rn(v[u].y, b[u].y), __fadd_rn(v[u].z, b[u].z),
+                             __fadd_rn(v[u].w, b[u].w));
+        reinterpret_cast<float4*>(ss)[i4] = v[u];
+      }
+    }
   }
   for (int ee = tid; ee < E; ee += RT_THREADS) {
     gt_s[ee] = 0;
@@ -331,7 +360,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
     for (int ee = tid; ee < E; ee += RT_THREADS) {
       const float dlt = __fsub_rn(bmax[ee], thr_m);
       const bool keep = dlt > 0.0f;
-      if (a.allowed) a.allowed[(int64_t)blockIdx.x * E + ee] = keep ? 1 : 0;
+      if (a.allowed && part == 0) a.allowed[blk_id * E + ee] = keep ? 1 : 0;
       addv[ee] = keep ? 0.0f : -1e30f;
     }
     __syncthreads();
@@ -343,7 +372,9 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
   // lanes' bests, and only the winning lane marks its candidate taken and rescans.
   const int warp = tid >> 5, lane = tid & 31;
   const int ncand = (E - lane + 31) / 32;  // this lane's candidates (<= 32)
-  for (int t = warp; t < ntok; t += RT_THREADS / 32) {
+  const int per = (tpb + a.tok_split - 1) / a.tok_split;
+  const int tb = part * per, te = min(ntok, tb + per);
+  for (int t = tb + warp; t < te; t += RT_THREADS / 32) {
     const float* st = ss + t * E;
     uint32_t taken = 0;
     float hv = 0.0f;
@@ -410,13 +441,15 @@ cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t
   const unsigned gy = (unsigned)((e + RL_EXP - 1) / RL_EXP);
   if (split) {
     dim3 grid((unsigned)((n + rl_tok<2>() - 1) / rl_tok<2>()), gy, (unsigned)nseg);
-    cudaFuncSetAttribute(router_logits_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, rl_smem<2>());
+    cudaFuncSetAttribute(router_logits_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         rl_smem<2, true>());
     if (!arrivals) return cudaErrorInvalidValue;
-    router_logits_kernel<2, true><<<grid, RL_THREADS, rl_smem<2>(), st>>>(x, wrt, part, n, h, e, arrivals);
+    router_logits_kernel<2, true><<<grid, RL_THREADS, rl_smem<2, true>(), st>>>(x, wrt, part, n, h, e, arrivals);
   } else {
     dim3 grid((unsigned)((n + rl_tok<4>() - 1) / rl_tok<4>()), gy, 1u);
-    cudaFuncSetAttribute(router_logits_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, rl_smem<4>());
-    router_logits_kernel<4, false><<<grid, RL_THREADS, rl_smem<4>(), st>>>(x, wrt, part, n, h, e, nullptr);
+    cudaFuncSetAttribute(router_logits_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         rl_smem<4, false>());
+    router_logits_kernel<4, false><<<grid, RL_THREADS, rl_smem<4, false>(), st>>>(x, wrt, part, n, h, e, nullptr);
   }
   return cudaGetLastError();
 }
@@ -431,12 +464,16 @@ int64_t router_arrivals(int64_t n, int e) { return ((n + rl_tok<2>() - 1) / rl_t
 
 size_t route_smem_bytes(int64_t tpb, int64_t e) { return sizeof(float) * (size_t)((2 * tpb + 5) * e); }
 
-cudaError_t launch_route(const RouteArgs& a, cudaStream_t st) {
+cudaError_t launch_route(const RouteArgs& a_in, cudaStream_t st) {
+  RouteArgs a = a_in;
   const int tpb = a.use_block ? a.blk : 32;
   const int64_t nblocks = (a.n + tpb - 1) / tpb;
+  if (a.e % 4) return cudaErrorInvalidValue;
+  // few blocks: 4 CTAs per block share its tokens' top-k (each repeats the block-level steps)
+  a.tok_split = nblocks < 64 ? 4 : 1;
   const size_t smem = route_smem_bytes(tpb, a.e);
   cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRouteSmemMax);
-  route_kernel<<<(unsigned)nblocks, RT_THREADS, smem, st>>>(a);
+  route_kernel<<<(unsigned)(nblocks * a.tok_split), RT_THREADS, smem, st>>>(a);
   return cudaGetLastError();
 }
 
