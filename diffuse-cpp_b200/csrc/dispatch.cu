@@ -13,6 +13,7 @@
 // combine_kernel     out[t] = ((y_0 + y_1) + ... + y_{k-1}) + shared[t], the slot sum and the
 //                    shared-expert add of src/diffuse-moe-graph.cpp:273-286 in that order
 #include "dmoe_internal.h"
+#include "sm100.cuh"
 
 namespace dmoe {
 
@@ -22,6 +23,8 @@ __global__ void __launch_bounds__(1024) scan_tiles_kernel(const int32_t* __restr
                                                           TokTile* __restrict__ tiles, int32_t* __restrict__ n_tiles,
                                                           int32_t* __restrict__ n_active) {
   __shared__ int32_t s_cnt[1024];
+  pdl_wait();
+  pdl_trigger();
   __shared__ int32_t s_tt[1024];
   const int tid = threadIdx.x;
   const int c = tid < e ? counts[tid] : 0;
@@ -74,8 +77,11 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ x
                                                      const int32_t* __restrict__ off, int32_t* __restrict__ fill,
                                                      __half* __restrict__ xg, int32_t* __restrict__ pair_tok,
                                                      float* __restrict__ pair_w, int32_t* __restrict__ pair_row,
-                                                     int swap_shared, int swap_routed, int with_shared) {
+                                                     int swap_shared, int swap_routed, int with_shared,
+                                                     float* __restrict__ zero_out) {
   __shared__ int64_t rows[kMaxTopK + 1];
+  pdl_wait();
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   const int tid = threadIdx.x;
   const int r0 = with_shared ? 1 : 0;
@@ -106,6 +112,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const float* __restrict__ x
       const bool swp = shared_row ? swap_shared : swap_routed;
       reinterpret_cast<uint2*>(xg + rows[r] * h)[q] = swp ? pk_swp : pk_nat;
     }
+    if (zero_out) reinterpret_cast<float4*>(zero_out + t * h)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -135,6 +142,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
                                                       const int32_t* __restrict__ pair_row, int top_k,
                                                       float* __restrict__ out, int64_t h, int add_out) {
   __shared__ int64_t rows[kMaxTopK];
+  pdl_wait();
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   if (threadIdx.x < top_k) rows[threadIdx.x] = (int64_t)(pair_row[t * top_k + threadIdx.x] - n) * y_ld;
   __syncthreads();
@@ -168,23 +177,21 @@ cudaError_t launch_combine(const float* y, int64_t y_ld, int64_t n, const int32_
                            int64_t h, int add_out, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   if (top_k < 1 || top_k > kMaxTopK || h % 4) return cudaErrorInvalidValue;
-  combine_kernel<<<(unsigned)n, 256, 0, st>>>(y, y_ld, n, pair_row, top_k, out, h, add_out);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, dim3((unsigned)n), dim3(256), 0, st, y, y_ld, n, pair_row, top_k, out, h, add_out);
 }
 
 cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, int32_t* off, int32_t* fill,
                               TokTile* tiles, int32_t* n_tiles, int32_t* n_active, cudaStream_t st) {
-  scan_tiles_kernel<<<1, 1024, 0, st>>>(counts, e, n, nt, off, fill, tiles, n_tiles, n_active);
-  return cudaGetLastError();
+  return launch_pdl(scan_tiles_kernel, dim3(1), dim3(1024), 0, st, counts, e, n, nt, off, fill, tiles, n_tiles, n_active);
 }
 
 cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
                           const int32_t* off, int32_t* fill, __half* xg, int32_t* pair_tok, float* pair_w,
-                          int32_t* pair_row, int swap_shared, int swap_routed, int with_shared, cudaStream_t st) {
+                          int32_t* pair_row, int swap_shared, int swap_routed, int with_shared, float* zero_out,
+                          cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  gather_kernel<<<(unsigned)n, 256, 0, st>>>(x, n, h, top_k, idx, w, off, fill, xg, pair_tok, pair_w, pair_row,
-                                             swap_shared, swap_routed, with_shared);
-  return cudaGetLastError();
+  return launch_pdl(gather_kernel, dim3((unsigned)n), dim3(256), 0, st, x, n, h, top_k, idx, w, off, fill, xg, pair_tok,
+                    pair_w, pair_row, swap_shared, swap_routed, with_shared, zero_out);
 }
 
 cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows, int64_t n, int is, int iw,

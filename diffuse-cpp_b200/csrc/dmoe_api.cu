@@ -164,6 +164,20 @@ dmoe_status grow(T*& p, size_t& cap, size_t need) {
 
 void dmoe::set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
+namespace {
+thread_local bool g_pdl_call = false;
+}
+
+void dmoe::set_pdl_for_call(bool on) {
+  static const bool allowed = [] {
+    const char* v = getenv("DMOE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  g_pdl_call = allowed && on;
+}
+
+bool dmoe::pdl_enabled() { return g_pdl_call; }
+
 struct dmoe_layer {
   // shapes / hyper-parameters
   int64_t H = 0, I = 0, Is = 0, E = 0, K = 0, cap = 0, blk = 0;
@@ -314,7 +328,8 @@ void fill_group(GemmGroup& g, const DevWeight& w, int32_t type, int64_t rows_per
 // indexes it), rt_rows of it zeroed here when it is not out_sh. combine = deterministic path
 // (single GPU only): routed rows stored to ybuf, then summed per token in slot order.
 dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t rows, int nt, int32_t* n_tiles,
-                        float* out_sh, float* out_rt, int64_t rt_rows, bool combine, bool prof, int& kernels) {
+                        float* out_sh, float* out_rt, int64_t rt_rows, bool combine, bool out_sh_zeroed, bool prof,
+                        int& kernels) {
   const int64_t H = L->H, K = L->K;
   const int64_t Imax = std::max(L->I, L->Is);
   const int64_t E_here = L->world > 1 ? L->e_local : L->E;
@@ -407,7 +422,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   if (combine) {
     if ((s = grow(L->ybuf, L->ybuf_cap, (size_t)pairs * H)) != DMOE_OK) return s;
   }
-  if (!combine || !L->has_shared) DMOE_CUDA(cudaMemsetAsync(out_sh, 0, (size_t)n_sh * H * 4, st));
+  if ((!combine || !L->has_shared) && !out_sh_zeroed) DMOE_CUDA(cudaMemsetAsync(out_sh, 0, (size_t)n_sh * H * 4, st));
   if (out_rt != out_sh && rt_rows > 0) DMOE_CUDA(cudaMemsetAsync(out_rt, 0, (size_t)rt_rows * H * 4, st));
   GemmParams dp = gp;
   dp.tm_b = tm_h;
@@ -470,12 +485,14 @@ dmoe_status single_gpu_experts(dmoe_layer* L, cudaStream_t st, const float* xd, 
   if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
   if ((s = grow(L->pair_row, L->pair_row_cap, (size_t)n * K)) != DMOE_OK) return s;
   DMOE_CUDA(launch_scan_tiles(counts, (int)E, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
+  const bool det = (flags & DMOE_F_DETERMINISTIC) || n >= env_int("DMOE_COMBINE_MIN", 1 << 30);
+  // the atomic path's output is zeroed by the gather kernel, row by row (no memset in the chain)
   DMOE_CUDA(launch_gather(xd, n, (int)H, (int)K, idx, w, off, fill, L->xg, L->pair_tok, L->pair_w, L->pair_row,
-                          L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, L->has_shared ? 1 : 0, st));
+                          L->stype == DMOE_TYPE_Q4_K, L->etype == DMOE_TYPE_Q4_K, L->has_shared ? 1 : 0,
+                          det ? nullptr : od, st));
   kernels += 2;
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
-  const bool det = (flags & DMOE_F_DETERMINISTIC) || n >= env_int("DMOE_COMBINE_MIN", 1 << 30);
-  if ((s = run_experts(L, st, n, rows, nt, n_tiles, od, od, 0, det, prof, kernels)) != DMOE_OK) return s;
+  if ((s = run_experts(L, st, n, rows, nt, n_tiles, od, od, 0, det, !det, prof, kernels)) != DMOE_OK) return s;
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));
   DMOE_CUDA(cudaMemcpyAsync(L->host_counters, n_tiles, 8, cudaMemcpyDeviceToHost, st));
   return DMOE_OK;
@@ -627,7 +644,7 @@ dmoe_status ep_experts(dmoe_layer* L, cudaStream_t st, const float* xd, int64_t 
   DMOE_CUDA(launch_gather_rows(L->ep_xr, R, (int)H, (int)K, L->ep_mr, off, fill, L->xg, L->pair_tok, L->pair_w, st));
   kernels += 3;
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
-  if ((s = run_experts(L, st, n, rows, nt, n_tiles, od, L->ep_part, R, false, prof, kernels)) != DMOE_OK) return s;
+  if ((s = run_experts(L, st, n, rows, nt, n_tiles, od, L->ep_part, R, false, false, prof, kernels)) != DMOE_OK) return s;
   // ---- combine: partial rows back to their owners, then the owner's sum
   DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
   for (int p = 0; p < W; ++p) {
@@ -837,6 +854,7 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if (host && !stream) st = L->own_stream;
   L->last_stream = st;
   L->profiled = prof;
+  set_pdl_for_call(n < 1024);
   std::memset(&L->stats, 0, sizeof(L->stats));
   if (n == 0) return DMOE_OK;
 
@@ -883,8 +901,7 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[0], st));
 
   // ---- router (src/diffuse-moe-graph.cpp:203-262)
-  DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)E, st));
-  DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, rl_split, L->arrivals, st));
+  DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, rl_split, L->arrivals, counts, st));
   ++kernels;
   RouteArgs ra{};
   ra.probs = L->parts;

@@ -306,6 +306,9 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  // everything above overlaps the previous kernel's tail; global memory only after this
+  pdl_wait();
+  pdl_trigger();
   const int total = tiles_total(p);
 
   auto stage_ptr = [&](int s) -> uint8_t* { return smem + s * C::STAGE_BYTES; };
@@ -581,8 +584,7 @@ static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t st) {
   auto kern = moe_gemm_kernel<WT, MODE, NT, NDQ>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, st, p);
 }
 
 // Launches with `ndq` dequant warpgroups when that configuration keeps NA >= NDQ, otherwise

@@ -121,6 +121,7 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
     return DMOE_ERR_CUDA;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  set_pdl_for_call(false);
   float* logits = scratch + kLogitsOff;
   float* wrt = scratch + kWrtOff;
   int32_t* counts = reinterpret_cast<int32_t*>(scratch + kCountsOff);
@@ -128,8 +129,7 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
   transpose_router_kernel<<<dim3((unsigned)((H + 31) / 32), (unsigned)((E + 31) / 32)), dim3(32, 8), 0, st>>>(
       w_router, wrt, E, H);
   e = cudaGetLastError();
-  if (e == cudaSuccess) e = cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)E, st);
-  if (e == cudaSuccess) e = launch_router(x, wrt, logits, n_tokens, H, E, false, nullptr, st);
+  if (e == cudaSuccess) e = launch_router(x, wrt, logits, n_tokens, H, E, false, nullptr, counts, st);
   if (e == cudaSuccess) {
     RouteArgs ra{};
     ra.probs = logits;

@@ -109,8 +109,13 @@ template <int TM, bool SPLIT>
 __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const float* __restrict__ x,
                                                                    const float* __restrict__ wrt,
                                                                    float* __restrict__ part, int64_t n, int h, int e,
-                                                                   int32_t* __restrict__ arrivals) {
+                                                                   int32_t* __restrict__ arrivals,
+                                                                   int32_t* __restrict__ zero_counts) {
   extern __shared__ __align__(16) float rl_smem_f[];
+  pdl_wait();
+  pdl_trigger();
+  if (zero_counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)  // route_kernel's counters
+    for (int i = threadIdx.x; i < e; i += RL_THREADS) zero_counts[i] = 0;
   constexpr int TT = rl_tok<TM>();
   constexpr int RL_STAGES = rl_stages<SPLIT>();
   const uint32_t sm0 = smem_u32(rl_smem_f);
@@ -271,6 +276,8 @@ constexpr int RT_THREADS = 1024;
 
 __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
   extern __shared__ float rsm[];
+  pdl_wait();
+  pdl_trigger();
   const int tpb = a.use_block ? a.blk : 32;  // tokens per CTA
   const int E = a.e;
   float* ss = rsm;                                 // [tpb][E] selection scores (masked in place)
@@ -435,7 +442,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
 // p = sigmoid(logit) into part[0] ([n][e]); the split path also uses part[1 .. h/256 - 1] for
 // partials and `arrivals` (router_arrivals(n, e) zeroed ints, left zeroed again).
 cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, bool split,
-                          int32_t* arrivals, cudaStream_t st) {
+                          int32_t* arrivals, int32_t* zero_counts, cudaStream_t st) {
   if (h % kRouterSeg) return cudaErrorInvalidValue;
   const int nseg = h / kRouterSeg;
   const unsigned gy = (unsigned)((e + RL_EXP - 1) / RL_EXP);
@@ -444,12 +451,14 @@ cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t
     cudaFuncSetAttribute(router_logits_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          rl_smem<2, true>());
     if (!arrivals) return cudaErrorInvalidValue;
-    router_logits_kernel<2, true><<<grid, RL_THREADS, rl_smem<2, true>(), st>>>(x, wrt, part, n, h, e, arrivals);
+    return launch_pdl(router_logits_kernel<2, true>, grid, dim3(RL_THREADS), rl_smem<2, true>(), st, x, wrt, part, n, h,
+                      e, arrivals, zero_counts);
   } else {
     dim3 grid((unsigned)((n + rl_tok<4>() - 1) / rl_tok<4>()), gy, 1u);
     cudaFuncSetAttribute(router_logits_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          rl_smem<4, false>());
-    router_logits_kernel<4, false><<<grid, RL_THREADS, rl_smem<4, false>(), st>>>(x, wrt, part, n, h, e, nullptr);
+    return launch_pdl(router_logits_kernel<4, false>, grid, dim3(RL_THREADS), rl_smem<4, false>(), st, x, wrt, part, n,
+                      h, e, (int32_t*)nullptr, zero_counts);
   }
   return cudaGetLastError();
 }
@@ -473,8 +482,7 @@ cudaError_t launch_route(const RouteArgs& a_in, cudaStream_t st) {
   a.tok_split = nblocks < 64 ? 4 : 1;
   const size_t smem = route_smem_bytes(tpb, a.e);
   cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRouteSmemMax);
-  route_kernel<<<(unsigned)(nblocks * a.tok_split), RT_THREADS, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(route_kernel, dim3((unsigned)(nblocks * a.tok_split)), dim3(RT_THREADS), smem, st, a);
 }
 
 }  // namespace dmoe

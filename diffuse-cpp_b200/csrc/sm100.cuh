@@ -244,6 +244,12 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// Programmatic dependent launch. pdl_wait: block until the preceding grid in the stream has
+// completed and its memory is visible (a no-op for a grid launched without the attribute).
+// pdl_trigger: let the next grid start launching (its CTAs then wait in their own pdl_wait).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 
