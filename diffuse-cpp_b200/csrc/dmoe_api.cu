@@ -285,8 +285,10 @@ int pick_nt(const dmoe_layer* L, int64_t n) {
   // count is at most the number of tokens that can reach it and is estimated as 3x the mean + 8
   const double avg = active > 0 ? (double)pairs / (double)active : 0.0;
   const double busiest = std::min((double)n * L->world, 3.0 * avg + 8.0);
+  // measured on B200 (c3): N = 64 tiles run at the full tensor rate (32 cycles per MMA) and keep
+  // double-buffered accumulators, so 128 only pays once the average expert has > 128 tokens
   if (busiest <= 32.0) return 32;
-  if (busiest <= 64.0) return 64;
+  if (avg <= 128.0) return 64;
   return 128;
 }
 
@@ -312,8 +314,11 @@ int pick_ksplit(int64_t tiles_est, int sms, std::initializer_list<int> kstages) 
   return best;
 }
 
-void fill_group(GemmGroup& g, const DevWeight& w, int32_t type, int64_t rows_per_exp, int64_t n_out_rows) {
-  g.n_mt = (int32_t)(n_out_rows / kMTile);
+// n_out_rows / rows_per_tile output tiles per expert (gate/up tiles cover 128 rows of each of the
+// two matrices, down tiles 256 rows of the one)
+void fill_group(GemmGroup& g, const DevWeight& w, int32_t type, int64_t rows_per_exp, int64_t n_out_rows,
+                int64_t rows_per_tile = kMTile) {
+  g.n_mt = (int32_t)(n_out_rows / rows_per_tile);
   g.k_stages = (int32_t)(w.k / gemm_stage_k(type));
   g.rows_per_exp = (int32_t)rows_per_exp;
   g.present = 1;
@@ -439,11 +444,11 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   if (L->has_shared) {
     dp.tm_w[0][0] = L->sdown.tm_q;
     dp.tm_s[0][0] = L->sdown.tm_s;
-    fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H);
+    fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt));
   }
   dp.tm_w[1][0] = L->down.tm_q;
   dp.tm_s[1][0] = L->down.tm_s;
-  fill_group(dp.grp[1], L->down, L->etype, L->H, L->H);
+  fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt));
   if (same_type) {
     DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, dp, grid, st));
     ++kernels;

@@ -122,6 +122,7 @@ cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows,
                                  __half* hbuf, int64_t h_ld, int swap_shared, int swap_routed, cudaStream_t st);
 cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st);
 int gemm_stage_k(int wtype);
+int gemm_out_rows(int mode, int nt);  // output rows per tile of one expert matrix
 
 // Launch with programmatic stream serialization: the kernel may start while its predecessor in
 // the stream finishes; every such kernel calls pdl_wait() before touching global memory.

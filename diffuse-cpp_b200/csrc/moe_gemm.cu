@@ -6,6 +6,7 @@
 //
 //   MODE_GATEUP: h[row][i] = silu(Wg_e[i] . x_row) * (Wu_e[i] . x_row)   -> fp16 hbuf
 //   MODE_DOWN:   out[tok][o] += w_row * (Wd_e[o] . h_row)                  -> fp32 out (red.add)
+//                (256 output rows per tile: two 128-row MMA tiles share one activation tile)
 //                or, for large N, y[row][o] = w_row * (Wd_e[o] . h_row) summed by combine_kernel
 //
 // "Swap-AB" orientation: weights are the MMA's M side (128 rows per tile), the tokens of one
@@ -34,7 +35,12 @@ namespace dmoe {
 template <int WT, int MODE, int NT, int NDQ_ = 2>
 struct GemmCfg {
   static constexpr bool QUANT = (WT != WT_F16);
-  static constexpr int MATS = (MODE == MODE_GATEUP) ? 2 : 1;
+  // two weight tiles share each activation (B) tile: gate and up, or (down, NT <= 64) two
+  // adjacent 128-row blocks of the down matrix, so B crosses L2 once per 256 output rows. At
+  // NT = 128 the down tile keeps one block: two 128-column accumulators would leave TMEM no room
+  // to double-buffer them, and the epilogue's overlap with the next tile is worth more there.
+  static constexpr int MATS = (MODE == MODE_GATEUP || NT <= 64) ? 2 : 1;
+  static constexpr int OUT_ROWS = (MODE == MODE_GATEUP) ? kMTile : MATS * kMTile;  // output rows per tile
   static constexpr int STAGE_K = (WT == WT_Q4_K) ? 256 : 128;
   static constexpr int KB_PER_STAGE = STAGE_K / 128;
   static constexpr int B_BYTES = STAGE_K * NT * 2;
@@ -298,7 +304,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     for (int g = 0; g < 2; ++g) {
       if (!p.grp[g].present) continue;
       tma_prefetch_desc(&p.tm_w[g][0]);
-      if (C::MATS > 1) tma_prefetch_desc(&p.tm_w[g][1]);
+      if (MODE == MODE_GATEUP) tma_prefetch_desc(&p.tm_w[g][1]);
     }
     tma_prefetch_desc(&p.tm_b);
   }
@@ -321,7 +327,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     uint32_t stage_seq = 0;
     for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
       const TileInfo ti = decode_tile<NT>(p, t);
-      const int wrow = ti.expert * p.grp[ti.group].rows_per_exp + ti.mt * kMTile;
+      const int wrow = ti.expert * p.grp[ti.group].rows_per_exp + ti.mt * C::OUT_ROWS;
       bool ok = true;
       for (int kc = ti.k0; kc < ti.k1; ++kc) {
         const int s = stage_seq % C::STAGES;
@@ -335,14 +341,17 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
 #pragma unroll
           for (int m = 0; m < C::MATS; ++m) {
             uint8_t* wt = wtile_ptr(s, m);
+            // gate/up: matrix m at the tile's rows; down: the one matrix, row block m
+            const int mi = MODE == MODE_GATEUP ? m : 0;
+            const int wr = MODE == MODE_GATEUP ? wrow : wrow + m * kMTile;
             if constexpr (WT == WT_Q4_K) {
-              tma_load_2d_hint(wt, &p.tm_w[ti.group][m], kc * 144, wrow, &full[s], pol_w);
+              tma_load_2d_hint(wt, &p.tm_w[ti.group][mi], kc * 144, wr, &full[s], pol_w);
             } else if constexpr (WT == WT_Q8_0) {
-              tma_load_2d_hint(wt, &p.tm_w[ti.group][m], kc * 128, wrow, &full[s], pol_w);
-              tma_load_2d_hint(wt + 128 * 128, &p.tm_s[ti.group][m], kc * 4, wrow, &full[s], pol_w);
+              tma_load_2d_hint(wt, &p.tm_w[ti.group][mi], kc * 128, wr, &full[s], pol_w);
+              tma_load_2d_hint(wt + 128 * 128, &p.tm_s[ti.group][mi], kc * 4, wr, &full[s], pol_w);
             } else {
-              tma_load_2d_hint(wt, &p.tm_w[ti.group][m], kc * 128, wrow, &full[s], pol_w);
-              tma_load_2d_hint(wt + 128 * 128, &p.tm_w[ti.group][m], kc * 128 + 64, wrow, &full[s], pol_w);
+              tma_load_2d_hint(wt, &p.tm_w[ti.group][mi], kc * 128, wr, &full[s], pol_w);
+              tma_load_2d_hint(wt + 128 * 128, &p.tm_w[ti.group][mi], kc * 128 + 64, wr, &full[s], pol_w);
             }
           }
         }
@@ -454,14 +463,14 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
       if (!role_wait(&accfull[ab], aph, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
       tc_fence_after();
       const uint32_t dbase = tbase + lane_off + ab * C::ACC_COLS;
-      const int obase = ti.mt * kMTile + quarter * 32;  // first output feature of this warp
+      const int obase = ti.mt * C::OUT_ROWS + quarter * 32;  // first output feature of this warp
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         const int c0 = cb + 16 * ch;
         if (c0 >= ti.nrows) break;  // warp-uniform
-        uint32_t acc0[16];
-        tmem_ld16(dbase + c0, acc0);
         if constexpr (MODE == MODE_GATEUP) {
+          uint32_t acc0[16];
+          tmem_ld16(dbase + c0, acc0);
           uint32_t acc1[16];
           tmem_ld16(dbase + NT + c0, acc1);
           tmem_wait_ld();
@@ -485,16 +494,21 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
               }
           }
         } else {
+#pragma unroll 1
+         for (int m = 0; m < C::MATS; ++m) {  // row block m: accumulator columns [m NT, (m + 1) NT)
+          uint32_t acc0[16];
+          tmem_ld16(dbase + m * NT + c0, acc0);
+          const int ob = obase + m * kMTile;
           tmem_wait_ld();
           if (p.y != nullptr) {
             // shared rows into out, routed rows weighted into y
             if (ti.group == 0) {
-              float* ocol = p.out + (int64_t)(ti.row0 + c0) * p.out_ld + obase + lane;
+              float* ocol = p.out + (int64_t)(ti.row0 + c0) * p.out_ld + ob + lane;
 #pragma unroll
               for (int c = 0; c < 16; ++c)
                 if (c0 + c < ti.nrows) ocol[(int64_t)c * p.out_ld] = __uint_as_float(acc0[c]);
             } else {
-              float* ycol = p.y + (int64_t)(ti.row0 + c0 - p.n_tokens) * p.y_ld + obase + lane;
+              float* ycol = p.y + (int64_t)(ti.row0 + c0 - p.n_tokens) * p.y_ld + ob + lane;
 #pragma unroll
               for (int c = 0; c < 16; ++c) {
                 const int k = 16 * ch + c;
@@ -510,9 +524,10 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
               const float wgt = __shfl_sync(0xffffffffu, wv[k >> 5], k & 31);
               const int tok = __shfl_sync(0xffffffffu, tv[k >> 5], k & 31);
               float* dst = ti.group == 0 ? p.out : p.out_routed;
-              if (c0 + c < ti.nrows) atomicAdd(dst + (int64_t)tok * p.out_ld + obase + lane, __uint_as_float(acc0[c]) * wgt);
+              if (c0 + c < ti.nrows) atomicAdd(dst + (int64_t)tok * p.out_ld + ob + lane, __uint_as_float(acc0[c]) * wgt);
             }
           }
+         }
         }
       }
       tc_fence_before();
@@ -632,5 +647,7 @@ cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmPara
 }
 
 int gemm_stage_k(int wtype) { return wtype == WT_Q4_K ? 256 : 128; }
+
+int gemm_out_rows(int mode, int nt) { return mode == MODE_GATEUP ? kMTile : (nt <= 64 ? 2 * kMTile : kMTile); }
 
 }  // namespace dmoe

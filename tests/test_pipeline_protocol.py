@@ -21,14 +21,13 @@ GATEUP, DOWN = 0, 1
 def gemm_cfg(wt, mode, nt, ndq):
     """Restates GemmCfg<WT, MODE, NT, NDQ> (stage ring, TMEM ring) from moe_gemm.cu."""
     quant = wt != F16
-    mats = 2 if mode == GATEUP else 1
+    mats = 2 if (mode == GATEUP or nt <= 64) else 1  # down at NT <= 64: two 128-row blocks
     stage_k = 256 if wt == Q4_K else 128
     kb = stage_k // 128
     b_bytes = stage_k * nt * 2
     w_bytes = 128 * 144 if wt == Q4_K else (128 * 128 + 128 * 16 if wt == Q8_0 else 128 * 128 * 2)
     stage_bytes = b_bytes + mats * w_bytes
-    epi_bytes = ((4 * 16 * 33 * 4 + 1023) // 1024) * 1024
-    stages = min(6, (227 * 1024 - 2048 - epi_bytes) // stage_bytes)
+    stages = min(6, (227 * 1024 - 2048) // stage_bytes)
     acc_cols = mats * nt
     a_cols = mats * 64
     acc_bufs = 2 if 2 * acc_cols + (2 * a_cols if quant else 0) <= 512 else 1
