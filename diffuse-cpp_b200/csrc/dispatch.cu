@@ -21,7 +21,8 @@ namespace dmoe {
 __global__ void __launch_bounds__(1024) scan_tiles_kernel(const int32_t* __restrict__ counts, int e, int64_t n, int nt,
                                                           int32_t* __restrict__ off, int32_t* __restrict__ fill,
                                                           TokTile* __restrict__ tiles, int32_t* __restrict__ n_tiles,
-                                                          int32_t* __restrict__ n_active) {
+                                                          int32_t* __restrict__ n_active, int32_t* __restrict__ tt_done,
+                                                          int n_sh_tt) {
   __shared__ int32_t s_cnt[1024];
   pdl_wait();
   pdl_trigger();
@@ -58,6 +59,8 @@ __global__ void __launch_bounds__(1024) scan_tiles_kernel(const int32_t* __restr
   if (tid == 1023) {
     *n_tiles = s_tt[1023];
   }
+  if (tt_done)  // the fused GEMM's per-token-tile completion counters
+    for (int i = tid; i < n_sh_tt + s_tt[1023]; i += 1024) tt_done[i] = 0;
   // active expert count (experts with at least one pair)
   __syncthreads();
   s_cnt[tid] = (tid < e && c > 0) ? 1 : 0;
@@ -181,8 +184,10 @@ cudaError_t launch_combine(const float* y, int64_t y_ld, int64_t n, const int32_
 }
 
 cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, int32_t* off, int32_t* fill,
-                              TokTile* tiles, int32_t* n_tiles, int32_t* n_active, cudaStream_t st) {
-  return launch_pdl(scan_tiles_kernel, dim3(1), dim3(1024), 0, st, counts, e, n, nt, off, fill, tiles, n_tiles, n_active);
+                              TokTile* tiles, int32_t* n_tiles, int32_t* n_active, int32_t* tt_done, int n_sh_tt,
+                              cudaStream_t st) {
+  return launch_pdl(scan_tiles_kernel, dim3(1), dim3(1024), 0, st, counts, e, n, nt, off, fill, tiles, n_tiles, n_active,
+                    tt_done, n_sh_tt);
 }
 
 cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,

@@ -206,6 +206,7 @@ struct dmoe_layer {
   float* pair_w = nullptr; size_t pair_w_cap = 0;
   int32_t* pair_row = nullptr; size_t pair_row_cap = 0;
   float* ybuf = nullptr; size_t ybuf_cap = 0;
+  int32_t* tt_done = nullptr; size_t tt_done_cap = 0;  // fused GEMM: per token tile completion counters
   float* xdev = nullptr; size_t xdev_cap = 0;
   float* odev = nullptr; size_t odev_cap = 0;
   uint32_t* err = nullptr;
@@ -399,8 +400,20 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   gp.tm_s[1][1] = L->up.tm_s;
   fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I);
   const int grid = L->sms;
-  const int ndq = env_int("DMOE_NDQ", 2);  // dequant warpgroups per CTA (2, 3 or 4)
-  if (same_type) {
+  // dequant warpgroups per CTA: the largest of 4 / 3 / 2 the TMEM ring allows (measured 2-3 %
+  // faster than 2 at 1-8 blocks)
+  const int ndq = env_int("DMOE_NDQ", 4);
+  // One launch for both GEMMs at small N (the persistent kernel runs all gate/up tiles, then the
+  // down tiles, each as soon as its token tile's h rows are written): saves a launch, its ramp
+  // and its tail imbalance. Measured on B200 (c3): 1 block 107 -> 95 us for the two GEMMs, even
+  // at 8 blocks, 70 us slower at 64 blocks; so only up to 128 tokens (DMOE_FUSED=0/1 overrides).
+  const int f_env = env_int("DMOE_FUSED", -1);
+  const bool fused = same_type && ks_gu == 1 && ks_dn == 1 && nt <= 64 &&
+                     (f_env == 1 || (f_env != 0 && n_sh <= 128));
+  gp.tt_done = L->tt_done;
+  if (fused) {
+    // launched below, once the down operands are set
+  } else if (same_type) {
     DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, gp, grid, st));
     ++kernels;
   } else {
@@ -449,7 +462,25 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   dp.tm_w[1][0] = L->down.tm_q;
   dp.tm_s[1][0] = L->down.tm_s;
   fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt));
-  if (same_type) {
+  if (fused) {
+    GemmParams fp = gp;  // gate/up operands and tiles ...
+    fp.tm_b_dn = dp.tm_b;  // ... then the down phase's
+    fp.tm_w_dn[0] = dp.tm_w[0][0];
+    fp.tm_w_dn[1] = dp.tm_w[1][0];
+    fp.tm_s_dn[0] = dp.tm_s[0][0];
+    fp.tm_s_dn[1] = dp.tm_s[1][0];
+    fp.grp_dn[0] = dp.grp[0];
+    fp.grp_dn[1] = dp.grp[1];
+    fp.out = dp.out;
+    fp.out_ld = dp.out_ld;
+    fp.out_routed = dp.out_routed;
+    fp.y = dp.y;
+    fp.y_ld = dp.y_ld;
+    fp.pair_tok = dp.pair_tok;
+    fp.pair_w = dp.pair_w;
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_FUSED, nt, ndq, fp, grid, st));
+    ++kernels;
+  } else if (same_type) {
     DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, dp, grid, st));
     ++kernels;
   } else {
@@ -467,6 +498,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   L->stats.token_tile = nt;
   L->stats.ksplit_gateup = ks_gu;
   L->stats.ksplit_down = ks_dn;
+  L->stats.fused_gemm = fused ? 1 : 0;
   return DMOE_OK;
 }
 
@@ -489,7 +521,9 @@ dmoe_status single_gpu_experts(dmoe_layer* L, cudaStream_t st, const float* xd, 
   if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows)) != DMOE_OK) return s;
   if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
   if ((s = grow(L->pair_row, L->pair_row_cap, (size_t)n * K)) != DMOE_OK) return s;
-  DMOE_CUDA(launch_scan_tiles(counts, (int)E, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
+  if ((s = grow(L->tt_done, L->tt_done_cap, (size_t)(n * K / 32 + E + 2 + (n + 31) / 32))) != DMOE_OK) return s;
+  DMOE_CUDA(launch_scan_tiles(counts, (int)E, n, nt, off, fill, L->tiles, n_tiles, n_active, L->tt_done,
+                              L->has_shared ? (int)((n + nt - 1) / nt) : 0, st));
   const bool det = (flags & DMOE_F_DETERMINISTIC) || n >= env_int("DMOE_COMBINE_MIN", 1 << 30);
   // the atomic path's output is zeroed by the gather kernel, row by row (no memset in the chain)
   DMOE_CUDA(launch_gather(xd, n, (int)H, (int)K, idx, w, off, fill, L->xg, L->pair_tok, L->pair_w, L->pair_row,
@@ -641,7 +675,9 @@ dmoe_status ep_experts(dmoe_layer* L, cudaStream_t st, const float* xd, int64_t 
   if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
   DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)El, st));
   DMOE_CUDA(launch_ep_count(L->ep_mr, R, (int)K, counts, st));
-  DMOE_CUDA(launch_scan_tiles(counts, (int)El, n, nt, off, fill, L->tiles, n_tiles, n_active, st));
+  if ((s = grow(L->tt_done, L->tt_done_cap, (size_t)(P / 32 + El + 2 + (n + 31) / 32))) != DMOE_OK) return s;
+  DMOE_CUDA(launch_scan_tiles(counts, (int)El, n, nt, off, fill, L->tiles, n_tiles, n_active, L->tt_done,
+                              L->has_shared ? (int)((n + nt - 1) / nt) : 0, st));
   if (L->has_shared) {
     DMOE_CUDA(launch_gather_shared(xd, n, (int)H, L->stype == DMOE_TYPE_Q4_K, L->xg, st));
     ++kernels;
@@ -828,6 +864,7 @@ void dmoe_destroy(dmoe_layer* L) {
   cudaFree(L->pair_w);
   cudaFree(L->pair_row);
   cudaFree(L->ybuf);
+  cudaFree(L->tt_done);
   cudaFree(L->xdev);
   cudaFree(L->odev);
   cudaFree(L->err);

@@ -13,7 +13,8 @@ namespace dmoe {
 enum WType : int { WT_F32 = 0, WT_F16 = 1, WT_Q8_0 = 8, WT_Q4_K = 12 };
 
 // The GEMM kernel's two epilogues.
-enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1 };
+// MODE_FUSED: one launch runs every gate/up tile, then every down tile (token tiles <= 64).
+enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_FUSED = 2 };
 
 constexpr int kRouterSeg = 256;  // canonical router segment length (fma chain per segment)
 constexpr int kMTile = 128;      // weight rows per MMA tile (tcgen05 M)
@@ -70,6 +71,14 @@ struct GemmParams {
   int64_t y_ld;
   const int32_t* pair_tok;
   const float* pair_w;
+  // fused launch: the down phase's operands (tiles numbered after all gate/up tiles) and, per
+  // token tile (shared tiles first, then routed), the gate/up epilogue warps that have written
+  // its h rows; a down tile starts once all of them have (zeroed by scan_tiles_kernel)
+  CUtensorMap tm_w_dn[2];  // [group] down weight (quant / f16)
+  CUtensorMap tm_s_dn[2];  // [group] q8_0 scales
+  CUtensorMap tm_b_dn;     // fp16 h rows
+  GemmGroup grp_dn[2];
+  int32_t* tt_done;
   uint32_t* err;
 };
 
@@ -98,7 +107,8 @@ constexpr size_t kRouteSmemMax = 200 * 1024;
 size_t route_smem_bytes(int64_t tpb, int64_t e);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
 cudaError_t launch_scan_tiles(const int32_t* counts, int e, int64_t n, int nt, int32_t* off, int32_t* fill,
-                              TokTile* tiles, int32_t* n_tiles, int32_t* n_active, cudaStream_t st);
+                              TokTile* tiles, int32_t* n_tiles, int32_t* n_active, int32_t* tt_done, int n_sh_tt,
+                              cudaStream_t st);
 cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
                           const int32_t* off, int32_t* fill, __half* xg, int32_t* pair_tok, float* pair_w,
                           int32_t* pair_row, int swap_shared, int swap_routed, int with_shared, float* zero_out,

@@ -35,12 +35,15 @@ namespace dmoe {
 template <int WT, int MODE, int NT, int NDQ_ = 2>
 struct GemmCfg {
   static constexpr bool QUANT = (WT != WT_F16);
+  static constexpr bool FUSED = MODE == MODE_FUSED;
   // two weight tiles share each activation (B) tile: gate and up, or (down, NT <= 64) two
   // adjacent 128-row blocks of the down matrix, so B crosses L2 once per 256 output rows. At
   // NT = 128 the down tile keeps one block: two 128-column accumulators would leave TMEM no room
   // to double-buffer them, and the epilogue's overlap with the next tile is worth more there.
-  static constexpr int MATS = (MODE == MODE_GATEUP || NT <= 64) ? 2 : 1;
-  static constexpr int OUT_ROWS = (MODE == MODE_GATEUP) ? kMTile : MATS * kMTile;  // output rows per tile
+  static constexpr int MATS = (MODE != MODE_DOWN || NT <= 64) ? 2 : 1;
+  static_assert(!FUSED || NT <= 64, "the fused launch needs the two-block down tiles");
+  // output rows per tile of one expert matrix, for a tile of mode `tmode`
+  static constexpr int out_rows(int tmode) { return tmode == MODE_GATEUP ? kMTile : MATS * kMTile; }
   static constexpr int STAGE_K = (WT == WT_Q4_K) ? 256 : 128;
   static constexpr int KB_PER_STAGE = STAGE_K / 128;
   static constexpr int B_BYTES = STAGE_K * NT * 2;
@@ -78,47 +81,72 @@ struct GemmCfg {
   static constexpr bool RING_OK = !QUANT || NA >= NDQ;
 };
 
+// mode: MODE_GATEUP or MODE_DOWN (per tile in a fused launch); ttx: the token tile's index in
+// the fused launch's completion counters (shared tiles first, then routed)
 struct TileInfo {
-  int group, expert, row0, nrows, mt, k0, k1;
+  int group, expert, row0, nrows, mt, k0, k1, mode, ttx;
 };
 
-__device__ __forceinline__ int tiles_total(const GemmParams& p) {
-  int n0 = p.grp[0].present ? p.n_shared_tt * p.grp[0].n_mt * p.ksplit : 0;
-  int n1 = p.grp[1].present ? (*p.n_tiles) * p.grp[1].n_mt * p.ksplit : 0;
+__device__ __forceinline__ int tiles_in(const GemmParams& p, const GemmGroup* gr) {
+  const int n0 = gr[0].present ? p.n_shared_tt * gr[0].n_mt * p.ksplit : 0;
+  const int n1 = gr[1].present ? (*p.n_tiles) * gr[1].n_mt * p.ksplit : 0;
   return n0 + n1;
 }
 
-template <int NT>
+template <int MODE>
+__device__ __forceinline__ int tiles_total(const GemmParams& p) {
+  return tiles_in(p, p.grp) + (MODE == MODE_FUSED ? tiles_in(p, p.grp_dn) : 0);
+}
+
+template <int MODE, int NT>
 __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
   TileInfo ti;
-  const int n0 = p.grp[0].present ? p.n_shared_tt * p.grp[0].n_mt * p.ksplit : 0;
+  ti.mode = MODE == MODE_FUSED ? MODE_GATEUP : MODE;
+  const GemmGroup* gr = p.grp;
+  if (MODE == MODE_FUSED) {
+    const int ngu = tiles_in(p, p.grp);
+    if (t >= ngu) {
+      t -= ngu;
+      ti.mode = MODE_DOWN;
+      gr = p.grp_dn;
+    }
+  }
+  const int n0 = gr[0].present ? p.n_shared_tt * gr[0].n_mt * p.ksplit : 0;
   int per_tt, r;
   if (t < n0) {
     ti.group = 0;
-    per_tt = p.grp[0].n_mt * p.ksplit;
+    per_tt = gr[0].n_mt * p.ksplit;
     const int tt = t / per_tt;
     r = t - tt * per_tt;
     ti.expert = 0;
     ti.row0 = tt * NT;
     const int64_t left = p.n_tokens - (int64_t)ti.row0;
     ti.nrows = left < NT ? (int)left : NT;
+    ti.ttx = tt;
   } else {
     t -= n0;
     ti.group = 1;
-    per_tt = p.grp[1].n_mt * p.ksplit;
+    per_tt = gr[1].n_mt * p.ksplit;
     const int tt = t / per_tt;
     r = t - tt * per_tt;
     const TokTile tk = p.tiles[tt];
     ti.expert = tk.expert;
     ti.row0 = tk.row0;
     ti.nrows = tk.nrows;
+    ti.ttx = p.n_shared_tt + tt;
   }
   ti.mt = r / p.ksplit;
   const int ks = r - ti.mt * p.ksplit;
-  const int ksz = p.grp[ti.group].k_stages / p.ksplit;
+  const int ksz = gr[ti.group].k_stages / p.ksplit;
   ti.k0 = ks * ksz;
   ti.k1 = ti.k0 + ksz;
   return ti;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -153,6 +181,26 @@ __device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, uint32
       return false;
     }
   }
+}
+
+// Fused launch: waits (bounded, like every wait here) until `*ctr` reaches `target`, i.e. every
+// gate/up epilogue warp of the token tile has published its h rows; then orders those generic-
+// proxy writes before this thread's TMA reads of them.
+__device__ __forceinline__ bool wait_count(const int32_t* ctr, int target, uint32_t* err, volatile int* abort_flag) {
+  if (ld_acquire_gpu(ctr) < target) {
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_gpu(ctr) < target) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > DMOE_WAIT_NS) {
+        atomicOr(err, ERRBIT_TIMEOUT_DEP);
+        *abort_flag = 1;
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 // Warp-uniform forms for roles whose whole warp walks the schedule: every lane waits, and
@@ -304,9 +352,11 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     for (int g = 0; g < 2; ++g) {
       if (!p.grp[g].present) continue;
       tma_prefetch_desc(&p.tm_w[g][0]);
-      if (MODE == MODE_GATEUP) tma_prefetch_desc(&p.tm_w[g][1]);
+      if (MODE != MODE_DOWN) tma_prefetch_desc(&p.tm_w[g][1]);
+      if (MODE == MODE_FUSED) tma_prefetch_desc(&p.tm_w_dn[g]);
     }
     tma_prefetch_desc(&p.tm_b);
+    if (MODE == MODE_FUSED) tma_prefetch_desc(&p.tm_b_dn);
   }
   tc_fence_before();
   __syncthreads();
@@ -315,7 +365,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
   // everything above overlaps the previous kernel's tail; global memory only after this
   pdl_wait();
   pdl_trigger();
-  const int total = tiles_total(p);
+  const int total = tiles_total<MODE>(p);
 
   auto stage_ptr = [&](int s) -> uint8_t* { return smem + s * C::STAGE_BYTES; };
   auto wtile_ptr = [&](int s, int m) -> uint8_t* { return smem + s * C::STAGE_BYTES + C::B_BYTES + m * C::W_BYTES; };
@@ -326,8 +376,18 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     const uint64_t pol_w = l2_policy_evict_first();
     uint32_t stage_seq = 0;
     for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
-      const TileInfo ti = decode_tile<NT>(p, t);
-      const int wrow = ti.expert * p.grp[ti.group].rows_per_exp + ti.mt * C::OUT_ROWS;
+      const TileInfo ti = decode_tile<MODE, NT>(p, t);
+      const bool dn = ti.mode == MODE_DOWN;
+      const bool dn_fused = C::FUSED && dn;
+      const GemmGroup& gg = dn_fused ? p.grp_dn[ti.group] : p.grp[ti.group];
+      const int wrow = ti.expert * gg.rows_per_exp + ti.mt * C::out_rows(ti.mode);
+      const CUtensorMap* tmb = dn_fused ? &p.tm_b_dn : &p.tm_b;
+      if (dn_fused) {
+        // the token tile's h rows: written by all of its gate/up tiles' epilogue warps
+        bool ready = true;
+        if (lane == 0) ready = wait_count(p.tt_done + ti.ttx, p.grp[ti.group].n_mt * C::EPI_WARPS, p.err, abort_flag);
+        if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) break;
+      }
       bool ok = true;
       for (int kc = ti.k0; kc < ti.k1; ++kc) {
         const int s = stage_seq % C::STAGES;
@@ -337,21 +397,22 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
           mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
 #pragma unroll
           for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
-            tma_load_2d(stage_ptr(s) + bx * NT * 128, &p.tm_b, kc * C::STAGE_K + bx * 64, ti.row0, &full[s]);
+            tma_load_2d(stage_ptr(s) + bx * NT * 128, tmb, kc * C::STAGE_K + bx * 64, ti.row0, &full[s]);
 #pragma unroll
           for (int m = 0; m < C::MATS; ++m) {
             uint8_t* wt = wtile_ptr(s, m);
             // gate/up: matrix m at the tile's rows; down: the one matrix, row block m
-            const int mi = MODE == MODE_GATEUP ? m : 0;
-            const int wr = MODE == MODE_GATEUP ? wrow : wrow + m * kMTile;
+            const CUtensorMap* tw = dn_fused ? &p.tm_w_dn[ti.group] : &p.tm_w[ti.group][dn ? 0 : m];
+            const CUtensorMap* ts = dn_fused ? &p.tm_s_dn[ti.group] : &p.tm_s[ti.group][dn ? 0 : m];
+            const int wr = dn ? wrow + m * kMTile : wrow;
             if constexpr (WT == WT_Q4_K) {
-              tma_load_2d_hint(wt, &p.tm_w[ti.group][mi], kc * 144, wr, &full[s], pol_w);
+              tma_load_2d_hint(wt, tw, kc * 144, wr, &full[s], pol_w);
             } else if constexpr (WT == WT_Q8_0) {
-              tma_load_2d_hint(wt, &p.tm_w[ti.group][mi], kc * 128, wr, &full[s], pol_w);
-              tma_load_2d_hint(wt + 128 * 128, &p.tm_s[ti.group][mi], kc * 4, wr, &full[s], pol_w);
+              tma_load_2d_hint(wt, tw, kc * 128, wr, &full[s], pol_w);
+              tma_load_2d_hint(wt + 128 * 128, ts, kc * 4, wr, &full[s], pol_w);
             } else {
-              tma_load_2d_hint(wt, &p.tm_w[ti.group][mi], kc * 128, wr, &full[s], pol_w);
-              tma_load_2d_hint(wt + 128 * 128, &p.tm_w[ti.group][mi], kc * 128 + 64, wr, &full[s], pol_w);
+              tma_load_2d_hint(wt, tw, kc * 128, wr, &full[s], pol_w);
+              tma_load_2d_hint(wt + 128 * 128, tw, kc * 128 + 64, wr, &full[s], pol_w);
             }
           }
         }
@@ -369,7 +430,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     constexpr uint32_t idesc = idesc_f16_f32(128, NT);
     uint32_t stage_seq = 0, tile_seq = 0;
     for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
-      const TileInfo ti = decode_tile<NT>(p, t);
+      const TileInfo ti = decode_tile<MODE, NT>(p, t);
       const int ab = tile_seq % C::ACC_BUFS;
       const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
       if (!warp_role_wait(&accempty[ab], aph ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) break;
@@ -448,7 +509,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint32_t tile_seq = 0;
     for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-      const TileInfo ti = decode_tile<NT>(p, t);
+      const TileInfo ti = decode_tile<MODE, NT>(p, t);
       const int ab = tile_seq % C::ACC_BUFS;
       const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
       float wv[NWR];
@@ -456,19 +517,19 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
 #pragma unroll
       for (int j = 0; j < NWR; ++j) {
         const int c = cb + 32 * j + lane;
-        const bool routed = MODE == MODE_DOWN && ti.group != 0 && c < ti.nrows && 32 * j + lane < HC;
+        const bool routed = ti.mode == MODE_DOWN && ti.group != 0 && c < ti.nrows && 32 * j + lane < HC;
         wv[j] = routed ? p.pair_w[ti.row0 + c] : 1.0f;
         tv[j] = (routed && p.y == nullptr) ? p.pair_tok[ti.row0 + c] : ti.row0 + c;
       }
       if (!role_wait(&accfull[ab], aph, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
       tc_fence_after();
       const uint32_t dbase = tbase + lane_off + ab * C::ACC_COLS;
-      const int obase = ti.mt * C::OUT_ROWS + quarter * 32;  // first output feature of this warp
+      const int obase = ti.mt * C::out_rows(ti.mode) + quarter * 32;  // first output feature of this warp
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         const int c0 = cb + 16 * ch;
         if (c0 >= ti.nrows) break;  // warp-uniform
-        if constexpr (MODE == MODE_GATEUP) {
+        if (ti.mode == MODE_GATEUP) {
           uint32_t acc0[16];
           tmem_ld16(dbase + c0, acc0);
           uint32_t acc1[16];
@@ -530,6 +591,12 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
          }
         }
       }
+      if (C::FUSED && ti.mode == MODE_GATEUP) {
+        // publish this warp's h rows of the token tile to the down tiles that wait for them
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.tt_done + ti.ttx, 1);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[ab]);
@@ -544,7 +611,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     uint32_t stage_seq = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
-      const TileInfo ti = decode_tile<NT>(p, t);
+      const TileInfo ti = decode_tile<MODE, NT>(p, t);
       for (int kc = ti.k0; kc < ti.k1; ++kc) {
         const int s = stage_seq % C::STAGES;
         const uint32_t ph = (stage_seq / C::STAGES) & 1u;
@@ -624,7 +691,9 @@ static cudaError_t launch_nt(const GemmParams& p, int nt, int ndq, int grid, cud
   switch (nt) {
     case 32: return launch_ndq<WT, MODE, 32>(p, ndq, grid, st);
     case 64: return launch_ndq<WT, MODE, 64>(p, ndq, grid, st);
-    case 128: return launch_ndq<WT, MODE, 128>(p, ndq, grid, st);
+    case 128:
+      if constexpr (MODE != MODE_FUSED) return launch_ndq<WT, MODE, 128>(p, ndq, grid, st);
+      return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
@@ -635,6 +704,12 @@ cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmPara
       case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_GATEUP>(p, nt, ndq, grid, st);
       case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_GATEUP>(p, nt, ndq, grid, st);
       case WT_F16: return launch_nt<WT_F16, MODE_GATEUP>(p, nt, ndq, grid, st);
+    }
+  } else if (mode == MODE_FUSED) {
+    switch (wtype) {
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_FUSED>(p, nt, ndq, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_FUSED>(p, nt, ndq, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_FUSED>(p, nt, ndq, grid, st);
     }
   } else {
     switch (wtype) {

@@ -20,7 +20,8 @@ enum : uint32_t {
   ERRBIT_TIMEOUT_EMPTY = 1u << 1,  // producer waited too long for a free stage
   ERRBIT_TIMEOUT_MMA = 1u << 2,    // waited too long for tensor-core completion
   ERRBIT_TIMEOUT_TMEM = 1u << 3,   // waited too long for a TMEM operand / accumulator hand-off
-  ERRBIT_BAD_TILE = 1u << 4,       // a tile descriptor pointed outside its buffers
+  ERRBIT_TIMEOUT_DEP = 1u << 4,    // fused launch: waited too long for a token tile's h rows
+  ERRBIT_BAD_TILE = 1u << 5,       // a tile descriptor pointed outside its buffers
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -98,6 +98,7 @@ class Stats(ctypes.Structure):
         ("ms_total", ctypes.c_float),
         ("ep_rows_sent", ctypes.c_int64),
         ("ep_rows_received", ctypes.c_int64),
+        ("fused_gemm", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict:

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define DMOE_ABI_VERSION 2
+#define DMOE_ABI_VERSION 3
 
 /* Replaces the reference's bool returns + DIFFUSE_DIE/exit(1) (src/diffuse-common.h:22-27,
  * src/diffuse-moe-graph.cpp:325-329). */
@@ -123,6 +123,7 @@ typedef struct dmoe_stats {
   float ms_total;
   int64_t ep_rows_sent;     /* expert parallelism: (token, rank) rows sent / received */
   int64_t ep_rows_received;
+  int32_t fused_gemm;       /* 1: gate/up and down ran as one launch (ms_down holds both, ms_gateup ~ 0) */
 } dmoe_stats;
 
 #define DMOE_F_HOST_PTRS 1u   /* x, out and route_out are host memory: the call copies them and

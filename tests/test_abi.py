@@ -31,7 +31,7 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version():
-    assert dm.load().dmoe_abi_version() == 2
+    assert dm.load().dmoe_abi_version() == 3
 
 
 def test_argument_errors_are_status_codes():
