@@ -95,14 +95,25 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// d = a * b + d on two fp32 lanes at once (sm_100 fma.rn.f32x2): each lane is an IEEE
-// round-to-nearest fma, bitwise the same as fmaf, at half the issue slots.
-__device__ __forceinline__ void ffma2(float2& d, float2 a, float2 b) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "+f"(d.x), "+f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+// Packed fp32 pairs (low word = first value) for sm_100's fma.rn.f32x2: each lane is an IEEE
+// round-to-nearest fma, bitwise the same as fmaf, at half the issue slots. Accumulators and
+// weight pairs stay packed in 64-bit registers; each x value is duplicated once per k.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ void ffma2(f32x2& d, f32x2 a, f32x2 b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ f32x2 dup2(float x) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float2 unpack2(f32x2 v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ void lds2x64(uint32_t a, f32x2& lo, f32x2& hi) {
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "r"(a));
 }
 
 template <int TM, bool SPLIT>
@@ -150,13 +161,13 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
   };
 
   float tot[TM][8];
-  float2 acc[TM][4];  // experts (2 jp, 2 jp + 1) of the thread's 8
+  f32x2 acc[TM][4];  // experts (2 jp, 2 jp + 1) of the thread's 8, packed
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) tot[i][j] = 0.0f;
 #pragma unroll
-    for (int jp = 0; jp < 4; ++jp) acc[i][jp] = make_float2(0.0f, 0.0f);
+    for (int jp = 0; jp < 4; ++jp) acc[i][jp] = 0ull;  // (+0.0f, +0.0f)
   }
 
 #pragma unroll
@@ -179,13 +190,12 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t wrow = ws + ((4 * k4 + kk) * RL_EXP) * 4;
-        const float4 wa = lds128f(wrow + (4 * tx) * 4), wb = lds128f(wrow + (32 + 4 * tx) * 4);
-        const float2 wp[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
-                              make_float2(wb.z, wb.w)};
+        f32x2 wp[4];
+        lds2x64(wrow + (4 * tx) * 4, wp[0], wp[1]);
+        lds2x64(wrow + (32 + 4 * tx) * 4, wp[2], wp[3]);
 #pragma unroll
         for (int i = 0; i < TM; ++i) {
-          const float xi = kk == 0 ? xv[i].x : kk == 1 ? xv[i].y : kk == 2 ? xv[i].z : xv[i].w;
-          const float2 xx = make_float2(xi, xi);
+          const f32x2 xx = dup2(kk == 0 ? xv[i].x : kk == 1 ? xv[i].y : kk == 2 ? xv[i].z : xv[i].w);
 #pragma unroll
           for (int jp = 0; jp < 4; ++jp) ffma2(acc[i][jp], xx, wp[jp]);
         }
@@ -197,9 +207,10 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
       for (int i = 0; i < TM; ++i)
 #pragma unroll
         for (int jp = 0; jp < 4; ++jp) {
-          tot[i][2 * jp] = first ? acc[i][jp].x : __fadd_rn(tot[i][2 * jp], acc[i][jp].x);
-          tot[i][2 * jp + 1] = first ? acc[i][jp].y : __fadd_rn(tot[i][2 * jp + 1], acc[i][jp].y);
-          acc[i][jp] = make_float2(0.0f, 0.0f);
+          const float2 a = unpack2(acc[i][jp]);
+          tot[i][2 * jp] = first ? a.x : __fadd_rn(tot[i][2 * jp], a.x);
+          tot[i][2 * jp + 1] = first ? a.y : __fadd_rn(tot[i][2 * jp + 1], a.y);
+          acc[i][jp] = 0ull;
         }
     }
   }
