@@ -70,7 +70,8 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 //                  of a tile to finish (per-tile arrival counter) adds P_0 .. P_{S-1} left to
 //                  right, writes p to part[0] and re-arms the counter (small N, where whole-K
 //                  tiles cannot fill the GPU).
-// TM = 4 for large N (fewer shared-memory reads per fma), TM = 2 for small N (more CTAs).
+// TM = 8 for large N (fewer shared-memory reads per fma, the router weight re-read half as often),
+// TM = 2 for small N (more CTAs).
 // ------------------------------------------------------------------------------------------
 constexpr int RL_EXP = 64, RL_KC = 32, RL_THREADS = 128;
 constexpr int RL_XP = RL_KC + 4;  // x tile row pitch (floats)
@@ -83,8 +84,14 @@ constexpr int rl_stage_floats() { return rl_tok<TM>() * RL_XP + RL_KC * RL_EXP; 
 // instead of eight); the whole-K path keeps a 3-deep ring
 template <bool SPLIT>
 constexpr int rl_stages() { return SPLIT ? kRouterSeg / RL_KC : 3; }
+// TM = 8 keeps the running segment sums tot in shared memory (expert-major: [TM x 8][thread],
+// conflict-free) instead of 64 more registers
+template <int TM>
+constexpr bool rl_tot_smem() { return TM >= 8; }
 template <int TM, bool SPLIT>
-constexpr int rl_smem() { return rl_stages<SPLIT>() * rl_stage_floats<TM>() * 4; }
+constexpr int rl_smem() {
+  return rl_stages<SPLIT>() * rl_stage_floats<TM>() * 4 + (rl_tot_smem<TM>() ? TM * 8 * RL_THREADS * 4 : 0);
+}
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
@@ -117,7 +124,7 @@ __device__ __forceinline__ void lds2x64(uint32_t a, f32x2& lo, f32x2& hi) {
 }
 
 template <int TM, bool SPLIT>
-__global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(RL_THREADS, TM >= 8 ? 2 : 4) router_logits_kernel(const float* __restrict__ x,
                                                                    const float* __restrict__ wrt,
                                                                    float* __restrict__ part, int64_t n, int h, int e,
                                                                    int32_t* __restrict__ arrivals,
@@ -160,15 +167,20 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
     }
   };
 
-  float tot[TM][8];
+  constexpr bool TOT_SMEM = rl_tot_smem<TM>();
+  float tot[TOT_SMEM ? 1 : TM][8];
+  float* tot_s = rl_smem_f + RL_STAGES * rl_stage_floats<TM>();  // TOT_SMEM: [TM * 8][RL_THREADS]
   f32x2 acc[TM][4];  // experts (2 jp, 2 jp + 1) of the thread's 8, packed
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) tot[i][j] = 0.0f;
+    for (int j = 0; j < 8; ++j)
+      if (!TOT_SMEM) tot[i][j] = 0.0f;
 #pragma unroll
     for (int jp = 0; jp < 4; ++jp) acc[i][jp] = 0ull;  // (+0.0f, +0.0f)
   }
+  // tot[i][j] lives in tot_s[(8 i + j) * RL_THREADS + tid] when TOT_SMEM
+  auto tot_ref = [&](int i, int j) -> float& { return TOT_SMEM ? tot_s[(8 * i + j) * RL_THREADS + tid] : tot[TOT_SMEM ? 0 : i][j]; };
 
 #pragma unroll
   for (int c = 0; c < RL_STAGES - 1; ++c) {
@@ -208,8 +220,10 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
 #pragma unroll
         for (int jp = 0; jp < 4; ++jp) {
           const float2 a = unpack2(acc[i][jp]);
-          tot[i][2 * jp] = first ? a.x : __fadd_rn(tot[i][2 * jp], a.x);
-          tot[i][2 * jp + 1] = first ? a.y : __fadd_rn(tot[i][2 * jp + 1], a.y);
+          float& t0r = tot_ref(i, 2 * jp);
+          float& t1r = tot_ref(i, 2 * jp + 1);
+          t0r = first ? a.x : __fadd_rn(t0r, a.x);
+          t1r = first ? a.y : __fadd_rn(t1r, a.y);
           acc[i][jp] = 0ull;
         }
     }
@@ -224,12 +238,12 @@ __global__ void __launch_bounds__(RL_THREADS, 4) router_logits_kernel(const floa
     for (int j = 0; j < 8; j += 4) {
       const int ee = e0 + (j == 0 ? 4 * tx : 32 + 4 * tx);
       if (ee >= e) continue;
+      const float v0 = tot_ref(i, j), v1 = tot_ref(i, j + 1), v2 = tot_ref(i, j + 2), v3 = tot_ref(i, j + 3);
       if constexpr (SPLIT) {
-        *reinterpret_cast<float4*>(dst + tok * e + ee) = make_float4(tot[i][j], tot[i][j + 1], tot[i][j + 2], tot[i][j + 3]);
+        *reinterpret_cast<float4*>(dst + tok * e + ee) = make_float4(v0, v1, v2, v3);
       } else {
         *reinterpret_cast<float4*>(dst + tok * e + ee) =
-            make_float4(sigmoid_canonical(tot[i][j]), sigmoid_canonical(tot[i][j + 1]),
-                        sigmoid_canonical(tot[i][j + 2]), sigmoid_canonical(tot[i][j + 3]));
+            make_float4(sigmoid_canonical(v0), sigmoid_canonical(v1), sigmoid_canonical(v2), sigmoid_canonical(v3));
       }
     }
   }
@@ -465,19 +479,20 @@ cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t
     return launch_pdl(router_logits_kernel<2, true>, grid, dim3(RL_THREADS), rl_smem<2, true>(), st, x, wrt, part, n, h,
                       e, arrivals, zero_counts);
   } else {
-    dim3 grid((unsigned)((n + rl_tok<4>() - 1) / rl_tok<4>()), gy, 1u);
-    cudaFuncSetAttribute(router_logits_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         rl_smem<4, false>());
-    return launch_pdl(router_logits_kernel<4, false>, grid, dim3(RL_THREADS), rl_smem<4, false>(), st, x, wrt, part, n,
+    dim3 grid((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, 1u);
+    cudaFuncSetAttribute(router_logits_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         rl_smem<8, false>());
+    return launch_pdl(router_logits_kernel<8, false>, grid, dim3(RL_THREADS), rl_smem<8, false>(), st, x, wrt, part, n,
                       h, e, (int32_t*)nullptr, zero_counts);
   }
   return cudaGetLastError();
 }
 
-// Splitting by segment pays when the whole-K tiles cannot fill the GPU twice over.
+// Splitting by segment pays while the whole-K tiles would leave most SMs idle. Measured on B200
+// (E = 256, H = 4096): split 224 vs whole-K 307 us at 2048 tokens, 449 vs 310 us at 4096.
 bool router_split(int64_t n, int e, int sms) {
-  const int64_t tiles = ((n + rl_tok<4>() - 1) / rl_tok<4>()) * ((e + RL_EXP - 1) / RL_EXP);
-  return tiles < 2LL * sms;
+  const int64_t tiles = ((n + rl_tok<8>() - 1) / rl_tok<8>()) * ((e + RL_EXP - 1) / RL_EXP);
+  return 2 * tiles < sms;
 }
 
 int64_t router_arrivals(int64_t n, int e) { return ((n + rl_tok<2>() - 1) / rl_tok<2>()) * ((e + RL_EXP - 1) / RL_EXP); }
