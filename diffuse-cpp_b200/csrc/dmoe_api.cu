@@ -187,6 +187,11 @@ struct dmoe_layer {
   bool has_shared = false, has_bias = false;
   int device = 0, sms = 148;
   cudaStream_t own_stream = nullptr;
+  // host-buffer calls of many tokens: chunk copies overlap the compute (two copy streams, so the
+  // two PCIe directions run at once), kMaxChunks events per direction
+  static constexpr int kMaxChunks = 8;
+  cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;
+  cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {}, ev_start = nullptr;
   // weights
   float* wr = nullptr;  // router weight transposed, [H][E]
   float* br = nullptr;
@@ -703,6 +708,71 @@ dmoe_status ep_experts(dmoe_layer* L, cudaStream_t st, const float* xd, int64_t 
   return DMOE_OK;
 }
 
+// Chunk size for a pipelined host-buffer call, or 0 to run it whole. Only on one GPU, without
+// routing outputs or profiling (their per-call buffers would be shared between chunks), for at
+// least 4096 tokens, and only where chunking cannot change the routing: chunks are whole routing
+// blocks when the call uses block routing, and a call that does not (n % block != 0) is not
+// chunked if a chunk of whole blocks would switch block routing on.
+int64_t host_chunk_tokens(const dmoe_layer* L, int64_t n, bool host, const dmoe_route_out* route, uint32_t flags) {
+  if (!host || route || (flags & (DMOE_F_ROUTE_ONLY | DMOE_F_PROFILE)) || L->world > 1) return 0;
+  const int64_t target = env_int("DMOE_HOST_CHUNK", 2048);
+  if (target <= 0 || n < 2 * target) return 0;
+  const bool block_possible = L->blk > 1 && L->cap > 0 && L->cap < L->E;
+  int64_t chunk = target;
+  if (block_possible) {
+    if (n % L->blk) return 0;
+    chunk = std::max<int64_t>(L->blk, target / L->blk * L->blk);
+  }
+  if ((n + chunk - 1) / chunk > dmoe_layer::kMaxChunks) chunk = (n + dmoe_layer::kMaxChunks - 1) / dmoe_layer::kMaxChunks;
+  if (block_possible) chunk = (chunk + L->blk - 1) / L->blk * L->blk;
+  return chunk;
+}
+
+}  // namespace
+
+extern "C" {
+dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, const dmoe_route_out* route,
+                         void* stream, uint32_t flags);
+}
+
+namespace {
+
+// Host-buffer call in chunks: H2D of every chunk on h2d_stream, each chunk's layer on the layer's
+// stream once its input has landed, the D2H of its output on d2h_stream once it is computed.
+// The statistics describe the last chunk.
+dmoe_status forward_chunked(dmoe_layer* L, const float* x, int64_t n, float* out, int64_t chunk, uint32_t flags) {
+  const int64_t H = L->H;
+  dmoe_status s;
+  if ((s = grow(L->xdev, L->xdev_cap, (size_t)n * H)) != DMOE_OK) return s;
+  if ((s = grow(L->odev, L->odev_cap, (size_t)n * H)) != DMOE_OK) return s;
+  cudaStream_t ks = L->own_stream;
+  // the copies reuse xdev / odev: order them after earlier work on the layer's stream
+  DMOE_CUDA(cudaEventRecord(L->ev_start, ks));
+  DMOE_CUDA(cudaStreamWaitEvent(L->h2d_stream, L->ev_start, 0));
+  DMOE_CUDA(cudaStreamWaitEvent(L->d2h_stream, L->ev_start, 0));
+  const int nc = (int)((n + chunk - 1) / chunk);
+  for (int c = 0; c < nc; ++c) {
+    const int64_t t0 = c * chunk, cn = std::min(chunk, n - t0);
+    DMOE_CUDA(cudaMemcpyAsync(L->xdev + t0 * H, x + t0 * H, (size_t)cn * H * 4, cudaMemcpyHostToDevice, L->h2d_stream));
+    DMOE_CUDA(cudaEventRecord(L->ev_in[c], L->h2d_stream));
+  }
+  int kernels = 0;
+  for (int c = 0; c < nc; ++c) {
+    const int64_t t0 = c * chunk, cn = std::min(chunk, n - t0);
+    DMOE_CUDA(cudaStreamWaitEvent(ks, L->ev_in[c], 0));
+    if ((s = dmoe_forward(L, L->xdev + t0 * H, cn, L->odev + t0 * H, nullptr, ks, flags & ~DMOE_F_HOST_PTRS)) != DMOE_OK)
+      return s;
+    kernels += L->stats.kernels;
+    DMOE_CUDA(cudaEventRecord(L->ev_done[c], ks));
+    DMOE_CUDA(cudaStreamWaitEvent(L->d2h_stream, L->ev_done[c], 0));
+    DMOE_CUDA(cudaMemcpyAsync(out + t0 * H, L->odev + t0 * H, (size_t)cn * H * 4, cudaMemcpyDeviceToHost, L->d2h_stream));
+  }
+  DMOE_CUDA(cudaStreamSynchronize(L->d2h_stream));
+  L->stats.kernels = kernels;
+  L->last_stream = ks;
+  return dmoe_sync(L);
+}
+
 }  // namespace
 
 extern "C" {
@@ -769,8 +839,16 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
   L->rank = world > 1 ? dist->rank : 0;
   L->e_local = L->E / world;
   L->timeout_ms = (dist && dist->timeout_ms > 0) ? dist->timeout_ms : 60000;
-  if (cudaStreamCreateWithFlags(&L->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+  if (cudaStreamCreateWithFlags(&L->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&L->h2d_stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&L->d2h_stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(fail(DMOE_ERR_CUDA, "stream create"));
+  for (int c = 0; c < dmoe_layer::kMaxChunks; ++c)
+    if (cudaEventCreateWithFlags(&L->ev_in[c], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&L->ev_done[c], cudaEventDisableTiming) != cudaSuccess)
+      return bail(fail(DMOE_ERR_CUDA, "event create"));
+  if (cudaEventCreateWithFlags(&L->ev_start, cudaEventDisableTiming) != cudaSuccess)
+    return bail(fail(DMOE_ERR_CUDA, "event create"));
   for (auto& e : L->ev)
     if (cudaEventCreate(&e) != cudaSuccess) return bail(fail(DMOE_ERR_CUDA, "event create"));
   {
@@ -876,6 +954,16 @@ void dmoe_destroy(dmoe_layer* L) {
   for (auto& e : L->ev)
     if (e) cudaEventDestroy(e);
   if (L->own_stream) cudaStreamDestroy(L->own_stream);
+  for (cudaStream_t cs : {L->h2d_stream, L->d2h_stream})
+    if (cs) {
+      cudaStreamSynchronize(cs);
+      cudaStreamDestroy(cs);
+    }
+  for (int c = 0; c < dmoe_layer::kMaxChunks; ++c) {
+    if (L->ev_in[c]) cudaEventDestroy(L->ev_in[c]);
+    if (L->ev_done[c]) cudaEventDestroy(L->ev_done[c]);
+  }
+  if (L->ev_start) cudaEventDestroy(L->ev_start);
   delete L;
 }
 
@@ -899,6 +987,8 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   set_pdl_for_call(n < 1024);
   std::memset(&L->stats, 0, sizeof(L->stats));
   if (n == 0) return DMOE_OK;
+  if (const int64_t chunk = host_chunk_tokens(L, n, host, route, flags); chunk > 0)
+    return forward_chunked(L, x, n, out, chunk, flags);
 
   const int64_t H = L->H, E = L->E, K = L->K;
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;
