@@ -416,6 +416,11 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   const bool fused = same_type && ks_gu == 1 && ks_dn == 1 && nt <= 64 &&
                      (f_env == 1 || (f_env != 0 && n_sh <= 128));
   gp.tt_done = L->tt_done;
+  // experts average more than one token tile: their weight tiles are re-read, keep them in L2
+  {
+    const int wk = env_int("DMOE_WKEEP", -1);
+    gp.w_keep = wk >= 0 ? (wk != 0) : (pairs >= (int64_t)nt * std::min<int64_t>(E_here, pairs) ? 1 : 0);
+  }
   if (fused) {
     // launched below, once the down operands are set
   } else if (same_type) {

@@ -54,6 +54,7 @@ struct GemmParams {
   const int32_t* n_tiles;      // number of routed token tiles (device)
   int32_t n_shared_tt;         // shared-expert token tiles (host-known: ceil(N / NT))
   int32_t ksplit;              // split-K factor
+  int32_t w_keep;              // 1: weight tiles are re-read by several token tiles (L2 evict normal)
   int64_t n_tokens;
   // gate/up epilogue
   __half* hbuf;

@@ -373,7 +373,9 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     // (whole warp walks the schedule; one elected lane issues each stage's copies)
-    const uint64_t pol_w = l2_policy_evict_first();
+    // weights read by one token tile stream through L2 (evict first); weights of experts with
+    // several token tiles are re-read and kept (evict normal) -- chosen by the host
+    const uint64_t pol_w = p.w_keep ? l2_policy_evict_normal() : l2_policy_evict_first();
     uint32_t stage_seq = 0;
     for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
       const TileInfo ti = decode_tile<MODE, NT>(p, t);
