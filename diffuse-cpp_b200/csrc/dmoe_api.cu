@@ -320,6 +320,17 @@ int pick_ksplit(int64_t tiles_est, int sms, std::initializer_list<int> kstages) 
   return best;
 }
 
+// CTA-pair GEMM tiles (256 output rows per tile, one activation tile per two SMs): quantised
+// weights at NT = 128, every expert matrix a multiple of 256 rows. DMOE_PAIR = 0 / 1 overrides.
+bool use_pair(const dmoe_layer* L, int nt) {
+  const int forced = env_int("DMOE_PAIR", -1);
+  if (forced == 0) return false;
+  const bool quant = L->etype != DMOE_TYPE_F16 && (!L->has_shared || L->stype != DMOE_TYPE_F16);
+  const bool rows256 = L->I % 256 == 0 && L->H % 256 == 0 && (!L->has_shared || L->Is % 256 == 0);
+  if (!(quant && rows256 && gemm_pair_ok(L->etype, MODE_GATEUP, nt))) return false;
+  return forced == 1;
+}
+
 // n_out_rows / rows_per_tile output tiles per expert (gate/up tiles cover 128 rows of each of the
 // two matrices, down tiles 256 rows of the one)
 void fill_group(GemmGroup& g, const DevWeight& w, int32_t type, int64_t rows_per_exp, int64_t n_out_rows,
@@ -345,12 +356,15 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   const int64_t Imax = std::max(L->I, L->Is);
   const int64_t E_here = L->world > 1 ? L->e_local : L->E;
   dmoe_status s;
+  const bool pair = use_pair(L, nt);
+  // activation tiles: NT token rows, or each pair CTA's half of them
+  const uint32_t b_rows = (uint32_t)(pair ? nt / 2 : nt);
   CUtensorMap tm_x, tm_h;
   if ((s = make_map(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->xg, (uint64_t)H, (uint64_t)rows, (uint64_t)H * 2, 64,
-                    (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+                    b_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
     return s;
   if ((s = make_map(&tm_h, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->hbuf, (uint64_t)Imax, (uint64_t)rows,
-                    (uint64_t)Imax * 2, 64, (uint32_t)nt, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+                    (uint64_t)Imax * 2, 64, b_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
     return s;
   const int64_t pairs = rows - n_sh;
   const int64_t tt_est = std::min<int64_t>(E_here, pairs) + pairs / nt;
@@ -397,13 +411,13 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
     gp.tm_w[0][1] = L->sup.tm_q;
     gp.tm_s[0][0] = L->sgate.tm_s;
     gp.tm_s[0][1] = L->sup.tm_s;
-    fill_group(gp.grp[0], L->sgate, L->stype, L->Is, L->Is);
+    fill_group(gp.grp[0], L->sgate, L->stype, L->Is, L->Is, gemm_out_rows(MODE_GATEUP, nt, pair));
   }
   gp.tm_w[1][0] = L->gate.tm_q;
   gp.tm_w[1][1] = L->up.tm_q;
   gp.tm_s[1][0] = L->gate.tm_s;
   gp.tm_s[1][1] = L->up.tm_s;
-  fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I);
+  fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I, gemm_out_rows(MODE_GATEUP, nt, pair));
   const int grid = L->sms;
   // dequant warpgroups per CTA: the largest of 4 / 3 / 2 the TMEM ring allows (measured 2-3 %
   // faster than 2 at 1-8 blocks)
@@ -424,14 +438,14 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   if (fused) {
     // launched below, once the down operands are set
   } else if (same_type) {
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, gp, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, pair, gp, grid, st));
     ++kernels;
   } else {
     GemmParams g0 = gp, g1 = gp;
     g0.grp[1].present = 0;
     g1.grp[0].present = 0;
-    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, ndq, g0, grid, st));
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, g1, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, ndq, pair, g0, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, pair, g1, grid, st));
     kernels += 2;
   }
   if (ks_gu > 1) {
@@ -467,11 +481,11 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   if (L->has_shared) {
     dp.tm_w[0][0] = L->sdown.tm_q;
     dp.tm_s[0][0] = L->sdown.tm_s;
-    fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt));
+    fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair));
   }
   dp.tm_w[1][0] = L->down.tm_q;
   dp.tm_s[1][0] = L->down.tm_s;
-  fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt));
+  fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair));
   if (fused) {
     GemmParams fp = gp;  // gate/up operands and tiles ...
     fp.tm_b_dn = dp.tm_b;  // ... then the down phase's
@@ -488,17 +502,17 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
     fp.y_ld = dp.y_ld;
     fp.pair_tok = dp.pair_tok;
     fp.pair_w = dp.pair_w;
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_FUSED, nt, ndq, fp, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_FUSED, nt, ndq, false, fp, grid, st));
     ++kernels;
   } else if (same_type) {
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, dp, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, pair, dp, grid, st));
     ++kernels;
   } else {
     GemmParams d0 = dp, d1 = dp;
     d0.grp[1].present = 0;
     d1.grp[0].present = 0;
-    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, d0, grid, st));
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, d1, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, pair, d0, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, pair, d1, grid, st));
     kernels += 2;
   }
   if (combine) {

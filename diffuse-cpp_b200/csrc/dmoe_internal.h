@@ -131,9 +131,13 @@ cudaError_t launch_ep_final(float* out, const float* back, int64_t n, int h, con
                             const RankOffsets& soff, cudaStream_t st);
 cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows, int64_t n, int is, int iw,
                                  __half* hbuf, int64_t h_ld, int swap_shared, int swap_routed, cudaStream_t st);
-cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st);
+// pair: clusters of two CTAs sharing 256-row tiles (tcgen05 cta_group::2); gemm_pair_ok says
+// which launches have that form (quantised weights, NT = 128, separate gate/up and down launches)
+cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, bool pair, const GemmParams& p, int grid,
+                            cudaStream_t st);
+bool gemm_pair_ok(int wtype, int mode, int nt);
 int gemm_stage_k(int wtype);
-int gemm_out_rows(int mode, int nt);  // output rows per tile of one expert matrix
+int gemm_out_rows(int mode, int nt, bool pair);  // output rows per tile of one expert matrix
 
 // Launch with programmatic stream serialization: the kernel may start while its predecessor in
 // the stream finishes; every such kernel calls pdl_wait() before touching global memory.

@@ -32,21 +32,31 @@
 
 namespace dmoe {
 
-template <int WT, int MODE, int NT, int NDQ_ = 2>
+// PAIR: a cluster of two CTAs shares each tile through tcgen05 cta_group::2 (M = 256): CTA r
+// dequantises weight rows [128 r, 128 r + 128) of a 256-row tile into its own TMEM and loads its
+// half of the NT tokens; the leader (rank 0) issues the MMAs, which read both CTAs' halves and
+// write each CTA's 128 rows x NT accumulator. Each activation tile then crosses L2 once per 256
+// rows instead of once per 128. Quantised weights at NT = 128 only.
+template <int WT, int MODE, int NT, int NDQ_ = 2, bool PAIR_ = false>
 struct GemmCfg {
   static constexpr bool QUANT = (WT != WT_F16);
   static constexpr bool FUSED = MODE == MODE_FUSED;
+  static constexpr bool PAIR = PAIR_;
+  static constexpr int B_ROWS = PAIR ? NT / 2 : NT;  // token rows of B this CTA loads
   // two weight tiles share each activation (B) tile: gate and up, or (down, NT <= 64) two
   // adjacent 128-row blocks of the down matrix, so B crosses L2 once per 256 output rows. At
   // NT = 128 the down tile keeps one block: two 128-column accumulators would leave TMEM no room
   // to double-buffer them, and the epilogue's overlap with the next tile is worth more there.
   static constexpr int MATS = (MODE != MODE_DOWN || NT <= 64) ? 2 : 1;
   static_assert(!FUSED || NT <= 64, "the fused launch needs the two-block down tiles");
+  static_assert(!PAIR || (QUANT && !FUSED && NT == 128 && MATS * 64 * 2 <= 256), "pair tiles: quantised, NT = 128");
   // output rows per tile of one expert matrix, for a tile of mode `tmode`
-  static constexpr int out_rows(int tmode) { return tmode == MODE_GATEUP ? kMTile : MATS * kMTile; }
+  static constexpr int out_rows(int tmode) {
+    return PAIR ? 2 * kMTile : (tmode == MODE_GATEUP ? kMTile : MATS * kMTile);
+  }
   static constexpr int STAGE_K = (WT == WT_Q4_K) ? 256 : 128;
   static constexpr int KB_PER_STAGE = STAGE_K / 128;
-  static constexpr int B_BYTES = STAGE_K * NT * 2;
+  static constexpr int B_BYTES = STAGE_K * B_ROWS * 2;
   // per matrix per stage: q4_K 128 rows x one 144 B super-block; q8_0 128 x 128 int8 (SW128)
   // + 128 x 4 fp32 scales; f16 two SW128 boxes of 128 x 64.
   static constexpr int W_BYTES = (WT == WT_Q4_K) ? 128 * 144 : (WT == WT_Q8_0) ? (128 * 128 + 128 * 16) : (128 * 128 * 2);
@@ -308,10 +318,10 @@ __device__ __forceinline__ float silu_f(float g) { return g * __frcp_rn(1.0f + _
 
 __device__ __forceinline__ int quad_swap(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
 
-template <int WT, int MODE, int NT, int NDQ_>
-__global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
+template <int WT, int MODE, int NT, int NDQ_, bool PAIR>
+__global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p) {
-  using C = GemmCfg<WT, MODE, NT, NDQ_>;
+  using C = GemmCfg<WT, MODE, NT, NDQ_, PAIR>;
   static_assert(C::RING_OK, "A ring needs at least one buffer per dequant warpgroup");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -322,11 +332,38 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
   uint64_t* aempty = afull + 4;
   uint64_t* accfull = aempty + 4;
   uint64_t* accempty = accfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
+  uint64_t* full_b = accempty + 2;  // PAIR: both CTAs' activation halves landed (leader's copy counts)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full_b + (C::PAIR ? C::STAGES : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
+  const uint32_t rank = C::PAIR ? cluster_ctarank() : 0u;  // 0 = leader of the pair
+  // PAIR: the leader's copy of barrier `b` (in the shared::cluster window)
+  auto leader = [&](uint64_t* b) -> uint32_t { return mapa_shared(smem_u32(b), 0); };
+  // waits: barriers that receive arrivals from the peer CTA acquire at cluster scope
+  auto bwait = [&](uint64_t* bar, uint32_t parity, uint32_t errbit) -> bool {
+    if constexpr (C::PAIR) {
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+      const uint64_t t0 = globaltimer_ns();
+      while (true) {
+        for (int i = 0; i < 32; ++i)
+          if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > DMOE_WAIT_NS) {
+          atomicOr(p.err, errbit);
+          *abort_flag = 1;
+          return false;
+        }
+      }
+    } else {
+      return role_wait(bar, parity, p.err, errbit, abort_flag);
+    }
+  };
+  auto wbwait = [&](uint64_t* bar, uint32_t parity, uint32_t errbit) -> bool {
+    const bool ok = bwait(bar, parity, errbit);
+    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -334,19 +371,26 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
       mbar_init(&empty[s], C::EMPTY_COUNT);
     }
     for (int a = 0; a < 4; ++a) {
-      mbar_init(&afull[a], 4);
+      mbar_init(&afull[a], C::PAIR ? 8 : 4);  // PAIR: both CTAs' dequant warps arrive on the leader's
       mbar_init(&aempty[a], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], C::EPI_WARPS);
+      mbar_init(&accempty[b], C::PAIR ? 2 * C::EPI_WARPS : C::EPI_WARPS);
     }
+    if (C::PAIR)
+      for (int s = 0; s < C::STAGES; ++s) mbar_init(&full_b[s], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if constexpr (C::PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);  // the same warp of both CTAs, same slot offset
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     for (int g = 0; g < 2; ++g) {
@@ -360,12 +404,16 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (C::PAIR) cluster_sync();  // the peer's barriers are initialised before any arrival
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   // everything above overlaps the previous kernel's tail; global memory only after this
   pdl_wait();
   pdl_trigger();
   const int total = tiles_total<MODE>(p);
+  // tile walk: one CTA per SM, or (PAIR) one pair per two SMs, both CTAs on the same tiles
+  const int t_first = C::PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int t_step = C::PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   auto stage_ptr = [&](int s) -> uint8_t* { return smem + s * C::STAGE_BYTES; };
   auto wtile_ptr = [&](int s, int m) -> uint8_t* { return smem + s * C::STAGE_BYTES + C::B_BYTES + m * C::W_BYTES; };
@@ -377,7 +425,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     // several token tiles are re-read and kept (evict normal) -- chosen by the host
     const uint64_t pol_w = p.w_keep ? l2_policy_evict_normal() : l2_policy_evict_first();
     uint32_t stage_seq = 0;
-    for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
+    for (int t = t_first; t < total && !warp_abort(abort_flag); t += t_step) {
       const TileInfo ti = decode_tile<MODE, NT>(p, t);
       const bool dn = ti.mode == MODE_DOWN;
       const bool dn_fused = C::FUSED && dn;
@@ -394,19 +442,31 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
       for (int kc = ti.k0; kc < ti.k1; ++kc) {
         const int s = stage_seq % C::STAGES;
         const uint32_t ph = (stage_seq / C::STAGES) & 1u;
-        if (!warp_role_wait(&empty[s], ph ^ 1u, p.err, ERRBIT_TIMEOUT_EMPTY, abort_flag)) { ok = false; break; }
+        if (!wbwait(&empty[s], ph ^ 1u, ERRBIT_TIMEOUT_EMPTY)) { ok = false; break; }
         if (elect_one()) {
-          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          if constexpr (C::PAIR) {
+            // weights count on this CTA's full[s]; both CTAs' activation halves on the leader's
+            // full_b[s] (its expected bytes are armed by the leader alone)
+            mbar_arrive_expect_tx(&full[s], C::MATS * C::W_BYTES);
+            if (rank == 0) mbar_arrive_expect_tx(&full_b[s], 2 * C::B_BYTES);
 #pragma unroll
-          for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
-            tma_load_2d(stage_ptr(s) + bx * NT * 128, tmb, kc * C::STAGE_K + bx * 64, ti.row0, &full[s]);
+            for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
+              tma_load_2d_pair(stage_ptr(s) + bx * C::B_ROWS * 128, tmb, kc * C::STAGE_K + bx * 64,
+                               ti.row0 + (int)rank * C::B_ROWS, leader(&full_b[s]));
+          } else {
+            mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+#pragma unroll
+            for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
+              tma_load_2d(stage_ptr(s) + bx * NT * 128, tmb, kc * C::STAGE_K + bx * 64, ti.row0, &full[s]);
+          }
 #pragma unroll
           for (int m = 0; m < C::MATS; ++m) {
             uint8_t* wt = wtile_ptr(s, m);
-            // gate/up: matrix m at the tile's rows; down: the one matrix, row block m
+            // gate/up: matrix m at the tile's rows; down: the one matrix, row block m; a pair's
+            // CTA r takes the 128-row half r of the tile
             const CUtensorMap* tw = dn_fused ? &p.tm_w_dn[ti.group] : &p.tm_w[ti.group][dn ? 0 : m];
             const CUtensorMap* ts = dn_fused ? &p.tm_s_dn[ti.group] : &p.tm_s[ti.group][dn ? 0 : m];
-            const int wr = dn ? wrow + m * kMTile : wrow;
+            const int wr = wrow + (dn ? m * kMTile : 0) + (int)rank * kMTile;
             if constexpr (WT == WT_Q4_K) {
               tma_load_2d_hint(wt, tw, kc * 144, wr, &full[s], pol_w);
             } else if constexpr (WT == WT_Q8_0) {
@@ -429,13 +489,16 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     // k-block's MMAs as one straight-line block. Issued this way a kind::f16 M=128 MMA costs
     // 24 / 32 / 64 cycles at N = 32 / 64 / 128; issued from a lane-0-only branch it costs
     // 46 cycles or more even at N <= 64, and a run-time branch between two MMAs about 100.
-    constexpr uint32_t idesc = idesc_f16_f32(128, NT);
+    // PAIR: only the leader's warp issues; its MMAs read both CTAs' A (TMEM) and B (shared
+    // memory) halves at the same addresses and write both CTAs' accumulators, and its commits
+    // arrive on the barriers of both CTAs (mask 0b11).
+    constexpr uint32_t idesc = idesc_f16_f32(C::PAIR ? 256 : 128, NT);
     uint32_t stage_seq = 0, tile_seq = 0;
-    for (int t = blockIdx.x; t < total && !warp_abort(abort_flag); t += gridDim.x) {
+    for (int t = t_first; t < total && !warp_abort(abort_flag) && (!C::PAIR || rank == 0); t += t_step) {
       const TileInfo ti = decode_tile<MODE, NT>(p, t);
       const int ab = tile_seq % C::ACC_BUFS;
       const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
-      if (!warp_role_wait(&accempty[ab], aph ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) break;
+      if (!wbwait(&accempty[ab], aph ^ 1u, ERRBIT_TIMEOUT_TMEM)) break;
       tc_fence_after();
       const uint32_t dbase = tbase + ab * C::ACC_COLS;
       bool first = true;
@@ -443,7 +506,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
       for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
         const int s = stage_seq % C::STAGES;
         const uint32_t ph = (stage_seq / C::STAGES) & 1u;
-        if (!warp_role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
+        if (!wbwait(C::PAIR ? &full_b[s] : &full[s], ph, ERRBIT_TIMEOUT_FULL)) { ok = false; break; }
         tc_fence_after();
         // Shared-memory descriptors are built once per stage; each (k-block, k-step) slice adds
         // a compile-time offset to the 14-bit start-address field (no carry: smem < 256 KB).
@@ -455,18 +518,24 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
             const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
             const int a = kbs % C::NA;
             const uint32_t u = kbs / C::NA;
-            if (!warp_role_wait(&afull[a], u & 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
+            if (!wbwait(&afull[a], u & 1u, ERRBIT_TIMEOUT_TMEM)) { ok = false; break; }
             tc_fence_after();
             const uint32_t abuf = tbase + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
             if (elect_one()) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const uint64_t bdesc = bdesc0 + (uint64_t)(((kb * 2 + j / 4) * (NT * 128) + (j % 4) * 32) >> 4);
+                const uint64_t bdesc = bdesc0 + (uint64_t)(((kb * 2 + j / 4) * (C::B_ROWS * 128) + (j % 4) * 32) >> 4);
                 const uint32_t acc = (kb == 0 && j == 0) ? acc_first : 1u;
 #pragma unroll
-                for (int m = 0; m < C::MATS; ++m) mma_f16_ts(dbase + m * NT, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
+                for (int m = 0; m < C::MATS; ++m) {
+                  if constexpr (C::PAIR)
+                    mma_f16_ts_pair(dbase + m * NT, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
+                  else
+                    mma_f16_ts(dbase + m * NT, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
+                }
               }
-              mma_commit(&aempty[a]);
+              if constexpr (C::PAIR) mma_commit_pair(&aempty[a], 3);
+              else mma_commit(&aempty[a]);
             }
             __syncwarp();
           }
@@ -490,12 +559,18 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
           __syncwarp();
         }
         first = false;
-        if (elect_one()) mma_commit(&empty[s]);
+        if (elect_one()) {
+          if constexpr (C::PAIR) mma_commit_pair(&empty[s], 3);
+          else mma_commit(&empty[s]);
+        }
         __syncwarp();
         ++stage_seq;
       }
       if (!ok) break;
-      if (elect_one()) mma_commit(&accfull[ab]);
+      if (elect_one()) {
+        if constexpr (C::PAIR) mma_commit_pair(&accfull[ab], 3);
+        else mma_commit(&accfull[ab]);
+      }
       __syncwarp();
       ++tile_seq;
     }
@@ -510,7 +585,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     const int cb = ((warp - C::EPI_WARP0) >> 2) * HC;  // first accumulator column of this warp
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint32_t tile_seq = 0;
-    for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+    for (int t = t_first; t < total && !*abort_flag; t += t_step) {
       const TileInfo ti = decode_tile<MODE, NT>(p, t);
       const int ab = tile_seq % C::ACC_BUFS;
       const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
@@ -523,12 +598,58 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
         wv[j] = routed ? p.pair_w[ti.row0 + c] : 1.0f;
         tv[j] = (routed && p.y == nullptr) ? p.pair_tok[ti.row0 + c] : ti.row0 + c;
       }
-      if (!role_wait(&accfull[ab], aph, p.err, ERRBIT_TIMEOUT_MMA, abort_flag)) break;
+      if (!bwait(&accfull[ab], aph, ERRBIT_TIMEOUT_MMA)) break;
       tc_fence_after();
       const uint32_t dbase = tbase + lane_off + ab * C::ACC_COLS;
-      const int obase = ti.mt * C::out_rows(ti.mode) + quarter * 32;  // first output feature of this warp
+      // first output feature of this warp (a pair's CTA r holds rows [128 r, 128 r + 128) of the tile)
+      const int obase = ti.mt * C::out_rows(ti.mode) + (int)rank * kMTile + quarter * 32;
+      bool released = false;
+      if (ti.mode == MODE_GATEUP && p.gu_acc == nullptr) {
+        // h = silu(g) * u for this warp's columns, kept as packed halves: the accumulator is
+        // released before the stores, so the next tile's MMAs (single-buffered accumulators at
+        // NT = 128) overlap them
+        uint32_t hv[NCH][8];
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
+        for (int ch = 0; ch < NCH; ++ch) {
+          const int c0 = cb + 16 * ch;
+          if (c0 < ti.nrows) {  // warp-uniform
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {  // 8 columns at a time keeps g and u in 16 registers
+              uint32_t g[8], u[8];
+              tmem_ld8(dbase + c0 + 8 * hh, g);
+              tmem_ld8(dbase + NT + c0 + 8 * hh, u);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 8; c += 2) {
+                const float h0 = silu_f(__uint_as_float(g[c])) * __uint_as_float(u[c]);
+                const float h1 = silu_f(__uint_as_float(g[c + 1])) * __uint_as_float(u[c + 1]);
+                hv[ch][4 * hh + c / 2] = as_u32(__floats2half2_rn(h0, h1));
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (C::PAIR) mbar_arrive_cluster(leader(&accempty[ab]));
+          else mbar_arrive(&accempty[ab]);
+        }
+        released = true;
+        // into the (possibly quad-swapped) h row: one 64-byte segment of a token's row per store
+        const int pl = ((p.h_quad_swap >> ti.group) & 1) ? quad_swap(lane) : lane;
+        __half* hcol = p.hbuf + (int64_t)(ti.row0 + cb) * p.h_ld + obase + pl;
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) {
+          if (cb + 16 * ch >= ti.nrows) break;
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            if (cb + 16 * ch + c < ti.nrows)
+              hcol[(int64_t)(16 * ch + c) * p.h_ld] =
+                  __ushort_as_half((unsigned short)((c & 1) ? (hv[ch][c / 2] >> 16) : (hv[ch][c / 2] & 0xffffu)));
+        }
+      }
+#pragma unroll
+      for (int ch = 0; ch < NCH && !released; ++ch) {
         const int c0 = cb + 16 * ch;
         if (c0 >= ti.nrows) break;  // warp-uniform
         if (ti.mode == MODE_GATEUP) {
@@ -537,25 +658,15 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
           uint32_t acc1[16];
           tmem_ld16(dbase + NT + c0, acc1);
           tmem_wait_ld();
+          // split-K: fp32 partial sums of g and u
           const int64_t r0 = ti.row0 + c0;
-          if (p.gu_acc == nullptr) {
-            // h = silu(g) * u into the (possibly quad-swapped) h row
-            const int pl = ((p.h_quad_swap >> ti.group) & 1) ? quad_swap(lane) : lane;
-            __half* hcol = p.hbuf + r0 * p.h_ld + obase + pl;
+          float* gcol = p.gu_acc + r0 * (2 * p.gu_half) + obase + lane;
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
-              if (c0 + c < ti.nrows)
-                hcol[(int64_t)c * p.h_ld] = __float2half_rn(silu_f(__uint_as_float(acc0[c])) * __uint_as_float(acc1[c]));
-          } else {
-            // split-K: fp32 partial sums of g and u
-            float* gcol = p.gu_acc + r0 * (2 * p.gu_half) + obase + lane;
-#pragma unroll
-            for (int c = 0; c < 16; ++c)
-              if (c0 + c < ti.nrows) {
-                atomicAdd(gcol + (int64_t)c * (2 * p.gu_half), __uint_as_float(acc0[c]));
-                atomicAdd(gcol + (int64_t)c * (2 * p.gu_half) + p.gu_half, __uint_as_float(acc1[c]));
-              }
-          }
+          for (int c = 0; c < 16; ++c)
+            if (c0 + c < ti.nrows) {
+              atomicAdd(gcol + (int64_t)c * (2 * p.gu_half), __uint_as_float(acc0[c]));
+              atomicAdd(gcol + (int64_t)c * (2 * p.gu_half) + p.gu_half, __uint_as_float(acc1[c]));
+            }
         } else {
 #pragma unroll 1
          for (int m = 0; m < C::MATS; ++m) {  // row block m: accumulator columns [m NT, (m + 1) NT)
@@ -599,9 +710,14 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
         __syncwarp();
         if (lane == 0) atomicAdd(p.tt_done + ti.ttx, 1);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&accempty[ab]);
+      if (!released) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (C::PAIR) mbar_arrive_cluster(leader(&accempty[ab]));
+          else mbar_arrive(&accempty[ab]);
+        }
+      }
       ++tile_seq;
     }
   } else if constexpr (C::QUANT) {
@@ -612,19 +728,19 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint32_t stage_seq = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok && !*abort_flag; t += gridDim.x) {
+    for (int t = t_first; t < total && ok && !*abort_flag; t += t_step) {
       const TileInfo ti = decode_tile<MODE, NT>(p, t);
       for (int kc = ti.k0; kc < ti.k1; ++kc) {
         const int s = stage_seq % C::STAGES;
         const uint32_t ph = (stage_seq / C::STAGES) & 1u;
-        if (!role_wait(&full[s], ph, p.err, ERRBIT_TIMEOUT_FULL, abort_flag)) { ok = false; break; }
+        if (!bwait(&full[s], ph, ERRBIT_TIMEOUT_FULL)) { ok = false; break; }
 #pragma unroll
         for (int kb = 0; kb < C::KB_PER_STAGE; ++kb) {
           const uint32_t kbs = stage_seq * C::KB_PER_STAGE + kb;
           if ((int)(kbs % C::NDQ) != wg) continue;
           const int a = kbs % C::NA;
           const uint32_t u = kbs / C::NA;
-          if (!role_wait(&aempty[a], (u & 1u) ^ 1u, p.err, ERRBIT_TIMEOUT_TMEM, abort_flag)) { ok = false; break; }
+          if (!bwait(&aempty[a], (u & 1u) ^ 1u, ERRBIT_TIMEOUT_TMEM)) { ok = false; break; }
           tc_fence_after();
           const uint32_t abuf = tbase + lane_off + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
 #pragma unroll
@@ -639,7 +755,10 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[a]);
+          if (lane == 0) {
+            if constexpr (C::PAIR) mbar_arrive_cluster(leader(&afull[a]));  // the leader's MMAs read it
+            else mbar_arrive(&afull[a]);
+          }
         }
         if (!ok) break;
         __syncwarp();
@@ -652,79 +771,125 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_>::THREADS, 1)
   // ---------------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  // PAIR: the leader's MMAs write the peer's TMEM and arrive on its barriers, and the peer's
+  // copies count on the leader's barriers: neither CTA releases TMEM or exits before both are done
+  if constexpr (C::PAIR) cluster_sync();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tbase, 512);
+    if constexpr (C::PAIR) tmem_dealloc_pair(tbase, 512);
+    else tmem_dealloc(tbase, 512);
   }
 }
 
 // ------------------------------------------------------------------------------------------
 // launcher
 // ------------------------------------------------------------------------------------------
-template <int WT, int MODE, int NT, int NDQ>
+template <int WT, int MODE, int NT, int NDQ, bool PAIR>
 static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t st) {
-  using C = GemmCfg<WT, MODE, NT, NDQ>;
-  auto kern = moe_gemm_kernel<WT, MODE, NT, NDQ>;
+  using C = GemmCfg<WT, MODE, NT, NDQ, PAIR>;
+  auto kern = moe_gemm_kernel<WT, MODE, NT, NDQ, PAIR>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, st, p);
+  if constexpr (!PAIR) {
+    return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, st, p);
+  } else {
+    // clusters of two CTAs; as many pairs as can be resident at once (the tile walk assumes a
+    // persistent grid), counted once per instantiation
+    static int max_pairs = 0;
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    if (max_pairs == 0) {
+      cfg.gridDim = dim3(grid & ~1);
+      cfg.numAttrs = 1;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return e;
+      if (n < 1) return cudaErrorInvalidConfiguration;
+      max_pairs = n;
+    }
+    cfg.gridDim = dim3(2 * std::min(grid / 2, max_pairs));
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+  }
 }
 
 // Launches with `ndq` dequant warpgroups when that configuration keeps NA >= NDQ, otherwise
 // with the largest smaller one that does (2 always does).
-template <int WT, int MODE, int NT>
+template <int WT, int MODE, int NT, bool PAIR = false>
 static cudaError_t launch_ndq(const GemmParams& p, int ndq, int grid, cudaStream_t st) {
   if constexpr (WT == WT_F16) {
-    return launch_one<WT, MODE, NT, 2>(p, grid, st);
+    return launch_one<WT, MODE, NT, 2, false>(p, grid, st);
   } else {
-    if constexpr (GemmCfg<WT, MODE, NT, 4>::RING_OK) {
-      if (ndq >= 4) return launch_one<WT, MODE, NT, 4>(p, grid, st);
+    if constexpr (GemmCfg<WT, MODE, NT, 4, PAIR>::RING_OK) {
+      if (ndq >= 4) return launch_one<WT, MODE, NT, 4, PAIR>(p, grid, st);
     }
-    if constexpr (GemmCfg<WT, MODE, NT, 3>::RING_OK) {
-      if (ndq >= 3) return launch_one<WT, MODE, NT, 3>(p, grid, st);
+    if constexpr (GemmCfg<WT, MODE, NT, 3, PAIR>::RING_OK) {
+      if (ndq >= 3) return launch_one<WT, MODE, NT, 3, PAIR>(p, grid, st);
     }
-    return launch_one<WT, MODE, NT, 2>(p, grid, st);
+    return launch_one<WT, MODE, NT, 2, PAIR>(p, grid, st);
   }
 }
 
 template <int WT, int MODE>
-static cudaError_t launch_nt(const GemmParams& p, int nt, int ndq, int grid, cudaStream_t st) {
+static cudaError_t launch_nt(const GemmParams& p, int nt, int ndq, bool pair, int grid, cudaStream_t st) {
   switch (nt) {
     case 32: return launch_ndq<WT, MODE, 32>(p, ndq, grid, st);
     case 64: return launch_ndq<WT, MODE, 64>(p, ndq, grid, st);
     case 128:
-      if constexpr (MODE != MODE_FUSED) return launch_ndq<WT, MODE, 128>(p, ndq, grid, st);
+      if constexpr (MODE != MODE_FUSED) {
+        if constexpr (WT != WT_F16) {
+          if (pair) return launch_ndq<WT, MODE, 128, true>(p, ndq, grid, st);
+        }
+        return launch_ndq<WT, MODE, 128>(p, ndq, grid, st);
+      }
       return cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, const GemmParams& p, int grid, cudaStream_t st) {
+cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, bool pair, const GemmParams& p, int grid,
+                            cudaStream_t st) {
+  if (pair && !gemm_pair_ok(wtype, mode, nt)) return cudaErrorInvalidValue;
   if (mode == MODE_GATEUP) {
     switch (wtype) {
-      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_GATEUP>(p, nt, ndq, grid, st);
-      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_GATEUP>(p, nt, ndq, grid, st);
-      case WT_F16: return launch_nt<WT_F16, MODE_GATEUP>(p, nt, ndq, grid, st);
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_GATEUP>(p, nt, ndq, pair, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_GATEUP>(p, nt, ndq, pair, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_GATEUP>(p, nt, ndq, pair, grid, st);
     }
   } else if (mode == MODE_FUSED) {
     switch (wtype) {
-      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_FUSED>(p, nt, ndq, grid, st);
-      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_FUSED>(p, nt, ndq, grid, st);
-      case WT_F16: return launch_nt<WT_F16, MODE_FUSED>(p, nt, ndq, grid, st);
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_FUSED>(p, nt, ndq, pair, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_FUSED>(p, nt, ndq, pair, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_FUSED>(p, nt, ndq, pair, grid, st);
     }
   } else {
     switch (wtype) {
-      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_DOWN>(p, nt, ndq, grid, st);
-      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_DOWN>(p, nt, ndq, grid, st);
-      case WT_F16: return launch_nt<WT_F16, MODE_DOWN>(p, nt, ndq, grid, st);
+      case WT_Q4_K: return launch_nt<WT_Q4_K, MODE_DOWN>(p, nt, ndq, pair, grid, st);
+      case WT_Q8_0: return launch_nt<WT_Q8_0, MODE_DOWN>(p, nt, ndq, pair, grid, st);
+      case WT_F16: return launch_nt<WT_F16, MODE_DOWN>(p, nt, ndq, pair, grid, st);
     }
   }
   return cudaErrorInvalidValue;
 }
 
+bool gemm_pair_ok(int wtype, int mode, int nt) { return wtype != WT_F16 && mode != MODE_FUSED && nt == 128; }
+
 int gemm_stage_k(int wtype) { return wtype == WT_Q4_K ? 256 : 128; }
 
-int gemm_out_rows(int mode, int nt) { return mode == MODE_GATEUP ? kMTile : (nt <= 64 ? 2 * kMTile : kMTile); }
+int gemm_out_rows(int mode, int nt, bool pair) {
+  if (pair) return 2 * kMTile;
+  return mode == MODE_GATEUP ? kMTile : (nt <= 64 ? 2 * kMTile : kMTile);
+}
 
 }  // namespace dmoe

@@ -18,13 +18,13 @@ F16, Q8_0, Q4_K = 1, 8, 12
 GATEUP, DOWN = 0, 1
 
 
-def gemm_cfg(wt, mode, nt, ndq):
-    """Restates GemmCfg<WT, MODE, NT, NDQ> (stage ring, TMEM ring) from moe_gemm.cu."""
+def gemm_cfg(wt, mode, nt, ndq, pair=False):
+    """Restates GemmCfg<WT, MODE, NT, NDQ, PAIR> (stage ring, TMEM ring) from moe_gemm.cu."""
     quant = wt != F16
     mats = 2 if (mode == GATEUP or nt <= 64) else 1  # down at NT <= 64: two 128-row blocks
     stage_k = 256 if wt == Q4_K else 128
     kb = stage_k // 128
-    b_bytes = stage_k * nt * 2
+    b_bytes = stage_k * (nt // 2 if pair else nt) * 2  # a pair's CTA loads half the token rows
     w_bytes = 128 * 144 if wt == Q4_K else (128 * 128 + 128 * 16 if wt == Q8_0 else 128 * 128 * 2)
     stage_bytes = b_bytes + mats * w_bytes
     stages = min(6, (227 * 1024 - 2048) // stage_bytes)
@@ -116,9 +116,90 @@ def roles(cfg, tiles):
     return rs
 
 
-def run(cfg, tiles, seed):
+def roles_pair(cfg, tiles):
+    """The CTA pair (PAIR = true): each CTA runs a producer, its dequant warpgroups and its
+    epilogue; the leader's MMA warp alone issues. Arrivals that cross the pair: both producers'
+    activation halves on the leader's full_b, both CTAs' dequant warps on the leader's afull, both
+    epilogues on the leader's accempty; the leader's commits arrive on aempty / empty / accfull
+    of both CTAs."""
+    S, NA, NDQ, KB, ACCB = cfg["stages"], max(cfg["na"], 1), cfg["ndq"], cfg["kb"], cfg["acc_bufs"]
+    cta = []
+    for r in range(2):
+        cta.append(dict(
+            full=[Bar(f"full{i}.{r}", 1) for i in range(S)],
+            empty=[Bar(f"empty{i}.{r}", 1 + 4 * NDQ) for i in range(S)],
+            aempty=[Bar(f"aempty{i}.{r}", 1) for i in range(NA)],
+            accfull=[Bar(f"accfull{i}.{r}", 1) for i in range(ACCB)],
+        ))
+    full_b = [Bar(f"full_b{i}", 2) for i in range(S)]  # both halves' bytes (leader's barrier)
+    afull = [Bar(f"afull{i}", 8) for i in range(NA)]
+    accempty = [Bar(f"accempty{i}", 8) for i in range(ACCB)]
+
+    def producer(r):
+        seq = 0
+        for t in tiles:
+            for _ in range(t):
+                s = seq % S
+                yield cta[r]["empty"][s], seq // S
+                cta[r]["full"][s].arrive()  # this CTA's weight tile
+                full_b[s].arrive()          # this CTA's activation half, counted by the leader
+                seq += 1
+
+    def mma():
+        seq = tseq = 0
+        for t in tiles:
+            ab = tseq % ACCB
+            yield accempty[ab], tseq // ACCB
+            for _ in range(t):
+                s = seq % S
+                yield full_b[s], seq // S + 1
+                for kb in range(KB):
+                    kbs = seq * KB + kb
+                    a, u = kbs % NA, kbs // NA
+                    yield afull[a], u + 1
+                    for r in range(2):
+                        cta[r]["aempty"][a].arrive()
+                for r in range(2):
+                    cta[r]["empty"][s].arrive()
+                seq += 1
+            for r in range(2):
+                cta[r]["accfull"][ab].arrive()
+            tseq += 1
+
+    def epilogue(r):
+        tseq = 0
+        for t in tiles:
+            ab = tseq % ACCB
+            yield cta[r]["accfull"][ab], tseq // ACCB + 1
+            accempty[ab].arrive()
+            tseq += 1
+
+    def dequant(r, g):
+        seq = 0
+        for t in tiles:
+            for _ in range(t):
+                s = seq % S
+                yield cta[r]["full"][s], seq // S + 1
+                for kb in range(KB):
+                    kbs = seq * KB + kb
+                    if kbs % NDQ != g:
+                        continue
+                    a, u = kbs % NA, kbs // NA
+                    yield cta[r]["aempty"][a], u
+                    afull[a].arrive()
+                cta[r]["empty"][s].arrive()
+                seq += 1
+
+    rs = [mma()]
+    for r in range(2):
+        rs += [producer(r)] + [epilogue(r) for _ in range(4)]
+        rs += [dequant(r, g) for g in range(NDQ) for _ in range(4)]
+    return rs
+
+
+def run(cfg, tiles, seed, pair=False):
     rng = random.Random(seed)
-    rs = roles(cfg, tiles)
+    rs = roles_pair(cfg, tiles) if pair else roles(cfg, tiles)
     cur = [None] * len(rs)
     alive = set(range(len(rs)))
     while alive:
@@ -167,4 +248,23 @@ def test_model_catches_a_short_ring():
     # fewer A buffers than dequant warpgroups: a group can wait two completions ahead
     cfg = dict(stages=4, na=3, ndq=4, kb=2, acc_bufs=2, quant=True, ring_ok=False)
     results = [run(cfg, [16, 16, 16], seed) for seed in range(25)]
+    assert any(r and "alias" in r for r in results)
+
+
+PAIR_LAUNCHABLE = [(wt, mode, ndq) for wt, mode, ndq in itertools.product([Q8_0, Q4_K], [GATEUP, DOWN], [2, 3, 4])
+                   if gemm_cfg(wt, mode, 128, ndq, pair=True)["ring_ok"]]
+
+
+@pytest.mark.parametrize("wt,mode,ndq", PAIR_LAUNCHABLE)
+def test_pair_configs_are_safe(wt, mode, ndq):
+    cfg = gemm_cfg(wt, mode, 128, ndq, pair=True)
+    assert cfg["stages"] >= 2 and cfg["na"] >= 2
+    for tiles in ([16, 16, 16], [3, 1, 2], [1, 1, 1, 1, 1]):
+        for seed in range(8):
+            assert run(cfg, tiles, seed, pair=True) is None, (cfg, tiles, seed)
+
+
+def test_pair_model_catches_a_short_ring():
+    cfg = dict(stages=3, na=2, ndq=4, kb=2, acc_bufs=1, quant=True, ring_ok=False)
+    results = [run(cfg, [16, 16], seed, pair=True) for seed in range(25)]
     assert any(r and "alias" in r for r in results)
