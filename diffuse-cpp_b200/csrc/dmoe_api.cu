@@ -732,19 +732,45 @@ dmoe_status ep_experts(dmoe_layer* L, cudaStream_t st, const float* xd, int64_t 
 // least 4096 tokens, and only where chunking cannot change the routing: chunks are whole routing
 // blocks when the call uses block routing, and a call that does not (n % block != 0) is not
 // chunked if a chunk of whole blocks would switch block routing on.
-int64_t host_chunk_tokens(const dmoe_layer* L, int64_t n, bool host, const dmoe_route_out* route, uint32_t flags) {
+// Chunk plan of a host-buffer call (0 chunks: one unchunked call). The copies share PCIe (about
+// 51 GB/s one way, 77 GB/s both ways at once, measured on B200) and a chunk's compute costs more
+// per token the smaller it is, so the plan starts small (its upload is exposed), grows while
+// earlier chunks compute, and ends small (its download is exposed): five chunks in proportions
+// 2:4:6:3:1 up to 8192 tokens, six in 1:2:4:4:2:1 above, each a multiple of 8 routing blocks.
+// Modelled from the measured per-size layer times, this takes 256 x 32 tokens from 5.6 to 5.2 ms
+// against four equal chunks. DMOE_HOST_CHUNK = t forces equal chunks of t tokens (0: never chunk).
+int host_chunk_plan(const dmoe_layer* L, int64_t n, bool host, const dmoe_route_out* route, uint32_t flags,
+                    int64_t (&sizes)[dmoe_layer::kMaxChunks]) {
   if (!host || route || (flags & (DMOE_F_ROUTE_ONLY | DMOE_F_PROFILE)) || L->world > 1) return 0;
-  const int64_t target = env_int("DMOE_HOST_CHUNK", 2048);
-  if (target <= 0 || n < 2 * target) return 0;
+  const int forced = env_int("DMOE_HOST_CHUNK", -1);
+  const int64_t threshold = forced > 0 ? 2 * (int64_t)forced : 4096;
+  if (forced == 0 || n < threshold) return 0;
   const bool block_possible = L->blk > 1 && L->cap > 0 && L->cap < L->E;
-  int64_t chunk = target;
-  if (block_possible) {
-    if (n % L->blk) return 0;
-    chunk = std::max<int64_t>(L->blk, target / L->blk * L->blk);
+  if (block_possible && n % L->blk) return 0;
+  const int64_t unit = block_possible ? L->blk : 32;  // chunks hold whole routing blocks
+  int nc = 0;
+  if (forced > 0) {
+    int64_t chunk = std::max<int64_t>(unit, forced / unit * unit);
+    if ((n + chunk - 1) / chunk > dmoe_layer::kMaxChunks)
+      chunk = ((n + dmoe_layer::kMaxChunks - 1) / dmoe_layer::kMaxChunks + unit - 1) / unit * unit;
+    for (int64_t t0 = 0; t0 < n; t0 += chunk) sizes[nc++] = std::min(chunk, n - t0);
+    return nc;
   }
-  if ((n + chunk - 1) / chunk > dmoe_layer::kMaxChunks) chunk = (n + dmoe_layer::kMaxChunks - 1) / dmoe_layer::kMaxChunks;
-  if (block_possible) chunk = (chunk + L->blk - 1) / L->blk * L->blk;
-  return chunk;
+  static constexpr int kW5[] = {2, 4, 6, 3, 1}, kW6[] = {1, 2, 4, 4, 2, 1};
+  const bool small = n <= 8192;
+  const int* w = small ? kW5 : kW6;
+  const int nw = small ? 5 : 6, wsum = 16, biggest = 2;
+  const int64_t g = 8 * unit;
+  int64_t rest = n;
+  for (int i = 0; i < nw; ++i) {
+    sizes[i] = std::max<int64_t>(g, (n * w[i] / wsum + g / 2) / g * g);
+    rest -= sizes[i];
+  }
+  sizes[biggest] += rest;  // the remainder (a multiple of the unit) goes to the largest chunk
+  if (sizes[biggest] < 0) return 0;
+  for (int i = 0; i < nw; ++i)
+    if (sizes[i] > 0) sizes[nc++] = sizes[i];
+  return nc;
 }
 
 }  // namespace
@@ -759,7 +785,8 @@ namespace {
 // Host-buffer call in chunks: H2D of every chunk on h2d_stream, each chunk's layer on the layer's
 // stream once its input has landed, the D2H of its output on d2h_stream once it is computed.
 // The statistics describe the last chunk.
-dmoe_status forward_chunked(dmoe_layer* L, const float* x, int64_t n, float* out, int64_t chunk, uint32_t flags) {
+dmoe_status forward_chunked(dmoe_layer* L, const float* x, int64_t n, float* out, const int64_t* sizes, int nc,
+                            uint32_t flags) {
   const int64_t H = L->H;
   dmoe_status s;
   if ((s = grow(L->xdev, L->xdev_cap, (size_t)n * H)) != DMOE_OK) return s;
@@ -769,15 +796,17 @@ dmoe_status forward_chunked(dmoe_layer* L, const float* x, int64_t n, float* out
   DMOE_CUDA(cudaEventRecord(L->ev_start, ks));
   DMOE_CUDA(cudaStreamWaitEvent(L->h2d_stream, L->ev_start, 0));
   DMOE_CUDA(cudaStreamWaitEvent(L->d2h_stream, L->ev_start, 0));
-  const int nc = (int)((n + chunk - 1) / chunk);
+  int64_t starts[dmoe_layer::kMaxChunks];
+  for (int64_t c = 0, t0 = 0; c < nc; t0 += sizes[c], ++c) starts[c] = t0;
+  if (starts[nc - 1] + sizes[nc - 1] != n) return fail(DMOE_ERR_INVALID_ARG, "chunk plan does not cover the call");
   for (int c = 0; c < nc; ++c) {
-    const int64_t t0 = c * chunk, cn = std::min(chunk, n - t0);
+    const int64_t t0 = starts[c], cn = sizes[c];
     DMOE_CUDA(cudaMemcpyAsync(L->xdev + t0 * H, x + t0 * H, (size_t)cn * H * 4, cudaMemcpyHostToDevice, L->h2d_stream));
     DMOE_CUDA(cudaEventRecord(L->ev_in[c], L->h2d_stream));
   }
   int kernels = 0;
   for (int c = 0; c < nc; ++c) {
-    const int64_t t0 = c * chunk, cn = std::min(chunk, n - t0);
+    const int64_t t0 = starts[c], cn = sizes[c];
     DMOE_CUDA(cudaStreamWaitEvent(ks, L->ev_in[c], 0));
     if ((s = dmoe_forward(L, L->xdev + t0 * H, cn, L->odev + t0 * H, nullptr, ks, flags & ~DMOE_F_HOST_PTRS)) != DMOE_OK)
       return s;
@@ -1006,8 +1035,11 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   set_pdl_for_call(n < 1024);
   std::memset(&L->stats, 0, sizeof(L->stats));
   if (n == 0) return DMOE_OK;
-  if (const int64_t chunk = host_chunk_tokens(L, n, host, route, flags); chunk > 0)
-    return forward_chunked(L, x, n, out, chunk, flags);
+  {
+    int64_t sizes[dmoe_layer::kMaxChunks];
+    if (const int nc = host_chunk_plan(L, n, host, route, flags, sizes); nc > 0)
+      return forward_chunked(L, x, n, out, sizes, nc, flags);
+  }
 
   const int64_t H = L->H, E = L->E, K = L->K;
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;

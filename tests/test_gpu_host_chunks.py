@@ -17,7 +17,7 @@ from test_gpu_parity import rel_l2
 def test_chunked_host_call_matches_device_call():
     spec = synth.config("c2")  # S shape, q8_0
     L = dm.MoELayer(spec.hparams(), synth.make_layer(spec))
-    n = 6144  # three 2048-token chunks
+    n = 6144  # five chunks of 24 to 64 routing blocks
     x = synth.make_input(n, spec.H, 13)
     xd = torch.from_numpy(x).cuda()
     dev_det = L.forward(xd, deterministic=True)
