@@ -270,7 +270,8 @@ dmoe_status validate(const dmoe_layer_desc* d) {
 }
 
 // Tuning overrides (DMOE_NT = 32 / 64 / 128, DMOE_KSPLIT_GU / DMOE_KSPLIT_DN = 1 / 2 / 4 / 8,
-// DMOE_ROUTER_SPLIT = 0 / 1, DMOE_COMBINE_MIN = tokens); unset or invalid values keep the
+// DMOE_ROUTER_SPLIT = 0 whole-K / 1 split 32-token tiles / 2 split 128-token tiles,
+// DMOE_COMBINE_MIN = tokens); unset or invalid values keep the
 // automatic choice.
 int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
@@ -320,15 +321,17 @@ int pick_ksplit(int64_t tiles_est, int sms, std::initializer_list<int> kstages) 
   return best;
 }
 
-// CTA-pair GEMM tiles (256 output rows per tile, one activation tile per two SMs): quantised
-// weights at NT = 128, every expert matrix a multiple of 256 rows. DMOE_PAIR = 0 / 1 overrides.
-bool use_pair(const dmoe_layer* L, int nt) {
-  const int forced = env_int("DMOE_PAIR", -1);
-  if (forced == 0) return false;
+// CTA-pair GEMM tiles (256 output rows per tile, each activation tile loaded half by each CTA of
+// a two-SM cluster): quantised weights at NT = 128, every expert matrix a multiple of 256 rows.
+// Measured on B200 (c3, 8192 tokens): gate/up 1434 -> 1218 us with pairs, down 997 -> 1077 us
+// (its single-matrix tiles already double-buffer the accumulators), so gate/up only by default.
+// DMOE_PAIR = 0: off; 1: gate/up; 2: gate/up and down.
+bool use_pair(const dmoe_layer* L, int nt, int mode) {
+  const int v = env_int("DMOE_PAIR", 1);
+  if (v <= 0 || (mode == MODE_DOWN && v < 2)) return false;
   const bool quant = L->etype != DMOE_TYPE_F16 && (!L->has_shared || L->stype != DMOE_TYPE_F16);
   const bool rows256 = L->I % 256 == 0 && L->H % 256 == 0 && (!L->has_shared || L->Is % 256 == 0);
-  if (!(quant && rows256 && gemm_pair_ok(L->etype, MODE_GATEUP, nt))) return false;
-  return forced == 1;
+  return quant && rows256 && gemm_pair_ok(L->etype, mode, nt);
 }
 
 // n_out_rows / rows_per_tile output tiles per expert (gate/up tiles cover 128 rows of each of the
@@ -356,15 +359,14 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   const int64_t Imax = std::max(L->I, L->Is);
   const int64_t E_here = L->world > 1 ? L->e_local : L->E;
   dmoe_status s;
-  const bool pair = use_pair(L, nt);
+  const bool pair_gu = use_pair(L, nt, MODE_GATEUP), pair_dn = use_pair(L, nt, MODE_DOWN);
   // activation tiles: NT token rows, or each pair CTA's half of them
-  const uint32_t b_rows = (uint32_t)(pair ? nt / 2 : nt);
   CUtensorMap tm_x, tm_h;
   if ((s = make_map(&tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->xg, (uint64_t)H, (uint64_t)rows, (uint64_t)H * 2, 64,
-                    b_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+                    (uint32_t)(pair_gu ? nt / 2 : nt), CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
     return s;
   if ((s = make_map(&tm_h, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->hbuf, (uint64_t)Imax, (uint64_t)rows,
-                    (uint64_t)Imax * 2, 64, b_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+                    (uint64_t)Imax * 2, 64, (uint32_t)(pair_dn ? nt / 2 : nt), CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
     return s;
   const int64_t pairs = rows - n_sh;
   const int64_t tt_est = std::min<int64_t>(E_here, pairs) + pairs / nt;
@@ -411,13 +413,13 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
     gp.tm_w[0][1] = L->sup.tm_q;
     gp.tm_s[0][0] = L->sgate.tm_s;
     gp.tm_s[0][1] = L->sup.tm_s;
-    fill_group(gp.grp[0], L->sgate, L->stype, L->Is, L->Is, gemm_out_rows(MODE_GATEUP, nt, pair));
+    fill_group(gp.grp[0], L->sgate, L->stype, L->Is, L->Is, gemm_out_rows(MODE_GATEUP, nt, pair_gu));
   }
   gp.tm_w[1][0] = L->gate.tm_q;
   gp.tm_w[1][1] = L->up.tm_q;
   gp.tm_s[1][0] = L->gate.tm_s;
   gp.tm_s[1][1] = L->up.tm_s;
-  fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I, gemm_out_rows(MODE_GATEUP, nt, pair));
+  fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I, gemm_out_rows(MODE_GATEUP, nt, pair_gu));
   const int grid = L->sms;
   // dequant warpgroups per CTA: the largest of 4 / 3 / 2 the TMEM ring allows (measured 2-3 %
   // faster than 2 at 1-8 blocks)
@@ -438,14 +440,14 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   if (fused) {
     // launched below, once the down operands are set
   } else if (same_type) {
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, pair, gp, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, pair_gu, gp, grid, st));
     ++kernels;
   } else {
     GemmParams g0 = gp, g1 = gp;
     g0.grp[1].present = 0;
     g1.grp[0].present = 0;
-    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, ndq, pair, g0, grid, st));
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, pair, g1, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_GATEUP, nt, ndq, pair_gu, g0, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_GATEUP, nt, ndq, pair_gu, g1, grid, st));
     kernels += 2;
   }
   if (ks_gu > 1) {
@@ -481,11 +483,11 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   if (L->has_shared) {
     dp.tm_w[0][0] = L->sdown.tm_q;
     dp.tm_s[0][0] = L->sdown.tm_s;
-    fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair));
+    fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair_dn));
   }
   dp.tm_w[1][0] = L->down.tm_q;
   dp.tm_s[1][0] = L->down.tm_s;
-  fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair));
+  fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair_dn));
   if (fused) {
     GemmParams fp = gp;  // gate/up operands and tiles ...
     fp.tm_b_dn = dp.tm_b;  // ... then the down phase's
@@ -505,14 +507,14 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
     DMOE_CUDA(launch_moe_gemm(L->etype, MODE_FUSED, nt, ndq, false, fp, grid, st));
     ++kernels;
   } else if (same_type) {
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, pair, dp, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, pair_dn, dp, grid, st));
     ++kernels;
   } else {
     GemmParams d0 = dp, d1 = dp;
     d0.grp[1].present = 0;
     d1.grp[0].present = 0;
-    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, pair, d0, grid, st));
-    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, pair, d1, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->stype, MODE_DOWN, nt, ndq, pair_dn, d0, grid, st));
+    DMOE_CUDA(launch_moe_gemm(L->etype, MODE_DOWN, nt, ndq, pair_dn, d1, grid, st));
     kernels += 2;
   }
   if (combine) {
@@ -1044,8 +1046,9 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   const int64_t H = L->H, E = L->E, K = L->K;
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;
   const int nseg = (int)((H + kRouterSeg - 1) / kRouterSeg);
-  bool rl_split = router_split(n, (int)E, L->sms);  // too few whole-K tiles: split by segment
-  if (const int f = env_int("DMOE_ROUTER_SPLIT", -1); f == 0 || f == 1) rl_split = f == 1;
+  RouterPlan rl_plan = router_plan(n, (int)E, (int)H, L->sms);  // too few whole-K tiles: split by segment
+  if (const int f = env_int("DMOE_ROUTER_SPLIT", -1); f >= 0 && f <= 2) rl_plan = (RouterPlan)f;
+  const bool rl_split = rl_plan != ROUTER_WHOLE;
   const int nparts = rl_split ? nseg : 1;
 
   dmoe_status s;
@@ -1084,7 +1087,7 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[0], st));
 
   // ---- router (src/diffuse-moe-graph.cpp:203-262)
-  DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, rl_split, L->arrivals, counts, st));
+  DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, rl_plan, L->arrivals, counts, st));
   ++kernels;
   RouteArgs ra{};
   ra.probs = L->parts;

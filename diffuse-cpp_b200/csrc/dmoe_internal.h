@@ -99,10 +99,13 @@ struct RouteArgs {
   int tok_split;       // CTAs per routing block (set by launch_route)
 };
 
-cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, bool split,
+// router logits launch: whole-K 128-token tiles, or per-256-k-segment partials of 128- or
+// 32-token tiles summed by each tile's last CTA (part[1 ..] and `arrivals` in use)
+enum RouterPlan { ROUTER_WHOLE = 0, ROUTER_SPLIT2 = 1, ROUTER_SPLIT8 = 2 };
+cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, RouterPlan plan,
                           int32_t* arrivals, int32_t* zero_counts, cudaStream_t st);
-bool router_split(int64_t n, int e, int sms);
-int64_t router_arrivals(int64_t n, int e);  // split path: per-tile arrival counters needed
+RouterPlan router_plan(int64_t n, int e, int h, int sms);
+int64_t router_arrivals(int64_t n, int e);  // split plans: per-tile arrival counters needed
 // shared memory of route_kernel for `tpb` tokens per CTA and e experts; at most kRouteSmemMax
 constexpr size_t kRouteSmemMax = 200 * 1024;
 size_t route_smem_bytes(int64_t tpb, int64_t e);

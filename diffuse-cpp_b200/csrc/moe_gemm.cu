@@ -77,6 +77,11 @@ struct GemmCfg {
   static constexpr int NA_RAW = QUANT ? (512 - ACC_BUFS * ACC_COLS) / A_COLS : 0;
   static constexpr int NA = NA_RAW > 4 ? 4 : NA_RAW;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  // gate/up launches: dequant warps convert a k-block's first matrix into 64 registers before
+  // its A buffer is free, where the launch leaves each thread the registers (two dequant
+  // warpgroups: 576 threads, up to 112 registers each). Measured on B200: gate/up 492 -> 471 us
+  // at 64 x 32 tokens; the down launches (their epilogue holds more registers) lost 5-8 %.
+  static constexpr bool PRECONVERT = QUANT && NDQ <= 2 && MODE == MODE_GATEUP;
   // every dequant warp arrives on each stage's `empty` (after its own k-blocks, if any)
   static constexpr int EMPTY_COUNT = 1 + 4 * NDQ;
   static_assert(STAGES >= 2, "smem ring needs two stages");
@@ -231,7 +236,8 @@ __device__ __forceinline__ bool warp_abort(volatile int* abort_flag) {
 // Low nibbles: (q & 0x000F000F) | 0x6400 -> 1024 + q, exact; minus 1024 -> q; fma(q, d, -m).
 // High nibbles: (q & 0x00F000F0) | 0x6400 -> 1024 + 16 q; minus 1024 -> 16 q (exact);
 // fma(16 q, d / 16, -m) with d / 16 an exact power-of-two rescaling of d (no shift needed).
-__device__ __forceinline__ void dequant_q4k_kblock(uint32_t rowp, int kb, uint32_t taddr) {
+// Writes the row's 64 packed halves (TMEM columns 0..63 of the k-block's A block) into v.
+__device__ __forceinline__ void q4k_convert(uint32_t rowp, int kb, uint32_t (&v)[64]) {
   const uint4 hdr = lds128(rowp);
   const __half2 dd = as_h2(__byte_perm(hdr.x, 0, 0x1010));    // {d, d}
   const __half2 dmn = as_h2(__byte_perm(hdr.x, 0, 0x3232));   // {dmin, dmin}
@@ -264,7 +270,7 @@ __device__ __forceinline__ void dequant_q4k_kblock(uint32_t rowp, int kb, uint32
     const __half2 mhi = gl == 0 ? __high2half2(nm01) : __high2half2(nm23);
     const uint4 qa = gl == 0 ? q0 : q2, qb = gl == 0 ? q1 : q3;
     const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    uint32_t lo[16], hi[16];
+    // columns [32 gl, 32 gl + 16): low nibbles; [32 gl + 16, 32 gl + 32): high nibbles
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       const uint32_t q = qw[w], q8 = q >> 8;
@@ -272,19 +278,17 @@ __device__ __forceinline__ void dequant_q4k_kblock(uint32_t rowp, int kb, uint32
       const uint32_t v13 = lop3_and_or(q8, 0x000F000Fu, 0x64006400u);
       const uint32_t h02 = lop3_and_or(q, 0x00F000F0u, 0x64006400u);
       const uint32_t h13 = lop3_and_or(q8, 0x00F000F0u, 0x64006400u);
-      lo[2 * w] = as_u32(__hfma2(__hsub2(as_h2(v02), k1024), dlo, mlo));
-      lo[2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(v13), k1024), dlo, mlo));
-      hi[2 * w] = as_u32(__hfma2(__hsub2(as_h2(h02), k1024), dhi, mhi));
-      hi[2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(h13), k1024), dhi, mhi));
+      v[32 * gl + 2 * w] = as_u32(__hfma2(__hsub2(as_h2(v02), k1024), dlo, mlo));
+      v[32 * gl + 2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(v13), k1024), dlo, mlo));
+      v[32 * gl + 16 + 2 * w] = as_u32(__hfma2(__hsub2(as_h2(h02), k1024), dhi, mhi));
+      v[32 * gl + 16 + 2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(h13), k1024), dhi, mhi));
     }
-    tmem_st16(taddr + 32 * gl, lo);
-    tmem_st16(taddr + 32 * gl + 16, hi);
   }
 }
 
 // q8_0 (repacked): `qtile` = shared address of a 128 x 128 int8 tile (128B-swizzled), `stile` =
 // 128 x 4 fp32 scales.
-__device__ __forceinline__ void dequant_q80_kblock(uint32_t qtile, uint32_t stile, int row, uint32_t taddr) {
+__device__ __forceinline__ void q80_convert(uint32_t qtile, uint32_t stile, int row, uint32_t (&v)[64]) {
   const float4 sc = lds128f(stile + row * 16);
   const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
   const __half2 k1152 = __float2half2_rn(1152.0f);
@@ -293,9 +297,8 @@ __device__ __forceinline__ void dequant_q80_kblock(uint32_t qtile, uint32_t stil
 #pragma unroll
   for (int c = 0; c < 8; ++c) qv8[c] = lds128(rp + ((c ^ (row & 7)) << 4));
 #pragma unroll
-  for (int blk = 0; blk < 4; ++blk) {
+  for (int blk = 0; blk < 4; ++blk) {  // columns [16 blk, 16 blk + 16): 32-quant block blk
     const __half2 d2 = __float2half2_rn(scv[blk]);
-    uint32_t r[16];
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const uint4 qv = qv8[2 * blk + cc];
@@ -305,12 +308,22 @@ __device__ __forceinline__ void dequant_q80_kblock(uint32_t qtile, uint32_t stil
         const uint32_t xq = qw[w] ^ 0x80808080u;
         const uint32_t v0 = __byte_perm(xq, 0x64646464u, 0x5140);
         const uint32_t v1 = __byte_perm(xq, 0x64646464u, 0x5342);
-        r[8 * cc + 2 * w] = as_u32(__hmul2(__hsub2(as_h2(v0), k1152), d2));
-        r[8 * cc + 2 * w + 1] = as_u32(__hmul2(__hsub2(as_h2(v1), k1152), d2));
+        v[16 * blk + 8 * cc + 2 * w] = as_u32(__hmul2(__hsub2(as_h2(v0), k1152), d2));
+        v[16 * blk + 8 * cc + 2 * w + 1] = as_u32(__hmul2(__hsub2(as_h2(v1), k1152), d2));
       }
     }
-    tmem_st16(taddr + 16 * blk, r);
   }
+}
+
+// one weight row's k-block of weight tile `wt` (q4_K super-block rows or a q8_0 tile) as 64 packed halves
+template <int WT>
+__device__ __forceinline__ void convert_kblock(uint32_t wt, int row, int kb, uint32_t (&v)[64]) {
+  if constexpr (WT == WT_Q4_K) q4k_convert(wt + row * 144, kb, v);
+  else q80_convert(wt, wt + 128 * 128, row, v);
+}
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&v)[64]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) tmem_st16(taddr + 16 * j, *reinterpret_cast<const uint32_t(*)[16]>(&v[16 * j]));
 }
 
 // silu(g) = g * (1 / (1 + e^-g)); for g -> -inf the reciprocal of inf is 0 and the product -0
@@ -740,17 +753,17 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
           if ((int)(kbs % C::NDQ) != wg) continue;
           const int a = kbs % C::NA;
           const uint32_t u = kbs / C::NA;
+          // the first matrix is converted while the A buffer may still be in use (PRECONVERT),
+          // so only its TMEM store waits for the buffer
+          uint32_t v[64];
+          if constexpr (C::PRECONVERT) convert_kblock<WT>(smem_u32(wtile_ptr(s, 0)), row, kb, v);
           if (!bwait(&aempty[a], (u & 1u) ^ 1u, ERRBIT_TIMEOUT_TMEM)) { ok = false; break; }
           tc_fence_after();
           const uint32_t abuf = tbase + lane_off + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
 #pragma unroll
           for (int m = 0; m < C::MATS; ++m) {
-            const uint32_t wt = smem_u32(wtile_ptr(s, m));
-            if constexpr (WT == WT_Q4_K) {
-              dequant_q4k_kblock(wt + row * 144, kb, abuf + m * 64);
-            } else {
-              dequant_q80_kblock(wt, wt + 128 * 128, row, abuf + m * 64);
-            }
+            if (!C::PRECONVERT || m > 0) convert_kblock<WT>(smem_u32(wtile_ptr(s, m)), row, kb, v);
+            tmem_st64(abuf + m * 64, v);
           }
           tmem_wait_st();
           tc_fence_before();

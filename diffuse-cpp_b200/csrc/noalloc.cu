@@ -129,7 +129,7 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
   transpose_router_kernel<<<dim3((unsigned)((H + 31) / 32), (unsigned)((E + 31) / 32)), dim3(32, 8), 0, st>>>(
       w_router, wrt, E, H);
   e = cudaGetLastError();
-  if (e == cudaSuccess) e = launch_router(x, wrt, logits, n_tokens, H, E, false, nullptr, counts, st);
+  if (e == cudaSuccess) e = launch_router(x, wrt, logits, n_tokens, H, E, ROUTER_WHOLE, nullptr, counts, st);
   if (e == cudaSuccess) {
     RouteArgs ra{};
     ra.probs = logits;

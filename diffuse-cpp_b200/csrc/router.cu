@@ -70,8 +70,9 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 //                  of a tile to finish (per-tile arrival counter) adds P_0 .. P_{S-1} left to
 //                  right, writes p to part[0] and re-arms the counter (small N, where whole-K
 //                  tiles cannot fill the GPU).
-// TM = 8 for large N (fewer shared-memory reads per fma, the router weight re-read half as often),
-// TM = 2 for small N (more CTAs).
+// TM = 8 for large N (fewer shared-memory reads per fma, the router weight re-read a quarter as
+// often), split by segment while whole-K TM = 8 tiles cannot fill the GPU; TM = 2 split for the
+// smallest N (more CTAs).
 // ------------------------------------------------------------------------------------------
 constexpr int RL_EXP = 64, RL_KC = 32, RL_THREADS = 128;
 constexpr int RL_XP = RL_KC + 4;  // x tile row pitch (floats)
@@ -80,17 +81,18 @@ template <int TM>
 constexpr int rl_tok() { return 16 * TM; }
 template <int TM>
 constexpr int rl_stage_floats() { return rl_tok<TM>() * RL_XP + RL_KC * RL_EXP; }
-// ring depth: the split path prefetches its whole 256-k segment at once (one memory latency
-// instead of eight); the whole-K path keeps a 3-deep ring
-template <bool SPLIT>
-constexpr int rl_stages() { return SPLIT ? kRouterSeg / RL_KC : 3; }
+// ring depth: the TM = 2 split path prefetches its whole 256-k segment at once (one memory
+// latency instead of eight); TM = 8 tiles (four times the shared memory per chunk) keep a 3-deep
+// ring, split or not
+template <int TM, bool SPLIT>
+constexpr int rl_stages() { return (SPLIT && TM <= 2) ? kRouterSeg / RL_KC : 3; }
 // TM = 8 keeps the running segment sums tot in shared memory (expert-major: [TM x 8][thread],
 // conflict-free) instead of 64 more registers
 template <int TM>
 constexpr bool rl_tot_smem() { return TM >= 8; }
 template <int TM, bool SPLIT>
 constexpr int rl_smem() {
-  return rl_stages<SPLIT>() * rl_stage_floats<TM>() * 4 + (rl_tot_smem<TM>() ? TM * 8 * RL_THREADS * 4 : 0);
+  return rl_stages<TM, SPLIT>() * rl_stage_floats<TM>() * 4 + (rl_tot_smem<TM>() ? TM * 8 * RL_THREADS * 4 : 0);
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -135,7 +137,7 @@ __global__ void __launch_bounds__(RL_THREADS, TM >= 8 ? 2 : 4) router_logits_ker
   if (zero_counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)  // route_kernel's counters
     for (int i = threadIdx.x; i < e; i += RL_THREADS) zero_counts[i] = 0;
   constexpr int TT = rl_tok<TM>();
-  constexpr int RL_STAGES = rl_stages<SPLIT>();
+  constexpr int RL_STAGES = rl_stages<TM, SPLIT>();
   const uint32_t sm0 = smem_u32(rl_smem_f);
   const int tid = threadIdx.x;
   const int ty = tid >> 3, tx = tid & 7;
@@ -466,33 +468,50 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
 
 // p = sigmoid(logit) into part[0] ([n][e]); the split path also uses part[1 .. h/256 - 1] for
 // partials and `arrivals` (router_arrivals(n, e) zeroed ints, left zeroed again).
-cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, bool split,
-                          int32_t* arrivals, int32_t* zero_counts, cudaStream_t st) {
-  if (h % kRouterSeg) return cudaErrorInvalidValue;
-  const int nseg = h / kRouterSeg;
-  const unsigned gy = (unsigned)((e + RL_EXP - 1) / RL_EXP);
-  if (split) {
-    dim3 grid((unsigned)((n + rl_tok<2>() - 1) / rl_tok<2>()), gy, (unsigned)nseg);
-    cudaFuncSetAttribute(router_logits_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         rl_smem<2, true>());
-    if (!arrivals) return cudaErrorInvalidValue;
-    return launch_pdl(router_logits_kernel<2, true>, grid, dim3(RL_THREADS), rl_smem<2, true>(), st, x, wrt, part, n, h,
-                      e, arrivals, zero_counts);
-  } else {
-    dim3 grid((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, 1u);
-    cudaFuncSetAttribute(router_logits_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         rl_smem<8, false>());
-    return launch_pdl(router_logits_kernel<8, false>, grid, dim3(RL_THREADS), rl_smem<8, false>(), st, x, wrt, part, n,
-                      h, e, (int32_t*)nullptr, zero_counts);
-  }
-  return cudaGetLastError();
+template <int TM, bool SPLIT>
+static cudaError_t launch_logits(dim3 grid, const float* x, const float* wrt, float* part, int64_t n, int h, int e,
+                                 int32_t* arrivals, int32_t* zero_counts, cudaStream_t st) {
+  auto kern = router_logits_kernel<TM, SPLIT>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rl_smem<TM, SPLIT>());
+  if (err != cudaSuccess) return err;
+  return launch_pdl(kern, grid, dim3(RL_THREADS), rl_smem<TM, SPLIT>(), st, x, wrt, part, n, h, e, arrivals,
+                    zero_counts);
 }
 
-// Splitting by segment pays while the whole-K tiles would leave most SMs idle. Measured on B200
-// (E = 256, H = 4096): split 224 vs whole-K 307 us at 2048 tokens, 449 vs 310 us at 4096.
-bool router_split(int64_t n, int e, int sms) {
-  const int64_t tiles = ((n + rl_tok<8>() - 1) / rl_tok<8>()) * ((e + RL_EXP - 1) / RL_EXP);
-  return 2 * tiles < sms;
+cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, RouterPlan plan,
+                          int32_t* arrivals, int32_t* zero_counts, cudaStream_t st) {
+  if (h % kRouterSeg) return cudaErrorInvalidValue;
+  const unsigned nseg = (unsigned)(h / kRouterSeg);
+  const unsigned gy = (unsigned)((e + RL_EXP - 1) / RL_EXP);
+  if (plan != ROUTER_WHOLE && !arrivals) return cudaErrorInvalidValue;
+  switch (plan) {
+    case ROUTER_WHOLE:
+      return launch_logits<8, false>(dim3((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, 1u), x, wrt, part, n, h,
+                                     e, nullptr, zero_counts, st);
+    case ROUTER_SPLIT8:
+      return launch_logits<8, true>(dim3((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, nseg), x, wrt, part, n, h,
+                                    e, arrivals, zero_counts, st);
+    case ROUTER_SPLIT2:
+      return launch_logits<2, true>(dim3((unsigned)((n + rl_tok<2>() - 1) / rl_tok<2>()), gy, nseg), x, wrt, part, n, h,
+                                    e, arrivals, zero_counts, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Whole-K TM = 8 tiles once they load every SM 1.4 times (a whole-K tile runs ~300 us alone on an
+// SM, ~490 us two to an SM, against ~2.4 us per 32 tokens split by segment); below that, the same
+// tiles split by 256-k segment while those give every SM one; below that, TM = 2 tiles split by
+// segment. Measured on B200 (E = 256, H = 4096; router stage, logits + routing), whole / split
+// 128 / split 32 tokens:
+//   256 tokens   293 /  71 /  59 us        2048 tokens  307 / 175 / 220 us
+//   512 tokens   303 /  82 /  86 us        3072 tokens  307 / 230 / 321 us
+//   1024 tokens  304 / 117 / 130 us       4096 tokens  310 / 302 / 436 us
+//   5120 tokens (whole) 515 us, 8192 tokens (whole) 490 us
+RouterPlan router_plan(int64_t n, int e, int h, int sms) {
+  const int64_t tiles8 = ((n + rl_tok<8>() - 1) / rl_tok<8>()) * ((e + RL_EXP - 1) / RL_EXP);
+  if (10 * tiles8 >= 14 * (int64_t)sms) return ROUTER_WHOLE;
+  if (tiles8 * (h / kRouterSeg) >= sms) return ROUTER_SPLIT8;
+  return ROUTER_SPLIT2;
 }
 
 int64_t router_arrivals(int64_t n, int e) { return ((n + rl_tok<2>() - 1) / rl_tok<2>()) * ((e + RL_EXP - 1) / RL_EXP); }

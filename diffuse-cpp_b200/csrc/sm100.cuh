@@ -270,9 +270,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
   return d;
 }
-// arrive on an mbarrier anywhere in the cluster (release at cluster scope)
+// arrive on an mbarrier anywhere in the cluster. The default semantics (release, CTA scope), as
+// CUTLASS's cluster pipelines use: TMEM hand-offs are ordered by tcgen05.fence::before_thread_sync
+// ahead of the arrive. An explicit .release.cluster arrive measured ~0.6 us per call on B200.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // wait on a local mbarrier whose arrivals come from the whole cluster (acquire at cluster scope)
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {

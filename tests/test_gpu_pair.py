@@ -1,7 +1,8 @@
 """CTA-pair expert GEMMs (GPU): clusters of two CTAs share each 256-row weight tile through
 tcgen05 cta_group::2, each CTA dequantising 128 of the rows and loading half of the 128 token
-rows. DMOE_PAIR=1 turns them on for quantised layers at a 128-token tile (DMOE_NT=128), 0 off.
-Both must meet the oracle tolerance; on the same input the two must agree to fp32 rounding.
+rows. Quantised layers at a 128-token tile (DMOE_NT=128) use them for gate/up by default
+(DMOE_PAIR=1); DMOE_PAIR=2 adds the down GEMM, 0 turns them off. Every setting must meet the
+oracle tolerance, and on the same input they must agree to fp32 rounding.
 """
 import os
 
@@ -41,14 +42,14 @@ def test_pair_matches_oracle_and_single(qtype, H, I, Is, n, env):
     ref = oracle.layer(spec.hparams(), t, x)[0]
     L = dm.MoELayer(spec.hparams(), t)
     outs = {}
-    for pair in (1, 0):
+    for pair in (2, 1, 0):
         env(DMOE_PAIR=pair, DMOE_NT=128)
         out = L.forward(x)
         L.sync()
         assert L.stats()["token_tile"] == 128
         assert rel_l2(out, ref) <= TOL[qtype], (pair, rel_l2(out, ref))
         outs[pair] = out
-    assert rel_l2(outs[1], outs[0]) < 1e-5
+    assert rel_l2(outs[1], outs[0]) < 1e-5 and rel_l2(outs[2], outs[0]) < 1e-5
     L.close()
 
 
@@ -62,9 +63,10 @@ def test_pair_flash_shape_many_tiles(env):
     x = synth.make_input(2048, spec.H, 5)
     env(DMOE_PAIR=0, DMOE_NT=128)
     a = L.forward(x)
-    env(DMOE_PAIR=1, DMOE_NT=128)
-    b = L.forward(x)
-    L.sync()
-    assert np.isfinite(b).all()
-    assert rel_l2(b, a) < 1e-5
+    for pair in (1, 2):
+        env(DMOE_PAIR=pair, DMOE_NT=128)
+        b = L.forward(x)
+        L.sync()
+        assert np.isfinite(b).all()
+        assert rel_l2(b, a) < 1e-5, pair
     L.close()
