@@ -270,7 +270,8 @@ dmoe_status validate(const dmoe_layer_desc* d) {
 }
 
 // Tuning overrides (DMOE_NT = 32 / 64 / 128, DMOE_KSPLIT_GU / DMOE_KSPLIT_DN = 1 / 2 / 4 / 8,
-// DMOE_ROUTER_SPLIT = 0 whole-K / 1 split 32-token tiles / 2 split 128-token tiles,
+// DMOE_ROUTER_SPLIT = 0 whole-K / 1 split 32-token tiles / 2 split 128-token tiles / 3 whole-K
+// 112-token tiles,
 // DMOE_COMBINE_MIN = tokens); unset or invalid values keep the
 // automatic choice.
 int env_int(const char* name, int dflt) {
@@ -1047,8 +1048,8 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   const bool use_block = L->blk > 1 && L->cap > 0 && L->cap < E && n % L->blk == 0;
   const int nseg = (int)((H + kRouterSeg - 1) / kRouterSeg);
   RouterPlan rl_plan = router_plan(n, (int)E, (int)H, L->sms);  // too few whole-K tiles: split by segment
-  if (const int f = env_int("DMOE_ROUTER_SPLIT", -1); f >= 0 && f <= 2) rl_plan = (RouterPlan)f;
-  const bool rl_split = rl_plan != ROUTER_WHOLE;
+  if (const int f = env_int("DMOE_ROUTER_SPLIT", -1); f >= 0 && f <= 3) rl_plan = (RouterPlan)f;
+  const bool rl_split = rl_plan == ROUTER_SPLIT2 || rl_plan == ROUTER_SPLIT8;
   const int nparts = rl_split ? nseg : 1;
 
   dmoe_status s;

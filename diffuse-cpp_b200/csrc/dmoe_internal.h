@@ -99,9 +99,9 @@ struct RouteArgs {
   int tok_split;       // CTAs per routing block (set by launch_route)
 };
 
-// router logits launch: whole-K 128-token tiles, or per-256-k-segment partials of 128- or
-// 32-token tiles summed by each tile's last CTA (part[1 ..] and `arrivals` in use)
-enum RouterPlan { ROUTER_WHOLE = 0, ROUTER_SPLIT2 = 1, ROUTER_SPLIT8 = 2 };
+// router logits launch: whole-K 128- or 112-token tiles, or per-256-k-segment partials of 128-
+// or 32-token tiles summed by each tile's last CTA (part[1 ..] and `arrivals` in use)
+enum RouterPlan { ROUTER_WHOLE = 0, ROUTER_SPLIT2 = 1, ROUTER_SPLIT8 = 2, ROUTER_WHOLE7 = 3 };
 cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, RouterPlan plan,
                           int32_t* arrivals, int32_t* zero_counts, cudaStream_t st);
 RouterPlan router_plan(int64_t n, int e, int h, int sms);

@@ -70,9 +70,9 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 //                  of a tile to finish (per-tile arrival counter) adds P_0 .. P_{S-1} left to
 //                  right, writes p to part[0] and re-arms the counter (small N, where whole-K
 //                  tiles cannot fill the GPU).
-// TM = 8 for large N (fewer shared-memory reads per fma, the router weight re-read a quarter as
-// often), split by segment while whole-K TM = 8 tiles cannot fill the GPU; TM = 2 split for the
-// smallest N (more CTAs).
+// TM = 8 (or 7, to balance the SMs) for large N (fewer shared-memory reads per fma, the router
+// weight re-read a quarter as often), split by segment while whole-K TM = 8 tiles cannot fill the
+// GPU; TM = 2 split for the smallest N (more CTAs).
 // ------------------------------------------------------------------------------------------
 constexpr int RL_EXP = 64, RL_KC = 32, RL_THREADS = 128;
 constexpr int RL_XP = RL_KC + 4;  // x tile row pitch (floats)
@@ -86,10 +86,10 @@ constexpr int rl_stage_floats() { return rl_tok<TM>() * RL_XP + RL_KC * RL_EXP; 
 // ring, split or not
 template <int TM, bool SPLIT>
 constexpr int rl_stages() { return (SPLIT && TM <= 2) ? kRouterSeg / RL_KC : 3; }
-// TM = 8 keeps the running segment sums tot in shared memory (expert-major: [TM x 8][thread],
-// conflict-free) instead of 64 more registers
+// TM >= 7 keeps the running segment sums tot in shared memory (expert-major: [TM x 8][thread],
+// conflict-free) instead of 56-64 more registers
 template <int TM>
-constexpr bool rl_tot_smem() { return TM >= 8; }
+constexpr bool rl_tot_smem() { return TM >= 7; }
 template <int TM, bool SPLIT>
 constexpr int rl_smem() {
   return rl_stages<TM, SPLIT>() * rl_stage_floats<TM>() * 4 + (rl_tot_smem<TM>() ? TM * 8 * RL_THREADS * 4 : 0);
@@ -126,7 +126,7 @@ __device__ __forceinline__ void lds2x64(uint32_t a, f32x2& lo, f32x2& hi) {
 }
 
 template <int TM, bool SPLIT>
-__global__ void __launch_bounds__(RL_THREADS, TM >= 8 ? 2 : 4) router_logits_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(RL_THREADS, TM >= 7 ? 2 : 4) router_logits_kernel(const float* __restrict__ x,
                                                                    const float* __restrict__ wrt,
                                                                    float* __restrict__ part, int64_t n, int h, int e,
                                                                    int32_t* __restrict__ arrivals,
@@ -483,10 +483,13 @@ cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t
   if (h % kRouterSeg) return cudaErrorInvalidValue;
   const unsigned nseg = (unsigned)(h / kRouterSeg);
   const unsigned gy = (unsigned)((e + RL_EXP - 1) / RL_EXP);
-  if (plan != ROUTER_WHOLE && !arrivals) return cudaErrorInvalidValue;
+  if ((plan == ROUTER_SPLIT2 || plan == ROUTER_SPLIT8) && !arrivals) return cudaErrorInvalidValue;
   switch (plan) {
     case ROUTER_WHOLE:
       return launch_logits<8, false>(dim3((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, 1u), x, wrt, part, n, h,
+                                     e, nullptr, zero_counts, st);
+    case ROUTER_WHOLE7:
+      return launch_logits<7, false>(dim3((unsigned)((n + rl_tok<7>() - 1) / rl_tok<7>()), gy, 1u), x, wrt, part, n, h,
                                      e, nullptr, zero_counts, st);
     case ROUTER_SPLIT8:
       return launch_logits<8, true>(dim3((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, nseg), x, wrt, part, n, h,
@@ -507,9 +510,14 @@ cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t
 //   512 tokens   303 /  82 /  86 us        3072 tokens  307 / 230 / 321 us
 //   1024 tokens  304 / 117 / 130 us       4096 tokens  310 / 302 / 436 us
 //   5120 tokens (whole) 515 us, 8192 tokens (whole) 490 us
+// Whole-K tiles of 112 tokens (TM = 7) where they put less work on the busiest SM than 128-token
+// tiles: at 8192 tokens 296 tiles run two per SM, where 256 tiles leave 40 SMs with one.
 RouterPlan router_plan(int64_t n, int e, int h, int sms) {
-  const int64_t tiles8 = ((n + rl_tok<8>() - 1) / rl_tok<8>()) * ((e + RL_EXP - 1) / RL_EXP);
-  if (10 * tiles8 >= 14 * (int64_t)sms) return ROUTER_WHOLE;
+  const int64_t etiles = (e + RL_EXP - 1) / RL_EXP;
+  const int64_t tiles8 = ((n + rl_tok<8>() - 1) / rl_tok<8>()) * etiles;
+  const int64_t tiles7 = ((n + rl_tok<7>() - 1) / rl_tok<7>()) * etiles;
+  if (10 * tiles8 >= 14 * (int64_t)sms)
+    return 7 * ((tiles7 + sms - 1) / sms) < 8 * ((tiles8 + sms - 1) / sms) ? ROUTER_WHOLE7 : ROUTER_WHOLE;
   if (tiles8 * (h / kRouterSeg) >= sms) return ROUTER_SPLIT8;
   return ROUTER_SPLIT2;
 }
