@@ -504,7 +504,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     // 46 cycles or more even at N <= 64, and a run-time branch between two MMAs about 100.
     // PAIR: only the leader's warp issues; its MMAs read both CTAs' A (TMEM) and B (shared
     // memory) halves at the same addresses and write both CTAs' accumulators, and its commits
-    // arrive on the barriers of both CTAs (mask 0b11).
+    // arrive on the barriers of both CTAs.
     constexpr uint32_t idesc = idesc_f16_f32(C::PAIR ? 256 : 128, NT);
     uint32_t stage_seq = 0, tile_seq = 0;
     for (int t = t_first; t < total && !warp_abort(abort_flag) && (!C::PAIR || rank == 0); t += t_step) {
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
                     mma_f16_ts(dbase + m * NT, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
                 }
               }
-              if constexpr (C::PAIR) mma_commit_pair(&aempty[a], 3);
+              if constexpr (C::PAIR) mma_commit_pair(&aempty[a]);
               else mma_commit(&aempty[a]);
             }
             __syncwarp();
@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
         }
         first = false;
         if (elect_one()) {
-          if constexpr (C::PAIR) mma_commit_pair(&empty[s], 3);
+          if constexpr (C::PAIR) mma_commit_pair(&empty[s]);
           else mma_commit(&empty[s]);
         }
         __syncwarp();
@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
       }
       if (!ok) break;
       if (elect_one()) {
-        if constexpr (C::PAIR) mma_commit_pair(&accfull[ab], 3);
+        if constexpr (C::PAIR) mma_commit_pair(&accfull[ab]);
         else mma_commit(&accfull[ab]);
       }
       __syncwarp();

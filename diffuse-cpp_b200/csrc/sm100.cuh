@@ -103,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
+// TMA (cp.async.bulk.tensor): every copy lands in the issuing CTA's own shared memory.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -257,7 +257,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// CTA pairs (clusters of 2, tcgen05 cta_group::2). No TMA multicast: each CTA loads its own data.
+// CTA pairs (clusters of 2, tcgen05 cta_group::2). Each CTA's copies land in its own shared memory.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -292,7 +292,7 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // 2-D tile load into this CTA's shared memory whose completion is counted on the mbarrier at
-// `bar_cluster` (the pair's leader CTA): cp.async.bulk.tensor .cta_group::2, no multicast
+// `bar_cluster` (the pair's leader CTA): cp.async.bulk.tensor .cta_group::2
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, int32_t c0, int32_t c1,
                                                  uint32_t bar_cluster) {
   asm volatile(
@@ -322,13 +322,15 @@ __device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// arrive once on the mbarrier at this offset in every CTA of `mask` when the pair's MMAs are done
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(mask)
-      : "memory");
+// arrive once on the mbarrier at this offset in both CTAs of the pair when the pair's MMAs issued
+// so far are done: two commits, to this CTA's copy and (through its shared::cluster address) the
+// peer's
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  const uint32_t own = smem_u32(bar);
+  uint32_t peer;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 1;" : "=r"(peer) : "r"(own));
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(own) : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer) : "memory");
 }
 
 // Programmatic dependent launch. pdl_wait: block until the preceding grid in the stream has
