@@ -333,6 +333,47 @@ def main():
               "rows_received_per_rank": [int(v.item()) for v in allv], "scaling": "strong",
               "bias": "0.5 log Zipf(1.1) over a random expert permutation"}
 
+    # ---- sampler step (dmoe_sample_step): one block of 32 masked positions over the flash-model
+    # vocabulary; 8 logits buffers in rotation (160 MB > L2), the block's seq reset every step
+    sampler = None
+    if rank == 0 and world == 1:
+        V, P, NB = 157184, 32, 8
+        gen = torch.Generator(device=dev).manual_seed(7)
+        lbufs = [torch.randn((P, V), device=dev, generator=gen) * 3 for _ in range(NB)]
+        seq0 = torch.full((P,), 156895, dtype=torch.int32, device=dev)  # every position masked
+        seqd = seq0.clone()
+        tok = torch.empty(P, dtype=torch.int32, device=dev)
+        prb = torch.empty(P, dtype=torch.float32, device=dev)
+        for i in range(5):
+            seqd.copy_(seq0)
+            dm.sample_step(lbufs[i % NB], seqd, 156895, 2, 0.95, tok, prb)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 40
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(reps):
+            seqd.copy_(seq0)
+            dm.sample_step(lbufs[i % NB], seqd, 156895, 2, 0.95, tok, prb)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        sbytes = P * V * 4
+        sampler = {"workload": "32 masked positions x 157184 logits (one LLaDA2 block), greedy, n_transfer 2, "
+                               "threshold 0.95", "us_per_step": us, "bytes": sbytes,
+                   "hbm_gbs": sbytes / (us / 1e6) / 1e9, "frac": sbytes / (us / 1e6) / 1e9 / peaks_hbm,
+                   "kernels_per_step": 2}
+        if not args.no_cpu:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle  # CPU baseline leg only
+
+            lg = lbufs[0].cpu().numpy()
+            t0 = time.perf_counter()
+            for _ in range(3):
+                oracle.sample_step(lg, np.full(P, 156895, np.int32), 156895, 2, 0.95)
+            sampler["cpu_baseline"] = {"us_per_step": (time.perf_counter() - t0) / 3 * 1e6, "cores": os.cpu_count(),
+                                       "kind": "port"}
+        del lbufs
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, sample = run_cpu_reference(spec, t, n_tok)
@@ -349,6 +390,8 @@ def main():
                 "ksplit": [st["ksplit_gateup"], st["ksplit_down"]], "sweep": sweep}
         if c4 is not None:
             line["c4"] = c4
+        if sampler is not None:
+            line["sampler"] = sampler
         print(json.dumps(line))
     layer.close()
     if world > 1:

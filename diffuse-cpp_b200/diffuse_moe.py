@@ -146,6 +146,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.dmoe_route_static.restype = ctypes.c_int
     lib.dmoe_nccl_unique_id.argtypes = [P]
     lib.dmoe_nccl_unique_id.restype = ctypes.c_int
+    lib.dmoe_sample_step.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int32, ctypes.c_int32,
+                                     ctypes.c_float, P, P, P, P]
+    lib.dmoe_sample_step.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -317,3 +320,19 @@ def route_static(x, w_router, b_router, hp: dict, idx, weights, stream: Optional
                                     hp["n_expert"], hp["n_expert_used"], hp.get("expert_capacity", 48),
                                     hp.get("moe_block_size", 32), hp.get("routed_scaling", 1.0),
                                     hp.get("norm_topk_prob", 1), _ptr(idx), _ptr(weights), stream if stream else None))
+
+
+def sample_step(logits, seq, mask_id: int, n_transfer: int, threshold: float, token, prob, n_committed=None,
+                stream: Optional[int] = None) -> None:
+    """dmoe_sample_step: one greedy denoising step of the block sampler on the GPU
+    (src/diffuse-sampler.cpp:29-49,183-237). torch CUDA tensors: logits [n_pos, n_vocab] f32,
+    seq [n_pos] int32 (updated in place; None: argmax and probability only), token [n_pos] int32
+    and prob [n_pos] f32 (outputs), n_committed [1] int32 or None. Enqueued on the current torch
+    stream."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+    n_pos, n_vocab = int(logits.shape[0]), int(logits.shape[1])
+    _check(load().dmoe_sample_step(_ptr(logits), n_pos, n_vocab, _ptr(seq), mask_id, n_transfer, threshold,
+                                   _ptr(token), _ptr(prob), _ptr(n_committed), stream if stream else None))

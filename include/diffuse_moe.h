@@ -204,6 +204,27 @@ dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64_t n_embd, 
                               int64_t expert_capacity, int64_t moe_block_size, float routed_scaling,
                               int32_t norm_topk_prob, int32_t* idx, float* weights, void* stream);
 
+/* One denoising step of the block sampler, greedy (temperature 0, low-confidence remasking: the
+ * reference's defaults, include/diffuse.h:42-46), on the GPU. Replaces sample_token's argmax
+ * branch (src/diffuse-sampler.cpp:29-49) for every masked position and the step's commit
+ * (:183-237), so the logits never leave the device (the reference copies all of them to the host,
+ * src/diffuse-moe-graph.cpp:331-332). All pointers are DEVICE memory:
+ *   logits  [n_pos][n_vocab] f32: the rows of the block's positions
+ *   seq     [n_pos] int32: the block's tokens; position r is a candidate iff seq[r] == mask_id.
+ *           Committed positions receive their token. NULL: every row is a candidate, nothing is
+ *           committed (argmax and probability only).
+ *   token, prob [n_pos]: per candidate its argmax (the lowest index among equal maxima) and
+ *           1 / sum_v exp(l_v - max); -1 and 0 for other positions
+ *   n_committed (optional) : how many positions were committed
+ * Commit rule: candidates by probability, highest first (equal probabilities in position order;
+ * the reference's std::sort leaves that order unspecified); the first n_transfer are committed,
+ * then every further one with probability >= threshold; at least one. Enqueued on `stream`
+ * (NULL = the CUDA default stream); n_pos <= DMOE_SAMPLE_MAX_POS. */
+#define DMOE_SAMPLE_MAX_POS 1024
+dmoe_status dmoe_sample_step(const float* logits, int64_t n_pos, int64_t n_vocab, int32_t* seq, int32_t mask_id,
+                             int32_t n_transfer, float threshold, int32_t* token, float* prob,
+                             int32_t* n_committed, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

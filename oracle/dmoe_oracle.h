@@ -65,6 +65,15 @@ int dmoe_oracle_route(const float* logits, int64_t n, int64_t e, const float* bi
 int dmoe_oracle_experts(const orc_layer* L, const float* x, int64_t n, const int32_t* idx, const float* w, float* out,
                         int mode, int nthreads);
 
+/* Greedy sampler step, src/diffuse-sampler.cpp:29-49,183-237 (dmoe_oracle_sampler.c):
+ * per masked position the argmax (strict `>` scan) and 1 / sum_v expf(l_v - max) summed in float
+ * in index order; the commit of the candidates sorted by probability (stable: equal
+ * probabilities in position order). seq may be NULL (every row a candidate, no commit).
+ * Returns the number committed. */
+void dmoe_oracle_sample_row(const float* logits, int64_t n_vocab, int32_t* token, float* prob);
+int32_t dmoe_oracle_sample_step(const float* logits, int64_t n_pos, int64_t n_vocab, int32_t* seq, int32_t mask_id,
+                                int32_t n_transfer, float threshold, int32_t* token, float* prob);
+
 #ifdef __cplusplus
 }
 #endif

@@ -75,6 +75,9 @@ def load() -> ctypes.CDLL:
     lib.dmoe_oracle_experts.argtypes = [ctypes.POINTER(OrcLayer), P, ctypes.c_int64, P, P, P, ctypes.c_int,
                                         ctypes.c_int]
     lib.dmoe_oracle_experts.restype = ctypes.c_int
+    lib.dmoe_oracle_sample_step.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_float, P, P]
+    lib.dmoe_oracle_sample_step.restype = ctypes.c_int32
     _lib = lib
     return lib
 
@@ -161,3 +164,17 @@ def layer(hp: dict, t: dict, x: np.ndarray, mode: int = 0, nthreads: int = 0):
                                      hp.get("routed_scaling", 1.0))
     out = experts(hp, t, x, idx, w, mode, nthreads)
     return out, idx, w, allowed, used
+
+
+def sample_step(logits: np.ndarray, seq, mask_id: int, n_transfer: int, threshold: float):
+    """Greedy sampler step (src/diffuse-sampler.cpp:29-49,183-237). logits [n_pos][n_vocab] f32;
+    seq [n_pos] int32 or None. Returns (token, prob, seq_after, n_committed)."""
+    lib = load()
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    n_pos, n_vocab = lg.shape
+    tok = np.empty(n_pos, np.int32)
+    pr = np.empty(n_pos, np.float32)
+    s = None if seq is None else np.array(seq, dtype=np.int32, copy=True)
+    nc = lib.dmoe_oracle_sample_step(_p(lg), n_pos, n_vocab, None if s is None else _p(s), mask_id, n_transfer,
+                                     threshold, _p(tok), _p(pr))
+    return tok, pr, s, int(nc)
