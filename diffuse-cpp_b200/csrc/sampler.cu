@@ -30,6 +30,7 @@ namespace {
 constexpr int kClusterCtas = 8;
 constexpr int kRowThreads = 512;
 constexpr int kCommitThreads = 1024;
+constexpr int kUnroll = 4;  // 16-byte loads in flight per thread
 static_assert(DMOE_SAMPLE_MAX_POS <= kCommitThreads, "one commit thread per position");
 
 struct Best {
@@ -104,23 +105,37 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kRowThrea
     // thread tid takes the 4-value groups tid, tid + 512, ... of the slice (increasing indices
     // within a thread), as one float4 load where the row is 16-byte aligned and as four loads
     // where it is not: the same values in the same order either way, so equal rows give equal bits
+    // kUnroll groups are loaded before any is consumed (enough bytes in flight to cover the
+    // memory latency), then visited in index order
     const int64_t n4 = (v1 - v0) / 4;
     const bool vec = ((reinterpret_cast<uintptr_t>(r + v0) & 15) == 0);
-    for (int64_t q = tid; q < n4; q += kRowThreads) {
-      const int64_t b = v0 + 4 * q;
-      float4 x;
-      if (vec) {
-        x = __ldcs(reinterpret_cast<const float4*>(r + b));
-      } else {
-        x.x = __ldcs(r + b);
-        x.y = __ldcs(r + b + 1);
-        x.z = __ldcs(r + b + 2);
-        x.w = __ldcs(r + b + 3);
+    for (int64_t q0 = tid; q0 < n4; q0 += kUnroll * kRowThreads) {
+      float4 x[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t q = q0 + (int64_t)u * kRowThreads;
+        const int64_t b = v0 + 4 * q;
+        if (q >= n4) {
+          x[u] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        } else if (vec) {
+          x[u] = __ldcs(reinterpret_cast<const float4*>(r + b));
+        } else {
+          x[u].x = __ldcs(r + b);
+          x[u].y = __ldcs(r + b + 1);
+          x[u].z = __ldcs(r + b + 2);
+          x[u].w = __ldcs(r + b + 3);
+        }
       }
-      visit(t, x.x, (int32_t)b);
-      visit(t, x.y, (int32_t)b + 1);
-      visit(t, x.z, (int32_t)b + 2);
-      visit(t, x.w, (int32_t)b + 3);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t q = q0 + (int64_t)u * kRowThreads;
+        if (q >= n4) break;
+        const int32_t b = (int32_t)(v0 + 4 * q);
+        visit(t, x[u].x, b);
+        visit(t, x[u].y, b + 1);
+        visit(t, x[u].z, b + 2);
+        visit(t, x[u].w, b + 3);
+      }
     }
     for (int64_t q = v0 + 4 * n4 + tid; q < v1; q += kRowThreads) visit(t, __ldcs(r + q), (int32_t)q);
   }
@@ -149,6 +164,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kRowThrea
     prob[row] = 1.0f / b.s;  // exp(max - max) / sum
   }
   cluster_sync();  // CTA 0 has read every peer's shared memory before they exit
+  pdl_trigger();
 }
 
 // One CTA: rank the candidates and commit (src/diffuse-sampler.cpp:212-237).
@@ -160,6 +176,7 @@ __global__ void __launch_bounds__(kCommitThreads)
   __shared__ int32_t cand_s[kCommitThreads];
   __shared__ int32_t committed, top;
   const int i = threadIdx.x;
+  pdl_wait();  // the rows kernel's token / prob are complete and visible
   const bool cand = i < n_pos && token[i] >= 0;
   const float p = cand ? prob[i] : 0.0f;
   p_s[i] = p;
@@ -220,9 +237,21 @@ extern "C" dmoe_status dmoe_sample_step(const float* logits, int64_t n_pos, int6
   sample_rows_kernel<<<dim3(kClusterCtas, (unsigned)n_pos), dim3(kRowThreads), 0, st>>>(logits, n_vocab, seq, mask_id,
                                                                                       token, prob);
   cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess && seq)
-    sample_commit_kernel<<<1, kCommitThreads, 0, st>>>((int)n_pos, seq, token, prob, n_transfer, threshold,
-                                                       n_committed);
+  if (e == cudaSuccess && seq) {
+    // programmatic dependent launch: the commit CTA starts while the rows kernel drains and
+    // waits for it in griddepcontrol.wait
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kCommitThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, sample_commit_kernel, (int)n_pos, seq, (const int32_t*)token, (const float*)prob,
+                           n_transfer, threshold, n_committed);
+  }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(msg, sizeof(msg), "dmoe_sample_step: launch failed: %s", cudaGetErrorString(e));
