@@ -12,7 +12,8 @@
 // sample_rows_kernel: one cluster of kClusterCtas CTAs per position. Each CTA scans its slice of
 // the row once, keeping a running (max, lowest index of the max, sum of exp(l - max)) per thread
 // (the sum is rescaled by exp(old max - new max) when the max grows); the threads' triples merge
-// in the CTA, and CTA 0 merges the CTAs' triples in rank order through distributed shared memory.
+// in the CTA, and CTA 0 merges the CTAs' triples (read through distributed shared memory) in a
+// fixed shuffle tree.
 // The row is read once: the kernel is HBM-bound (4 n_vocab bytes per masked position).
 // sample_commit_kernel: one CTA ranks the candidates (probability descending, position ascending
 // among equal probabilities, where the reference's std::sort leaves the order unspecified) and
@@ -30,7 +31,7 @@ namespace {
 constexpr int kClusterCtas = 8;
 constexpr int kRowThreads = 512;
 constexpr int kCommitThreads = 1024;
-constexpr int kUnroll = 4;  // 16-byte loads in flight per thread
+constexpr int kUnroll = 10;  // 16-byte loads in flight per thread: a 157,184-value row in one batch
 static_assert(DMOE_SAMPLE_MAX_POS <= kCommitThreads, "one commit thread per position");
 
 struct Best {
@@ -150,18 +151,22 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kRowThrea
     if (lane == 0) cta_best = t;
   }
   cluster_sync();  // every CTA's cta_best is written
-  if (rank == 0 && tid == 0) {
-    Best b = cta_best;
-    for (uint32_t c = 1; c < kClusterCtas; ++c) {
-      const uint32_t a = mapa_shared(smem_u32(&cta_best), c);
-      Best o;
+  if (rank == 0 && warp == 0) {
+    // lane c < kClusterCtas reads CTA c's triple (all at once), then a fixed shuffle tree merges
+    // them: the same order every time, so the bits do not depend on timing
+    Best o{-INFINITY, 0, 0.0f};
+    if (lane < kClusterCtas) {
+      const uint32_t a = mapa_shared(smem_u32(&cta_best), (uint32_t)lane);
       asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(o.m) : "r"(a));
       asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(o.i) : "r"(a + 4));
       asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(o.s) : "r"(a + 8));
-      b = merge(b, o);
     }
-    token[row] = b.i;
-    prob[row] = 1.0f / b.s;  // exp(max - max) / sum
+#pragma unroll
+    for (int off = kClusterCtas / 2; off; off >>= 1) o = merge(o, shfl_best(o, off));
+    if (lane == 0) {
+      token[row] = o.i;
+      prob[row] = 1.0f / o.s;  // exp(max - max) / sum
+    }
   }
   cluster_sync();  // CTA 0 has read every peer's shared memory before they exit
   pdl_trigger();
