@@ -49,7 +49,7 @@ struct GemmCfg {
   // to double-buffer them, and the epilogue's overlap with the next tile is worth more there.
   static constexpr int MATS = (MODE != MODE_DOWN || NT <= 64) ? 2 : 1;
   static_assert(!FUSED || NT <= 64, "the fused launch needs the two-block down tiles");
-  static_assert(!PAIR || (QUANT && !FUSED && NT == 128 && MATS * 64 * 2 <= 256), "pair tiles: quantised, NT = 128");
+  static_assert(!PAIR || (QUANT && !FUSED && NT == 128), "pair tiles: quantised weights, NT = 128, separate launches");
   // output rows per tile of one expert matrix, for a tile of mode `tmode`
   static constexpr int out_rows(int tmode) {
     return PAIR ? 2 * kMTile : (tmode == MODE_GATEUP ? kMTile : MATS * kMTile);
