@@ -27,6 +27,9 @@
 // pairs (k, k+2) and (k+1, k+3) with one LOP3 each, so the MMA's K order inside every aligned
 // quad is (0, 2, 1, 3). The activations for a q4_K matrix are written with the same quad swap
 // (gather kernel for x, gate/up epilogue for h); the dot products are unchanged.
+#include <algorithm>
+#include <atomic>
+
 #include "dmoe_internal.h"
 #include "sm100.cuh"
 
@@ -808,8 +811,9 @@ static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t st) {
     return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, st, p);
   } else {
     // clusters of two CTAs; as many pairs as can be resident at once (the tile walk assumes a
-    // persistent grid), counted once per instantiation
-    static int max_pairs = 0;
+    // persistent grid), counted once per instantiation (the library runs on B200s only, so every
+    // device of the process gives the same count; concurrent first calls store the same value)
+    static std::atomic<int> max_pairs{0};
     cudaLaunchConfig_t cfg{};
     cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = C::SMEM_BYTES;
@@ -822,16 +826,16 @@ static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t st) {
     at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    if (max_pairs == 0) {
+    if (max_pairs.load(std::memory_order_relaxed) == 0) {
       cfg.gridDim = dim3(grid & ~1);
       cfg.numAttrs = 1;
       int n = 0;
       e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
       if (e != cudaSuccess) return e;
       if (n < 1) return cudaErrorInvalidConfiguration;
-      max_pairs = n;
+      max_pairs.store(n, std::memory_order_relaxed);
     }
-    cfg.gridDim = dim3(2 * std::min(grid / 2, max_pairs));
+    cfg.gridDim = dim3(2 * std::min(grid / 2, max_pairs.load(std::memory_order_relaxed)));
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, p);
   }
