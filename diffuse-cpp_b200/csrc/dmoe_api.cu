@@ -300,26 +300,14 @@ int pick_nt(const dmoe_layer* L, int64_t n) {
   return 128;
 }
 
-// Smallest power-of-two split (<= 8) dividing every K-stage count that gives >= 4 waves.
+// Split-K factor of an expert GEMM. Measured on B200: the per-tile epilogue and pipeline refill
+// cost more than the wave quantisation they remove, at every block count, so split-K runs only
+// when forced (DMOE_KSPLIT_GU / DMOE_KSPLIT_DN).
 int pick_ksplit(int64_t tiles_est, int sms, std::initializer_list<int> kstages) {
-  // Measured on B200: the per-tile epilogue and pipeline refill cost more than the wave
-  // quantisation they remove, at every block count, so split-K is off unless forced.
   (void)tiles_est;
   (void)sms;
   (void)kstages;
   return 1;
-}
-
-[[maybe_unused]] int pick_ksplit_waves(int64_t tiles_est, int sms, std::initializer_list<int> kstages) {
-  int best = 1;
-  for (int s = 2; s <= 8; s *= 2) {
-    if (tiles_est * (best) >= 4LL * sms) break;
-    bool ok = true;
-    for (int ks : kstages) ok = ok && ks > 0 && ks % s == 0;
-    if (!ok) break;
-    best = s;
-  }
-  return best;
 }
 
 // CTA-pair GEMM tiles (256 output rows per tile, each activation tile loaded half by each CTA of

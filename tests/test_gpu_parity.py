@@ -98,3 +98,20 @@ def test_router_plans_bit_exact(plan, monkeypatch):
     monkeypatch.setenv("DMOE_ROUTER_SPLIT", str(plan))
     spec = tiny(dm.TYPE_Q8_0, H=1024, E=64, top_k=6, cap=20, seed=23)
     check_layer(spec, 608)  # 19 routing blocks: the last 128-token tile holds 96 tokens
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype", [dm.TYPE_Q8_0, dm.TYPE_Q4_K])
+def test_forced_split_k(qtype, monkeypatch):
+    """Split-K (off by default, forced with DMOE_KSPLIT_GU / DMOE_KSPLIT_DN): gate/up partial sums
+    in fp32 then the SwiGLU kernel, down partials reduced into the output; same oracle bar."""
+    monkeypatch.setenv("DMOE_KSPLIT_GU", "2")
+    monkeypatch.setenv("DMOE_KSPLIT_DN", "2")
+    spec = tiny(qtype, H=1024, I=512, Is=512, E=16, seed=29)
+    t = synth.make_layer(spec)
+    L = dm.MoELayer(spec.hparams(), t)
+    check_layer(spec, 96, t=t, layer=L)
+    L.forward(synth.make_input(96, spec.H, spec.seed), profile=True)
+    L.sync()
+    assert L.stats()["ksplit_gateup"] == 2 and L.stats()["ksplit_down"] == 2
+    L.close()
