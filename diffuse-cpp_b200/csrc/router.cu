@@ -534,7 +534,9 @@ cudaError_t launch_route(const RouteArgs& a_in, cudaStream_t st) {
   // few blocks: 4 CTAs per block share its tokens' top-k (each repeats the block-level steps)
   a.tok_split = nblocks < 64 ? 4 : 1;
   const size_t smem = route_smem_bytes(tpb, a.e);
-  cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRouteSmemMax);
+  const cudaError_t err = cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)kRouteSmemMax);
+  if (err != cudaSuccess) return err;
   return launch_pdl(route_kernel, dim3((unsigned)(nblocks * a.tok_split)), dim3(RT_THREADS), smem, st, a);
 }
 
