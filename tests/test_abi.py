@@ -57,3 +57,14 @@ def test_no_device_is_reported_not_worked_around():
     with pytest.raises(dm.DmoeError) as ei:
         dm.MoELayer(spec.hparams(), synth.make_layer(spec))
     assert ei.value.status == 3  # DMOE_ERR_NO_DEVICE
+
+
+def test_sample_step_argument_errors():
+    """dmoe_sample_step validates its arguments before touching the device."""
+    lib = dm.load()
+    assert lib.dmoe_sample_step(None, 4, 0, None, 0, 1, 0.5, None, None, None, None) == 1  # n_vocab <= 0
+    assert "n_vocab" in dm.last_error()
+    assert lib.dmoe_sample_step(None, 2000, 100, None, 0, 1, 0.5, None, None, None, None) == 2  # > max positions
+    assert lib.dmoe_sample_step(None, 4, 100, None, 0, 1, 0.5, None, None, None, None) == 1  # null logits
+    assert "null pointer" in dm.last_error()
+    assert lib.dmoe_sample_step(None, 0, 100, None, 0, 1, 0.5, None, None, None, None) == 0  # nothing to do
