@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <memory>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -798,6 +799,7 @@ dmoe_status forward_chunked(dmoe_layer* L, const float* x, int64_t n, float* out
   int kernels = 0;
   for (int c = 0; c < nc; ++c) {
     const int64_t t0 = starts[c], cn = sizes[c];
+    const NvtxRange nvtx_chunk("dmoe host chunk");
     DMOE_CUDA(cudaStreamWaitEvent(ks, L->ev_in[c], 0));
     if ((s = dmoe_forward(L, L->xdev + t0 * H, cn, L->odev + t0 * H, nullptr, ks, flags & ~DMOE_F_HOST_PTRS)) != DMOE_OK)
       return s;
@@ -1016,6 +1018,7 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   const bool prof = flags & DMOE_F_PROFILE;
   if (!route_only && n > 0 && !out) return fail(DMOE_ERR_INVALID_ARG, "null output");
   if (n * (1 + L->K) >= (1ll << 31)) return fail(DMOE_ERR_UNSUPPORTED, "too many tokens in one call");
+  const NvtxRange nvtx_call("dmoe_forward");
   DMOE_CUDA(cudaSetDevice(L->device));
   // device mode: the caller's stream as given (NULL = the CUDA default stream);
   // host mode without a stream: the layer's own stream
@@ -1076,6 +1079,7 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[0], st));
 
   // ---- router (src/diffuse-moe-graph.cpp:203-262)
+  auto nvtx_router = std::make_unique<NvtxRange>("dmoe router");
   DMOE_CUDA(launch_router(xd, L->wr, L->parts, n, (int)H, (int)E, rl_plan, L->arrivals, counts, st));
   ++kernels;
   RouteArgs ra{};
@@ -1096,8 +1100,10 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   DMOE_CUDA(launch_route(ra, st));
   ++kernels;
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[1], st));
+  nvtx_router.reset();
 
   if (!route_only) {
+    const NvtxRange nvtx_experts(L->world == 1 ? "dmoe experts" : "dmoe experts (expert parallel)");
     s = L->world == 1 ? single_gpu_experts(L, st, xd, n, ra.idx, ra.w, counts, od, flags, kernels)
                       : ep_experts(L, st, xd, n, ra.idx, ra.w, od, flags, kernels);
     if (s != DMOE_OK) return s;

@@ -4,6 +4,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstdint>
 #include <utility>
 
@@ -163,6 +165,15 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, 
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
+
+// NVTX range over a host scope: the layer's stages show up by name in Nsight timelines and can
+// filter ncu captures (--nvtx); a no-op when no tool is attached.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // records the message returned by dmoe_last_error on this thread (dmoe_api.cu)
 void set_last_error(const char* msg);

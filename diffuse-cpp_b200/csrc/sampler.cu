@@ -238,6 +238,7 @@ extern "C" dmoe_status dmoe_sample_step(const float* logits, int64_t n_pos, int6
     return DMOE_ERR_INVALID_ARG;
   }
   if (n_pos == 0) return DMOE_OK;
+  const NvtxRange nvtx_call("dmoe_sample_step");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   sample_rows_kernel<<<dim3(kClusterCtas, (unsigned)n_pos), dim3(kRowThreads), 0, st>>>(logits, n_vocab, seq, mask_id,
                                                                                       token, prob);
