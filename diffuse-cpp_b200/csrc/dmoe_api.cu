@@ -25,6 +25,7 @@
 
 #include "../../include/diffuse_moe.h"
 #include "dmoe_internal.h"
+#include "sm100.cuh"
 #include "nccl_dyn.h"
 
 using namespace dmoe;
@@ -398,6 +399,8 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   gp.gu_acc = ks_gu > 1 ? L->gu : nullptr;
   gp.gu_half = Imax;
   gp.err = L->err;
+  gp.rows_total = rows;
+  gp.n_experts = (int32_t)E_here;
   if (L->has_shared) {
     gp.tm_w[0][0] = L->sgate.tm_q;
     gp.tm_w[0][1] = L->sup.tm_q;
@@ -1155,6 +1158,8 @@ dmoe_status dmoe_sync(dmoe_layer* L) {
   }
   if (e) {
     cudaMemset(L->err, 0, 4);
+    if (e == ERRBIT_BAD_TILE)
+      return fail(DMOE_ERR_CUDA, "a device-built token tile was out of bounds and skipped (error bits 0x%x)", e);
     return fail(DMOE_ERR_TIMEOUT, "device wait timed out (error bits 0x%x); the kernel gave up", e);
   }
   return DMOE_OK;

@@ -83,6 +83,10 @@ struct GemmParams {
   GemmGroup grp_dn[2];
   int32_t* tt_done;
   uint32_t* err;
+  // bounds of the routed token tiles (built on the device): rows [n_tokens, rows_total) and
+  // experts [0, n_experts) of group 1; a tile outside them is skipped and reported
+  int64_t rows_total;
+  int32_t n_experts;
 };
 
 // Router: one routing block per CTA (src/diffuse-moe-graph.cpp:203-262).

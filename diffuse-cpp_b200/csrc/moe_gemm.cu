@@ -101,8 +101,10 @@ struct GemmCfg {
 
 // mode: MODE_GATEUP or MODE_DOWN (per tile in a fused launch); ttx: the token tile's index in
 // the fused launch's completion counters (shared tiles first, then routed)
+// bad: a routed tile whose rows or expert fall outside the buffers (a corrupt tile list); it is
+// decoded as an empty tile, so every role skips it the same way, and the producer reports it
 struct TileInfo {
-  int group, expert, row0, nrows, mt, k0, k1, mode, ttx;
+  int group, expert, row0, nrows, mt, k0, k1, mode, ttx, bad;
 };
 
 __device__ __forceinline__ int tiles_in(const GemmParams& p, const GemmGroup* gr) {
@@ -119,6 +121,7 @@ __device__ __forceinline__ int tiles_total(const GemmParams& p) {
 template <int MODE, int NT>
 __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
   TileInfo ti;
+  ti.bad = 0;
   ti.mode = MODE == MODE_FUSED ? MODE_GATEUP : MODE;
   const GemmGroup* gr = p.grp;
   if (MODE == MODE_FUSED) {
@@ -148,9 +151,13 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
     const int tt = t / per_tt;
     r = t - tt * per_tt;
     const TokTile tk = p.tiles[tt];
-    ti.expert = tk.expert;
-    ti.row0 = tk.row0;
-    ti.nrows = tk.nrows;
+    ti.bad = (tk.expert < 0 || tk.expert >= p.n_experts || tk.nrows < 0 || tk.nrows > NT ||
+              (int64_t)tk.row0 < p.n_tokens || (int64_t)tk.row0 + tk.nrows > p.rows_total)
+                 ? 1
+                 : 0;
+    ti.expert = ti.bad ? 0 : tk.expert;
+    ti.row0 = ti.bad ? (int)p.n_tokens : tk.row0;
+    ti.nrows = ti.bad ? 0 : tk.nrows;
     ti.ttx = p.n_shared_tt + tt;
   }
   ti.mt = r / p.ksplit;
@@ -443,6 +450,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     uint32_t stage_seq = 0;
     for (int t = t_first; t < total && !warp_abort(abort_flag); t += t_step) {
       const TileInfo ti = decode_tile<MODE, NT>(p, t);
+      if (ti.bad && lane == 0) atomicOr(p.err, ERRBIT_BAD_TILE);
       const bool dn = ti.mode == MODE_DOWN;
       const bool dn_fused = C::FUSED && dn;
       const GemmGroup& gg = dn_fused ? p.grp_dn[ti.group] : p.grp[ti.group];
