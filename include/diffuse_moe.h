@@ -156,7 +156,8 @@ dmoe_status dmoe_nccl_unique_id(void* id128);
 dmoe_status dmoe_forward(struct dmoe_layer* layer, const float* x, int64_t n_tokens, float* out,
                          const dmoe_route_out* route, void* stream, uint32_t flags);
 
-/* Waits for the layer's work, reports device-side timeouts, refreshes the statistics. */
+/* Waits for the layer's work, reports device-side timeouts (DMOE_ERR_TIMEOUT) and token tiles that
+ * the device built out of bounds (DMOE_ERR_CUDA; such a tile is skipped), refreshes the statistics. */
 dmoe_status dmoe_sync(struct dmoe_layer* layer);
 
 dmoe_status dmoe_get_stats(const struct dmoe_layer* layer, dmoe_stats* stats);
