@@ -401,6 +401,8 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   gp.err = L->err;
   gp.rows_total = rows;
   gp.n_experts = (int32_t)E_here;
+  // routed tiles index L->tiles and tt_done[sh_tt + tile]
+  gp.tiles_cap = (int32_t)std::min<int64_t>((int64_t)L->tiles_cap, (int64_t)L->tt_done_cap - sh_tt);
   if (L->has_shared) {
     gp.tm_w[0][0] = L->sgate.tm_q;
     gp.tm_w[0][1] = L->sup.tm_q;
@@ -1157,10 +1159,15 @@ dmoe_status dmoe_sync(dmoe_layer* L) {
     L->stats.ms_total = a + b + c + d;
   }
   if (e) {
+    // a timeout wins over an out-of-bounds tile (the status a caller retries on); the message
+    // names every condition that was seen
     cudaMemset(L->err, 0, 4);
-    if (e == ERRBIT_BAD_TILE)
-      return fail(DMOE_ERR_CUDA, "a device-built token tile was out of bounds and skipped (error bits 0x%x)", e);
-    return fail(DMOE_ERR_TIMEOUT, "device wait timed out (error bits 0x%x); the kernel gave up", e);
+    const bool bad = e & ERRBIT_BAD_TILE, timeout = e & ~(uint32_t)ERRBIT_BAD_TILE;
+    if (timeout)
+      return fail(DMOE_ERR_TIMEOUT, "device wait timed out; the kernel gave up%s (error bits 0x%x)",
+                  bad ? "; a device-built token tile (or tile count) was also out of bounds and skipped" : "", e);
+    return fail(DMOE_ERR_CUDA, "a device-built token tile (or tile count) was out of bounds and skipped (error bits 0x%x)",
+                e);
   }
   return DMOE_OK;
 }

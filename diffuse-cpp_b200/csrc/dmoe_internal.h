@@ -9,6 +9,8 @@
 #include <cstdint>
 #include <utility>
 
+#include "tile_check.h"
+
 namespace dmoe {
 
 // ggml_type ids of the formats on this path (ggml.h enum ggml_type)
@@ -26,15 +28,6 @@ constexpr int kMaxRanks = 32;    // expert-parallel world size limit (one mask b
 // Per-rank row offsets, passed by value to the expert-parallel kernels.
 struct RankOffsets {
   int32_t v[kMaxRanks];
-};
-
-// One token tile of one routed expert: rows [row0, row0 + nrows) of the gathered activation
-// buffer all belong to `expert`.
-struct TokTile {
-  int32_t expert;
-  int32_t row0;
-  int32_t nrows;
-  int32_t pad;
 };
 
 // A weight family processed by one GEMM launch. Group 0 is the shared expert (token rows
@@ -87,6 +80,7 @@ struct GemmParams {
   // experts [0, n_experts) of group 1; a tile outside them is skipped and reported
   int64_t rows_total;
   int32_t n_experts;
+  int32_t tiles_cap;  // capacity of `tiles` and of the routed part of `tt_done`: the count is clamped to it
 };
 
 // Router: one routing block per CTA (src/diffuse-moe-graph.cpp:203-262).

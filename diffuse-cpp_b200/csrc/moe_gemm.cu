@@ -107,9 +107,15 @@ struct TileInfo {
   int group, expert, row0, nrows, mt, k0, k1, mode, ttx, bad;
 };
 
+// routed token tiles in the device-built list, clamped to the list's capacity
+__device__ __forceinline__ int routed_tiles(const GemmParams& p) {
+  int over;
+  return tile_count_checked(*p.n_tiles, p.tiles_cap, &over);
+}
+
 __device__ __forceinline__ int tiles_in(const GemmParams& p, const GemmGroup* gr) {
   const int n0 = gr[0].present ? p.n_shared_tt * gr[0].n_mt * p.ksplit : 0;
-  const int n1 = gr[1].present ? (*p.n_tiles) * gr[1].n_mt * p.ksplit : 0;
+  const int n1 = gr[1].present ? routed_tiles(p) * gr[1].n_mt * p.ksplit : 0;
   return n0 + n1;
 }
 
@@ -150,14 +156,10 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
     per_tt = gr[1].n_mt * p.ksplit;
     const int tt = t / per_tt;
     r = t - tt * per_tt;
-    const TokTile tk = p.tiles[tt];
-    ti.bad = (tk.expert < 0 || tk.expert >= p.n_experts || tk.nrows < 0 || tk.nrows > NT ||
-              (int64_t)tk.row0 < p.n_tokens || (int64_t)tk.row0 + tk.nrows > p.rows_total)
-                 ? 1
-                 : 0;
-    ti.expert = ti.bad ? 0 : tk.expert;
-    ti.row0 = ti.bad ? (int)p.n_tokens : tk.row0;
-    ti.nrows = ti.bad ? 0 : tk.nrows;
+    const TokTile tk = tile_checked(p.tiles[tt], p.n_experts, NT, p.n_tokens, p.rows_total, &ti.bad);
+    ti.expert = tk.expert;
+    ti.row0 = tk.row0;
+    ti.nrows = tk.nrows;
     ti.ttx = p.n_shared_tt + tt;
   }
   ti.mt = r / p.ksplit;
@@ -447,6 +449,11 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     // weights read by one token tile stream through L2 (evict first); weights of experts with
     // several token tiles are re-read and kept (evict normal) -- chosen by the host
     const uint64_t pol_w = p.w_keep ? l2_policy_evict_normal() : l2_policy_evict_first();
+    if (blockIdx.x == 0 && lane == 0) {
+      int over;
+      tile_count_checked(*p.n_tiles, p.tiles_cap, &over);
+      if (over) atomicOr(p.err, ERRBIT_BAD_TILE);  // more routed tiles than the list holds
+    }
     uint32_t stage_seq = 0;
     for (int t = t_first; t < total && !warp_abort(abort_flag); t += t_step) {
       const TileInfo ti = decode_tile<MODE, NT>(p, t);

@@ -15,6 +15,7 @@
 // counters are cleared on every call, and calls that overlap on the GPU (other streams, other
 // threads) race on it.
 #include <algorithm>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -103,13 +104,23 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
     set_last_error("dmoe_route_static: n_embd must be a multiple of 256, n_expert of 4, n_expert_used <= 16");
     return DMOE_ERR_UNSUPPORTED;
   }
-  const int64_t tpb = moe_block_size > 1 ? std::max<int64_t>(moe_block_size, 32) : 32;
-  if (route_smem_bytes(tpb, n_expert) > kRouteSmemMax) {
+  // block routing switch (src/diffuse-moe-graph.cpp:215-216); without it the routing kernel
+  // runs 32-token CTAs whatever moe_block_size is
+  const bool use_block = moe_block_size > 1 && expert_capacity > 0 && expert_capacity < n_expert &&
+                         n_tokens % moe_block_size == 0;
+  if (route_smem_bytes(use_block ? moe_block_size : 32, n_expert) > kRouteSmemMax) {
     set_last_error("dmoe_route_static: moe_block_size x n_expert too large for the routing kernel");
     return DMOE_ERR_UNSUPPORTED;
   }
   if (n_tokens > 0 && (!x || !w_router || !idx || !weights)) {
     set_last_error("dmoe_route_static: null pointer");
+    return DMOE_ERR_INVALID_ARG;
+  }
+  // the logits kernel reads x with 16-byte copies and the routing kernel reads the bias as float4
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(b_router)) & 15u ||
+      (reinterpret_cast<uintptr_t>(w_router) | reinterpret_cast<uintptr_t>(idx) |
+       reinterpret_cast<uintptr_t>(weights)) & 3u) {
+    set_last_error("dmoe_route_static: x and b_router must be 16-byte aligned, w_router / idx / weights 4-byte aligned");
     return DMOE_ERR_INVALID_ARG;
   }
   if (n_tokens == 0) return DMOE_OK;
@@ -139,10 +150,7 @@ extern "C" dmoe_status dmoe_route_static(const float* x, int64_t n_tokens, int64
     ra.top_k = (int)n_expert_used;
     ra.cap = (int)expert_capacity;
     ra.blk = (int)moe_block_size;
-    ra.use_block = (moe_block_size > 1 && expert_capacity > 0 && expert_capacity < n_expert &&
-                    n_tokens % moe_block_size == 0)
-                       ? 1
-                       : 0;
+    ra.use_block = use_block ? 1 : 0;
     ra.norm_topk = norm_topk_prob;
     ra.scale = routed_scaling;
     ra.idx = idx;

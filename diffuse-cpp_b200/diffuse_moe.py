@@ -314,6 +314,25 @@ def route_static(x, w_router, b_router, hp: dict, idx, weights, stream: Optional
     idx [n, top_k] int32 and weights [n, top_k] f32. Enqueued on the current torch stream."""
     import torch
 
+    dev = None
+    for name, t, dt in (("x", x, torch.float32), ("w_router", w_router, torch.float32),
+                        ("b_router", b_router, torch.float32), ("idx", idx, torch.int32),
+                        ("weights", weights, torch.float32)):
+        if t is None and name == "b_router":
+            continue
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"route_static: {name} must be a CUDA tensor")
+        if dev is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        if t.device != dev:
+            raise ValueError(f"route_static: {name} must be a CUDA tensor on the current device {dev}")
+        if t.dtype != dt or not t.is_contiguous():
+            raise ValueError(f"route_static: {name} must be a contiguous {dt} tensor")
+    n = int(x.shape[0])
+    if (tuple(x.shape) != (n, hp["n_embd"]) or tuple(w_router.shape) != (hp["n_expert"], hp["n_embd"])
+            or tuple(idx.shape) != (n, hp["n_expert_used"]) or tuple(weights.shape) != (n, hp["n_expert_used"])
+            or (b_router is not None and tuple(b_router.shape) != (hp["n_expert"],))):
+        raise ValueError("route_static: tensor shapes do not match the layer's hyper-parameters")
     if stream is None:
         stream = torch.cuda.current_stream(x.device).cuda_stream
     _check(load().dmoe_route_static(_ptr(x), int(x.shape[0]), hp["n_embd"], _ptr(w_router), _ptr(b_router),

@@ -193,7 +193,9 @@ size_t dmoe_quantized_size(int32_t type, int64_t nrows, int64_t n_per_row);
  * before any stream capture. All calls share the array: calls that overlap on the GPU (other
  * streams or threads) race on it. Sizes above n_tokens <= DMOE_STATIC_MAX_TOKENS,
  * n_expert <= DMOE_STATIC_MAX_EXPERTS, n_embd <= DMOE_STATIC_MAX_EMBD are rejected with
- * DMOE_ERR_UNSUPPORTED; n_embd must be a multiple of 256, n_expert of 4. */
+ * DMOE_ERR_UNSUPPORTED; n_embd must be a multiple of 256, n_expert of 4. x and b_router must be
+ * 16-byte aligned and w_router, idx, weights 4-byte aligned (contiguous row-major tensors);
+ * other pointers are refused with DMOE_ERR_INVALID_ARG before any device work. */
 #define DMOE_STATIC_MAX_TOKENS 4096
 #define DMOE_STATIC_MAX_EXPERTS 256
 #define DMOE_STATIC_MAX_EMBD 8192

@@ -53,3 +53,30 @@ def test_route_static_refuses_sizes_beyond_its_scratch():
     st = lib.dmoe_route_static(None, n, 1024, None, None, 64, 8, 12, 32, 2.5, 1, None, None, None)
     assert st == 2, dm.STATUS_NAMES.get(st)  # DMOE_ERR_UNSUPPORTED
     assert "exceed the fixed scratch limits" in dm.last_error()
+
+
+def test_route_static_refuses_misaligned_pointers():
+    """x is read with 16-byte copies and the bias as float4: a pointer off that alignment (a tensor
+    view offset by one float) is refused with a status before any device work, not faulted on."""
+    lib = dm.load()
+    base = 1 << 20  # never dereferenced: the call returns before any device work
+    args = dict(n=64, h=1024, e=64)
+    for x, b in ((base + 4, base), (base, base + 8)):
+        st = lib.dmoe_route_static(x, args["n"], args["h"], base, b, args["e"], 8, 12, 32, 2.5, 1, base, base, None)
+        assert st == 1, dm.STATUS_NAMES.get(st)  # DMOE_ERR_INVALID_ARG
+        assert "16-byte aligned" in dm.last_error()
+    # a large moe_block_size is fine when block routing is off (n % block != 0): the routing kernel
+    # then runs 32-token CTAs, so the shared-memory check must not refuse it (it gets as far as the
+    # alignment check here)
+    st = lib.dmoe_route_static(base + 4, 96, 1024, base, None, 256, 8, 48, 4096, 2.5, 1, base, base, None)
+    assert st == 1 and "16-byte aligned" in dm.last_error(), dm.last_error()
+
+
+def test_route_static_python_checks_tensors():
+    """The Python binding refuses CPU, strided or wrongly typed tensors before calling the library."""
+    import torch
+
+    hp = _spec().hparams()
+    x = torch.zeros((4, hp["n_embd"]), dtype=torch.float32)
+    with pytest.raises(ValueError):
+        dm.route_static(x, x, None, hp, x, x)
