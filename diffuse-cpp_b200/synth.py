@@ -133,6 +133,16 @@ def make_layer(spec: LayerSpec) -> dict:
     return t
 
 
+_named_cache: dict = {}
+
+
+def cached_layer(name: str) -> dict:
+    """make_layer(config(name)), built once per process (the flash-shaped layers take ~30 s)."""
+    if name not in _named_cache:
+        _named_cache[name] = make_layer(config(name))
+    return _named_cache[name]
+
+
 def make_input(n: int, H: int, seed: int) -> np.ndarray:
     rng = np.random.default_rng([seed, 1])
     x = rng.standard_normal((n, H), dtype=np.float32)
