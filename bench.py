@@ -17,8 +17,14 @@ GPU); the timing is the max over ranks. N > 1 also reports `c4`: the BASELINE c4
 scaling measurement with per-rank expert loads.
 
 `--impl reference` times the reference's CPU algorithm on the host cores instead: the ggml CPU
-path cannot be built (its ggml submodule is empty), so this is the C restatement in oracle/
-(fp32, OpenMP), on a bounded sample of the same workload.
+path cannot be built (its ggml submodule is empty), so this is the oracle's ggml-faithful C
+restatement (weights in their GGUF blocks, activations rounded to Q8_K, AVX2 integer dot products,
+OpenMP on every host thread), each step a sample of the workload's blocks sized to fit a few
+minutes (the whole step when it fits).
+
+Besides the headline, the line carries `configs`: device-resident lines for BASELINE configs c1
+(small layer, F16 weights, 1 block) and c2 (small layer, q8_0 weights, 64 blocks), each with its
+HBM GB/s and fraction of the layer roofline.
 """
 from __future__ import annotations
 
@@ -119,26 +125,41 @@ def algorithmic(spec, n_tokens: int, n_active: int):
     return B, F, gateup_flops
 
 
-def run_cpu_reference(spec, t, n_tokens: int, budget_s: float = 15.0):
-    """Times the CPU restatement (oracle, fp32, all host threads) on a bounded sample of blocks.
-    Returns (tokens_per_s, cores, sample_description)."""
+def run_cpu_reference(spec, t, n_tokens: int, steps: int, warmup: int, budget_s: float):
+    """Times the reference's algorithm on the host cores: the oracle's ggml-faithful mode (the
+    ggml CPU path itself cannot be built: its submodule is empty). Weights stay in their GGUF
+    blocks, activations are rounded to the weight type's vec-dot type (Q8_K for q4_K) and every
+    dot product is an AVX2 integer block product, on all host threads; the router and the
+    routing run as in the reference. Each step is one call on a sample of the workload's routing
+    blocks, sized from a 4-block calibration call so that warmup + steps fit in budget_s (the
+    whole 256-block step when it fits). Returns (tokens_per_s, cores, sample, ms_per_step, blocks)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # CPU baseline leg only
     import synth
 
     cores = os.cpu_count() or 1
     hp = spec.hparams()
-    nblk = 1
-    done_tok, elapsed = 0, 0.0
-    while elapsed < budget_s and done_tok < n_tokens:
-        x = synth.make_input(32 * nblk, spec.H, spec.seed + 1000 + done_tok)
+    x4 = synth.make_input(128, spec.H, spec.seed + 1000)
+    oracle.layer(hp, t, x4, mode=oracle.MODE_GGML, nthreads=cores)  # page the weights in
+    t0 = time.perf_counter()
+    oracle.layer(hp, t, x4, mode=oracle.MODE_GGML, nthreads=cores)
+    per_block = (time.perf_counter() - t0) / 4
+    max_blocks = n_tokens // 32
+    blocks = int(max(1, min(max_blocks, budget_s / max(1, steps + warmup) / per_block)))
+    x = synth.make_input(32 * blocks, spec.H, spec.seed + 1001)
+    for _ in range(warmup):
+        oracle.layer(hp, t, x, mode=oracle.MODE_GGML, nthreads=cores)
+    times = []
+    for _ in range(steps):
         t0 = time.perf_counter()
-        oracle.layer(hp, t, x, mode=1, nthreads=cores)
-        dt = time.perf_counter() - t0
-        done_tok += 32 * nblk
-        elapsed += dt
-        nblk = min(nblk * 2, 16)
-    return done_tok / elapsed, cores, f"{done_tok} tokens ({done_tok // 32} blocks of the workload) in {elapsed:.1f} s"
+        oracle.layer(hp, t, x, mode=oracle.MODE_GGML, nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    mean_s = float(np.mean(times))
+    tps = 32 * blocks / mean_s
+    sample = (f"{steps} timed steps (+{warmup} warm-up) of {blocks} of the workload's {max_blocks} routing blocks "
+              f"({32 * blocks} tokens) each, {mean_s:.2f} s per step; ggml-faithful CPU restatement "
+              f"(q8_K activations, AVX2 integer dots), {cores} threads")
+    return tps, cores, sample, mean_s * 1e3, blocks
 
 
 def bench_sampler(dev, stream, peaks_hbm: float, no_cpu: bool) -> dict:
@@ -229,14 +250,18 @@ def main():
         if rank != 0:
             return
         t = synth.make_layer(spec)
-        tps, cores, sample = run_cpu_reference(spec, t, n_tok)
+        tps, cores, sample, ms_step, blocks = run_cpu_reference(spec, t, n_tok, args.steps, args.warmup,
+                                                                budget_s=150.0)
         line = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": 1000.0 * n_tok / tps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "q8_K x q4_K int8 dots, f32", "data": "synthetic",
+                "config": dict(cfg, reference_step=f"{blocks} of {n_tok // 32} blocks per step ({32 * blocks} tokens)"),
                 "impl": "reference",
                 "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
                 "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-                "note": "ggml CPU path unbuildable here (empty ggml submodule); oracle/ C restatement, fp32, OpenMP"}
+                "note": "ggml CPU path unbuildable here (empty ggml submodule); oracle/ ggml-faithful C "
+                        "restatement (weights in GGUF blocks, activations rounded to the vec-dot type, AVX2 integer "
+                        "dot products, OpenMP); ms_per_step is the time of one sampled step"}
         print(json.dumps(line))
         return
 
@@ -281,31 +306,43 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         return float(tt.item())
 
-    def time_device(n: int, steps: int, warmup: int, profile_pass: bool = True):
-        x = torch.from_numpy(synth.make_input(n, spec.H, spec.seed + 17 * rank)).to(dev)
-        out = torch.empty((n, spec.H), dtype=torch.float32, device=dev)
+    def time_layer(L, sp, n: int, steps: int, warmup: int, profile_pass: bool = True):
+        x = torch.from_numpy(synth.make_input(n, sp.H, sp.seed + 17 * rank)).to(dev)
+        out = torch.empty((n, sp.H), dtype=torch.float32, device=dev)
         for _ in range(warmup):
-            layer.forward(x, out=out)
+            L.forward(x, out=out)
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
         for _ in range(steps):
-            layer.forward(x, out=out)
+            L.forward(x, out=out)
         ev1.record(stream)
         barrier()
         ms = ev0.elapsed_time(ev1) / steps
-        layer.sync()
-        st = layer.stats()
+        L.sync()
+        st = L.stats()
         prof = None
         if profile_pass:  # per-stage CUDA events on the launching stream (separate, untimed pass)
             stages = []
             for _ in range(max(3, min(steps, 10))):
-                layer.forward(x, out=out, profile=True)
-                layer.sync()
-                stages.append(layer.stats())
+                L.forward(x, out=out, profile=True)
+                L.sync()
+                stages.append(L.stats())
             prof = {k: float(np.median([s[k] for s in stages])) for k in
                     ("ms_router", "ms_dispatch", "ms_gateup", "ms_down", "ms_total")}
         return max_over_ranks(ms), st, prof
+
+    def time_device(n: int, steps: int, warmup: int, profile_pass: bool = True):
+        return time_layer(layer, spec, n, steps, warmup, profile_pass)
+
+    def roof_entry(sp, n, ms, st, prof):
+        B, F, _ = algorithmic(sp, n, st["n_active"])
+        t_roof = max(B / (peaks_hbm * 1e9), F / (peaks["bf16_tflops"] * 1e12))
+        return {"tokens": n, "ms": ms, "tokens_per_s": n / (ms / 1e3), "hbm_gbs": B / (ms / 1e3) / 1e9,
+                "tflops": F / (ms / 1e3) / 1e12, "n_active": st["n_active"], "roofline_frac": t_roof / (ms / 1e3),
+                "bound": "hbm" if B / (peaks_hbm * 1e9) >= F / (peaks["bf16_tflops"] * 1e12) else "tensor",
+                "bytes": B, "flops": F, "stages_ms": prof, "token_tile": st["token_tile"],
+                "fused_gemm": st["fused_gemm"]}
 
     peaks_hbm = peaks["hbm_gbs"]
     sweep = []
@@ -321,6 +358,19 @@ def main():
                           "bound": "hbm" if B / (peaks_hbm * 1e9) >= F / (peaks["bf16_tflops"] * 1e12) else "tensor",
                           "stages_ms": prof, "token_tile": st["token_tile"], "ksplit": [st["ksplit_gateup"],
                                                                                         st["ksplit_down"]]})
+
+    # ---- BASELINE configs c1 (F16, 1 block) and c2 (q8_0, 64 blocks) of the small layer shape
+    configs = None
+    if not args.no_sweep and world == 1:
+        configs = {}
+        for cname, nb, what in (("c1", 1, "small layer H2048 E256 I512 Is512, F16 weights, 1 block x 32 tokens"),
+                                ("c2", 64, "small layer H2048 E256 I512 Is512, q8_0 weights, 64 blocks x 32 tokens")):
+            sp = synth.config(cname)
+            Lc = dm.MoELayer(sp.hparams(), synth.make_layer(sp))
+            ms_c, st_c, prof_c = time_layer(Lc, sp, 32 * nb, max(args.steps, 20), args.warmup)
+            configs[cname] = dict(roof_entry(sp, 32 * nb, ms_c, st_c, prof_c), workload=what)
+            Lc.close()
+            del Lc
 
     # ---- headline: device-resident throughput on this GPU's token shard
     with ClockSampler(torch.cuda.current_device()) as cs:
@@ -342,13 +392,14 @@ def main():
     e2e = {"value": n_tok * world / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(xh.nbytes),
            "d2h_bytes_per_step": int(oh.nbytes), "ms_per_step": e2e_s * 1e3}
 
-    # ---- roofline of the dominant kernel (gate/up grouped GEMM: 2/3 of the layer's flops)
+    # ---- roofline of the dominant kernel (gate/up grouped GEMM: 2/3 of the layer's flops); it is
+    # timed inside steps of a few ms, so against the burst (not the seconds-long sustained) peak
     gu_ms = prof["ms_gateup"]
     achieved = gu_flops / (gu_ms / 1e3) / 1e12
-    peak = peaks["bf16_tflops_sustained"]
+    peak = peaks["bf16_tflops"]
     roofline = {"kernel": "moe_gemm_kernel<q4_K, gate/up>", "bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic(f"gateup_{args.blocks}blk"),
-                "peak_source": f"{peaks['source']} bf16 sustained",
+                "peak_source": f"{peaks['source']} bf16 burst",
                 "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms}
     t_roof = max(B / (peaks_hbm * 1e9), F / (peaks["bf16_tflops"] * 1e12))
     layer_roof = {"bytes": B, "flops": F, "hbm_gbs": B / (ms / 1e3) / 1e9, "tflops": F / (ms / 1e3) / 1e12,
@@ -401,7 +452,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        tps, cores, sample = run_cpu_reference(spec, t, n_tok)
+        tps, cores, sample, _, _ = run_cpu_reference(spec, t, n_tok, 3, 1, budget_s=20.0)
         cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
@@ -415,6 +466,8 @@ def main():
                 "ksplit": [st["ksplit_gateup"], st["ksplit_down"]], "sweep": sweep}
         if c4 is not None:
             line["c4"] = c4
+        if configs:
+            line["configs"] = configs
         if sampler is not None:
             line["sampler"] = sampler
         print(json.dumps(line))

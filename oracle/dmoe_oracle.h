@@ -60,10 +60,18 @@ void dmoe_oracle_logits(const float* x, int64_t n, int64_t h, const float* wr, i
 int dmoe_oracle_route(const float* logits, int64_t n, int64_t e, const float* bias, int top_k, int cap, int blk,
                       int norm_topk, float scale, int32_t* idx, float* w, float* probs, uint8_t* allowed);
 
-/* expert FFN + slot sum + shared expert. mode 0: double accumulation (reference answer);
- * mode 1: float accumulation (the timed CPU baseline). Returns 0 on success. */
+/* expert FFN + slot sum + shared expert. mode 0: double accumulation on the dequantised weights
+ * (reference answer); mode 1: float accumulation on the dequantised weights; mode 2: ggml-faithful
+ * (dmoe_oracle_ggml.c: weights stay in their blocks, activations rounded to the weight type's
+ * vec-dot type, integer block dot products; the timed CPU baseline). Returns 0 on success. */
 int dmoe_oracle_experts(const orc_layer* L, const float* x, int64_t n, const int32_t* idx, const float* w, float* out,
                         int mode, int nthreads);
+int dmoe_oracle_experts_ggml(const orc_layer* L, const float* x, int64_t n, const int32_t* idx, const float* w,
+                             float* out, int nthreads);
+/* unit-test hooks of the ggml-faithful mode: nrows weight rows . x rounded to the vec-dot type
+ * (SIMD or scalar kernel), and x rounded to the vec-dot type and widened back to float */
+int dmoe_oracle_ggml_dot(int type, const void* w, int64_t nrows, int64_t k, const float* x, float* out, int simd);
+int dmoe_oracle_ggml_round_act(int type, const float* x, int64_t k, float* out);
 
 /* Greedy sampler step, src/diffuse-sampler.cpp:29-49,183-237 (dmoe_oracle_sampler.c):
  * per masked position the argmax (strict `>` scan) and 1 / sum_v expf(l_v - max) summed in float

@@ -74,6 +74,7 @@ static void swiglu(const float* Wg, const float* Wu, const float* Wd, int64_t H,
 
 int dmoe_oracle_experts(const orc_layer* L, const float* x, int64_t n, const int32_t* idx, const float* w, float* out,
                         int mode, int nthreads) {
+  if (mode == 2) return dmoe_oracle_experts_ggml(L, x, n, idx, w, out, nthreads);
   const int64_t H = L->H, I = L->I, E = L->E, K = L->top_k, Is = L->Is;
   const size_t rs_h = dmoe_oracle_row_size(L->expert_type, H);
   const size_t rs_i = dmoe_oracle_row_size(L->expert_type, I);

@@ -75,6 +75,10 @@ def load() -> ctypes.CDLL:
     lib.dmoe_oracle_experts.argtypes = [ctypes.POINTER(OrcLayer), P, ctypes.c_int64, P, P, P, ctypes.c_int,
                                         ctypes.c_int]
     lib.dmoe_oracle_experts.restype = ctypes.c_int
+    lib.dmoe_oracle_ggml_dot.argtypes = [ctypes.c_int, P, ctypes.c_int64, ctypes.c_int64, P, P, ctypes.c_int]
+    lib.dmoe_oracle_ggml_dot.restype = ctypes.c_int
+    lib.dmoe_oracle_ggml_round_act.argtypes = [ctypes.c_int, P, ctypes.c_int64, P]
+    lib.dmoe_oracle_ggml_round_act.restype = ctypes.c_int
     lib.dmoe_oracle_sample_step.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.c_float, P, P]
     lib.dmoe_oracle_sample_step.restype = ctypes.c_int32
@@ -127,9 +131,35 @@ def route(lg: np.ndarray, bias, top_k: int, cap: int, blk: int, norm_topk: int =
     return idx, w, probs, (allowed[:nb] if used else None), bool(used)
 
 
+MODE_EXACT, MODE_F32, MODE_GGML = 0, 1, 2
+
+
+def ggml_dot(qtype: int, w: np.ndarray, k: int, x: np.ndarray, simd: bool = True) -> np.ndarray:
+    """Weight rows (GGUF bytes [rows, row_bytes]) . x rounded to the vec-dot type, as the
+    ggml-faithful mode computes them (SIMD or scalar kernel)."""
+    w = np.ascontiguousarray(w)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(w.shape[0], np.float32)
+    if load().dmoe_oracle_ggml_dot(qtype, w.ctypes.data, w.shape[0], k, x.ctypes.data, out.ctypes.data,
+                                   1 if simd else 0) != 0:
+        raise ValueError("ggml_dot failed")
+    return out
+
+
+def ggml_round_act(qtype: int, x: np.ndarray) -> np.ndarray:
+    """x rounded to the vec-dot type of weight type qtype (Q8_K / Q8_0 / F16), widened to float."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    if load().dmoe_oracle_ggml_round_act(qtype, x.ctypes.data, x.size, out.ctypes.data) != 0:
+        raise ValueError("ggml_round_act failed")
+    return out
+
+
 def experts(hp: dict, t: dict, x: np.ndarray, idx: np.ndarray, w: np.ndarray, mode: int = 0,
             nthreads: int = 0) -> np.ndarray:
-    """Routed experts + slot sum + shared expert for the given routing. mode 0: double accumulation."""
+    """Routed experts + slot sum + shared expert for the given routing. mode 0: double
+    accumulation (the reference answer); 1: float accumulation; 2: ggml-faithful (activations
+    rounded to the weight type's vec-dot type, integer block dot products)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     idx = np.ascontiguousarray(idx, dtype=np.int32)
     w = np.ascontiguousarray(w, dtype=np.float32)

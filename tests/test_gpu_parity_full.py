@@ -69,10 +69,16 @@ def check_full(name: str, n: int, seed_off: int, want_nt: int, want_router_parts
     err = rel_l2(out[rows], r_out)
     per_block = [rel_l2(out[b * spec.blk:(b + 1) * spec.blk], r_out[i * spec.blk:(i + 1) * spec.blk])
                  for i, b in enumerate(blocks)]
+    # what the reference's ggml CPU backend would output (activations rounded to Q8_K)
+    g_out = oracle.experts(hp, t, x[rows], r_idx[rows], r_w[rows], mode=oracle.MODE_GGML)
+    err_g_exact, err_vs_g = rel_l2(g_out, r_out), rel_l2(out[rows], g_out)
     print(f"{name} {n} tokens: rel L2 {err:.3e} on blocks {blocks}; worst block {max(per_block):.3e}; "
-          f"distinct experts {len(np.unique(idx))}")
+          f"distinct experts {len(np.unique(idx))}; ggml-faithful vs exact {err_g_exact:.3e}, "
+          f"GPU vs ggml-faithful {err_vs_g:.3e}")
     assert err <= TOL_Q, f"rel L2 {err:.3e} > {TOL_Q}"
     assert max(per_block) <= TOL_Q, f"worst block rel L2 {max(per_block):.3e} > {TOL_Q}"
+    # the GPU path (fp16 activations) is closer to the exact answer than ggml's 8-bit activations
+    assert err < err_g_exact
     return idx
 
 
