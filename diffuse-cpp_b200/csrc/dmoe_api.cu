@@ -483,7 +483,46 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   dp.tm_w[1][0] = L->down.tm_q;
   dp.tm_s[1][0] = L->down.tm_s;
   fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair_dn));
-  if (fused) {
+  // Down GEMM with resident activation tiles (BRES, off by default): each CTA holds 64 token rows
+  // of h (all of K <= 1024, 128 KB) in shared memory and runs every 256-row m-tile of the down
+  // matrix against them, instead of re-reading the activation tile from L2 for each m-tile.
+  // DMOE_BRES = 1: at NT = 128 as CTA pairs (each CTA keeps its 64-row half; one 128-row block per
+  // CTA leaves room for five 18 KB weight stages); 2: also single CTAs on 64-token tiles (128-row
+  // list tiles as two halves, two weight stages). Measured on B200 (c3, ncu at 4096 tokens): the
+  // L2-to-SM reads fall from 4.40 to 1.18 GB per launch, but the launch takes 706 against 566 us
+  // (8192 tokens: 1.26 against ~1.0 ms; 2048 tokens single-CTA: 0.43 against 0.32 ms): the down
+  // GEMM is bound by its dequant issue rate (issue 55-57 % active, tensor pipe 34-38 %), not by
+  // L2, and the unit boundaries drain the pipeline.
+  const bool quant_dn = L->etype != DMOE_TYPE_F16;
+  const int bres_env = env_int("DMOE_BRES", 0);
+  const bool bres_ok = !fused && same_type && quant_dn && ks_dn == 1 &&
+                       std::max(L->I, L->has_shared ? L->Is : 0) <= kBresK;
+  const bool bres_pair = bres_ok && bres_env >= 1 && nt == 2 * kBresNT && use_pair(L, nt, MODE_GATEUP);
+  const bool bres = bres_pair || (bres_ok && bres_env >= 2 && (nt == kBresNT || nt == 2 * kBresNT));
+  if (bres) {
+    CUtensorMap tm_h64;
+    if ((s = make_map(&tm_h64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, L->hbuf, (uint64_t)Imax, (uint64_t)rows,
+                      (uint64_t)Imax * 2, 64, (uint32_t)kBresNT, CU_TENSOR_MAP_SWIZZLE_128B)) != DMOE_OK)
+      return s;
+    GemmParams bp = dp;
+    bp.tm_b = tm_h64;
+    const int bnt = bres_pair ? 2 * kBresNT : kBresNT;  // token rows per tile of the launch
+    bp.tile_div = nt / bnt;
+    bp.n_shared_tt = L->has_shared ? (int32_t)((n_sh + bnt - 1) / bnt) : 0;
+    fill_group(bp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, bnt, bres_pair));
+    if (L->has_shared) fill_group(bp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, bnt, bres_pair));
+    // m-chunks per token tile: whole token tiles while they give every SM (pair) about three units
+    const int n_mt = bp.grp[1].n_mt;
+    const int64_t units = bp.n_shared_tt + tt_est * bp.tile_div;
+    const int64_t workers = bres_pair ? L->sms / 2 : L->sms;
+    int chunks = 1;
+    while (chunks < 4 && n_mt % (2 * chunks) == 0 && units * chunks < 3 * workers) chunks *= 2;
+    if (const int fc = env_int("DMOE_BRES_CHUNKS", 0); fc == 1 || fc == 2 || fc == 4 || fc == 8)
+      if (n_mt % fc == 0) chunks = fc;
+    bp.bres_chunks = chunks;
+    DMOE_CUDA(launch_moe_gemm_bres(L->etype, bres_pair, ndq, bp, grid, st));
+    ++kernels;
+  } else if (fused) {
     GemmParams fp = gp;  // gate/up operands and tiles ...
     fp.tm_b_dn = dp.tm_b;  // ... then the down phase's
     fp.tm_w_dn[0] = dp.tm_w[0][0];

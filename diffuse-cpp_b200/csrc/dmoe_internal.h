@@ -81,6 +81,10 @@ struct GemmParams {
   int64_t rows_total;
   int32_t n_experts;
   int32_t tiles_cap;  // capacity of `tiles` and of the routed part of `tt_done`: the count is clamped to it
+  // resident-activation down launches (BRES): each routed list tile splits into tile_div tiles of
+  // the launch's NT rows; a unit (group, token tile) runs its m-tiles in bres_chunks chunks
+  int32_t tile_div;
+  int32_t bres_chunks;
 };
 
 // Router: one routing block per CTA (src/diffuse-moe-graph.cpp:203-262).
@@ -139,6 +143,13 @@ cudaError_t launch_swiglu_finish(const float* gu, int64_t gu_half, int64_t rows,
 cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, bool pair, const GemmParams& p, int grid,
                             cudaStream_t st);
 bool gemm_pair_ok(int wtype, int mode, int nt);
+// down launch with resident activation tiles (quantised weights), kBresNT token rows per CTA,
+// K <= kBresK: single CTAs on token tiles of kBresNT rows, or (pair) CTA pairs on token tiles of
+// 2 kBresNT rows; p.tile_div = list tile rows / launch tile rows, p.bres_chunks = m-chunks per
+// token tile
+constexpr int kBresNT = 64;
+constexpr int kBresK = 1024;
+cudaError_t launch_moe_gemm_bres(int wtype, bool pair, int ndq, const GemmParams& p, int grid, cudaStream_t st);
 int gemm_stage_k(int wtype);
 int gemm_out_rows(int mode, int nt, bool pair);  // output rows per tile of one expert matrix
 

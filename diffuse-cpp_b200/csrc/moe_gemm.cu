@@ -40,11 +40,21 @@ namespace dmoe {
 // half of the NT tokens; the leader (rank 0) issues the MMAs, which read both CTAs' halves and
 // write each CTA's 128 rows x NT accumulator. Each activation tile then crosses L2 once per 256
 // rows instead of once per 128. Quantised weights at NT = 128 only.
-template <int WT, int MODE, int NT, int NDQ_ = 2, bool PAIR_ = false>
+// BRES (down launches, quantised weights, NT = 64): the CTA keeps one token tile's activations
+// (NT rows x K <= kBresK, 128 KB) resident in shared memory and runs every 256-row m-tile of the
+// down matrix against it, so the activations cross L2 once per token tile instead of once per
+// m-tile; the stage ring carries weights only. The CTA walks whole units (group, token tile,
+// m-chunk) of consecutive m-tiles.
+static_assert(kBresK == 1024 && kBresNT == 64, "the host's BRES limits (dmoe_internal.h) match the kernel's");
+
+template <int WT, int MODE, int NT, int NDQ_ = 2, bool PAIR_ = false, bool BRES_ = false>
 struct GemmCfg {
   static constexpr bool QUANT = (WT != WT_F16);
   static constexpr bool FUSED = MODE == MODE_FUSED;
   static constexpr bool PAIR = PAIR_;
+  static constexpr bool BRES = BRES_;
+  static_assert(!BRES || (QUANT && MODE == MODE_DOWN && ((NT == kBresNT && !PAIR) || (NT == 2 * kBresNT && PAIR))),
+                "resident activation tiles: quantised down launches, 64 token rows per CTA");
   static constexpr int B_ROWS = PAIR ? NT / 2 : NT;  // token rows of B this CTA loads
   // two weight tiles share each activation (B) tile: gate and up, or (down, NT <= 64) two
   // adjacent 128-row blocks of the down matrix, so B crosses L2 once per 256 output rows. At
@@ -63,7 +73,10 @@ struct GemmCfg {
   // per matrix per stage: q4_K 128 rows x one 144 B super-block; q8_0 128 x 128 int8 (SW128)
   // + 128 x 4 fp32 scales; f16 two SW128 boxes of 128 x 64.
   static constexpr int W_BYTES = (WT == WT_Q4_K) ? 128 * 144 : (WT == WT_Q8_0) ? (128 * 128 + 128 * 16) : (128 * 128 * 2);
-  static constexpr int STAGE_BYTES = B_BYTES + MATS * W_BYTES;
+  // BRES: the resident activation tile, K / 64 128B-swizzled boxes of NT rows, before the ring
+  static constexpr int BRES_BYTES = BRES ? kBresK * B_ROWS * 2 : 0;
+  static constexpr int STAGE_B = BRES ? 0 : B_BYTES;  // activation bytes carried by each stage
+  static constexpr int STAGE_BYTES = STAGE_B + MATS * W_BYTES;
   // roles: warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 epilogue (two per TMEM lane
   // quarter, one per column half), then NDQ dequant warpgroups
   static constexpr int NDQ = QUANT ? NDQ_ : 0;
@@ -71,7 +84,7 @@ struct GemmCfg {
   static constexpr int THREADS = 32 * (DQ_WARP0 + 4 * NDQ);
   static constexpr int EPI_COLS = NT / 2;  // accumulator columns per epilogue warp
   static constexpr int SMEM_BUDGET = 227 * 1024 - 2048;
-  static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES_RAW = (SMEM_BUDGET - BRES_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
   // TMEM: accumulators (double-buffered when they fit next to a 2+ deep A ring), A ring
   static constexpr int ACC_COLS = MATS * NT;
@@ -79,7 +92,7 @@ struct GemmCfg {
   static constexpr int ACC_BUFS = (2 * ACC_COLS + (QUANT ? 2 * A_COLS : 0) <= 512) ? 2 : 1;
   static constexpr int NA_RAW = QUANT ? (512 - ACC_BUFS * ACC_COLS) / A_COLS : 0;
   static constexpr int NA = NA_RAW > 4 ? 4 : NA_RAW;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = BRES_BYTES + STAGES * STAGE_BYTES + 1024 + 256;
   // gate/up launches: dequant warps convert a k-block's first matrix into 64 registers before
   // its A buffer is free, where the launch leaves each thread the registers (two dequant
   // warpgroups: 576 threads, up to 112 registers each). Measured on B200: gate/up 492 -> 471 us
@@ -89,7 +102,8 @@ struct GemmCfg {
   static constexpr int EMPTY_COUNT = 1 + 4 * NDQ;
   static_assert(STAGES >= 2, "smem ring needs two stages");
   static_assert(!QUANT || NA >= 2, "TMEM A ring needs two buffers");
-  static_assert(B_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1024-B aligned stage parts");
+  static_assert(B_BYTES % 1024 == 0 && W_BYTES % 1024 == 0 && BRES_BYTES % 1024 == 0, "1024-B aligned stage parts");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
   static_assert(NT % 32 == 0 && NT >= 32 && NT <= 256, "tcgen05 M=128 needs N % 16 == 0; two column halves");
   static_assert(ACC_BUFS * ACC_COLS + NA * A_COLS <= 512, "TMEM budget");
   // The dequant warpgroups share the A ring round-robin (k-block kbs -> group kbs % NDQ,
@@ -103,8 +117,11 @@ struct GemmCfg {
 // the fused launch's completion counters (shared tiles first, then routed)
 // bad: a routed tile whose rows or expert fall outside the buffers (a corrupt tile list); it is
 // decoded as an empty tile, so every role skips it the same way, and the producer reports it
+// BRES walk: skip = no work at this index (past the last unit, or the empty half of a list tile:
+// every role skips it alike); bfirst / blast = first / last m-tile of its unit (the producer
+// loads the unit's activation tile before the first, the MMA releases it after the last)
 struct TileInfo {
-  int group, expert, row0, nrows, mt, k0, k1, mode, ttx, bad;
+  int group, expert, row0, nrows, mt, k0, k1, mode, ttx, bad, skip, bfirst, blast;
 };
 
 // routed token tiles in the device-built list, clamped to the list's capacity
@@ -167,6 +184,74 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
   const int ksz = gr[ti.group].k_stages / p.ksplit;
   ti.k0 = ks * ksz;
   ti.k1 = ti.k0 + ksz;
+  ti.skip = 0;
+  ti.bfirst = ti.blast = 0;
+  return ti;
+}
+
+// ---- BRES walk (resident activation tiles; down launches, no split-K) -----------------------
+// Units: (group 0, shared token tile, chunk) first, then (group 1, routed token tile, chunk),
+// a routed list tile of NT * tile_div rows giving tile_div token tiles of NT rows. Every unit
+// has mpu = n_mt / bres_chunks consecutive m-tiles. CTA b of G takes units b, b + G, ... and
+// runs each unit's m-tiles in order: walk index t = b + G k holds m-tile k % mpu of unit
+// b + G (k / mpu).
+__device__ __forceinline__ int bres_units(const GemmParams& p) {
+  const int u0 = p.grp[0].present ? p.n_shared_tt * p.bres_chunks : 0;
+  const int u1 = p.grp[1].present ? routed_tiles(p) * p.tile_div * p.bres_chunks : 0;
+  return u0 + u1;
+}
+__device__ __forceinline__ int bres_mpu(const GemmParams& p) {
+  return (p.grp[0].present ? p.grp[0].n_mt : p.grp[1].n_mt) / p.bres_chunks;
+}
+__device__ __forceinline__ int bres_total(const GemmParams& p, int G) {
+  return (bres_units(p) + G - 1) / G * G * bres_mpu(p);
+}
+
+template <int NT>
+__device__ __forceinline__ TileInfo decode_tile_bres(const GemmParams& p, int t, int G) {
+  TileInfo ti;
+  ti.bad = 0;
+  ti.mode = MODE_DOWN;
+  ti.ttx = 0;
+  const int mpu = bres_mpu(p);
+  const int b = t % G, k = t / G;
+  int u = b + (k / mpu) * G;
+  const int j = k % mpu;
+  ti.bfirst = j == 0;
+  ti.blast = j == mpu - 1;
+  ti.skip = u >= bres_units(p);
+  const int u0 = p.grp[0].present ? p.n_shared_tt * p.bres_chunks : 0;
+  int tt, c;
+  if (!ti.skip && u < u0) {
+    ti.group = 0;
+    tt = u / p.bres_chunks;
+    c = u - tt * p.bres_chunks;
+    ti.expert = 0;
+    ti.row0 = tt * NT;
+    const int64_t left = p.n_tokens - (int64_t)ti.row0;
+    ti.nrows = left < NT ? (int)left : NT;
+  } else {
+    u -= u0;
+    ti.group = 1;
+    tt = ti.skip ? 0 : u / p.bres_chunks;
+    c = ti.skip ? 0 : u - tt * p.bres_chunks;
+    const int tl = tt / p.tile_div, half = tt - tl * p.tile_div;
+    if (ti.skip) {
+      ti.expert = 0;
+      ti.row0 = (int)p.n_tokens;
+      ti.nrows = 0;
+    } else {
+      const TokTile tk = tile_checked(p.tiles[tl], p.n_experts, NT * p.tile_div, p.n_tokens, p.rows_total, &ti.bad);
+      ti.expert = tk.expert;
+      ti.row0 = tk.row0 + half * NT;
+      const int left = tk.nrows - half * NT;
+      ti.nrows = left < 0 ? 0 : (left < NT ? left : NT);
+      ti.skip = ti.nrows == 0;  // the empty half of a short list tile, or a tile out of bounds
+    }
+  }
+  ti.mt = c * mpu + j;
+  ti.k0 = 0;
+  ti.k1 = p.grp[ti.group].k_stages;
   return ti;
 }
 
@@ -343,14 +428,17 @@ __device__ __forceinline__ float silu_f(float g) { return g * __frcp_rn(1.0f + _
 
 __device__ __forceinline__ int quad_swap(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
 
-template <int WT, int MODE, int NT, int NDQ_, bool PAIR>
-__global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
+template <int WT, int MODE, int NT, int NDQ_, bool PAIR, bool BRES = false>
+__global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR, BRES>::THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p) {
-  using C = GemmCfg<WT, MODE, NT, NDQ_, PAIR>;
+  using C = GemmCfg<WT, MODE, NT, NDQ_, PAIR, BRES>;
   static_assert(C::RING_OK, "A ring needs at least one buffer per dequant warpgroup");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  // layout: [BRES: resident activation tile] [stage ring] [barriers]
+  uint8_t* bres = smem;
+  uint8_t* ring = smem + C::BRES_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + C::STAGES * C::STAGE_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = full + C::STAGES;
   uint64_t* afull = empty + C::STAGES;
@@ -358,7 +446,10 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
   uint64_t* accfull = aempty + 4;
   uint64_t* accempty = accfull + 2;
   uint64_t* full_b = accempty + 2;  // PAIR: both CTAs' activation halves landed (leader's copy counts)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full_b + (C::PAIR ? C::STAGES : 0));
+  // BRES: the resident tile has landed (TMA bytes) / is free again (MMA commit after a unit)
+  uint64_t* bfull = full_b + (C::PAIR ? C::STAGES : 0);
+  uint64_t* bempty = bfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bempty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -405,6 +496,8 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     }
     if (C::PAIR)
       for (int s = 0; s < C::STAGES; ++s) mbar_init(&full_b[s], 1);
+    mbar_init(bfull, 1);
+    mbar_init(bempty, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -435,13 +528,18 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
   // everything above overlaps the previous kernel's tail; global memory only after this
   pdl_wait();
   pdl_trigger();
-  const int total = tiles_total<MODE>(p);
-  // tile walk: one CTA per SM, or (PAIR) one pair per two SMs, both CTAs on the same tiles
+  // tile walk: one CTA per SM, or (PAIR) one pair per two SMs, both CTAs on the same tiles;
+  // BRES: whole units per CTA (decode_tile_bres)
   const int t_first = C::PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int t_step = C::PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int total = C::BRES ? bres_total(p, t_step) : tiles_total<MODE>(p);
+  auto decode = [&](int t) -> TileInfo {
+    if constexpr (C::BRES) return decode_tile_bres<NT>(p, t, t_step);
+    else return decode_tile<MODE, NT>(p, t);
+  };
 
-  auto stage_ptr = [&](int s) -> uint8_t* { return smem + s * C::STAGE_BYTES; };
-  auto wtile_ptr = [&](int s, int m) -> uint8_t* { return smem + s * C::STAGE_BYTES + C::B_BYTES + m * C::W_BYTES; };
+  auto stage_ptr = [&](int s) -> uint8_t* { return ring + s * C::STAGE_BYTES; };
+  auto wtile_ptr = [&](int s, int m) -> uint8_t* { return ring + s * C::STAGE_BYTES + C::STAGE_B + m * C::W_BYTES; };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -454,10 +552,30 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
       tile_count_checked(*p.n_tiles, p.tiles_cap, &over);
       if (over) atomicOr(p.err, ERRBIT_BAD_TILE);  // more routed tiles than the list holds
     }
-    uint32_t stage_seq = 0;
+    uint32_t stage_seq = 0, unit_seq = 0;
     for (int t = t_first; t < total && !warp_abort(abort_flag); t += t_step) {
-      const TileInfo ti = decode_tile<MODE, NT>(p, t);
+      const TileInfo ti = decode(t);
       if (ti.bad && lane == 0) atomicOr(p.err, ERRBIT_BAD_TILE);
+      if (ti.skip) continue;
+      if (C::BRES && ti.bfirst) {
+        // the unit's activation tile: all K of its NT rows, once the previous unit's MMAs are done
+        // (PAIR: each CTA its half of the rows, counted on the leader's bfull, armed by the leader)
+        if (!wbwait(bempty, (unit_seq & 1u) ^ 1u, ERRBIT_TIMEOUT_EMPTY)) break;
+        if (elect_one()) {
+          const int nbox = p.grp[ti.group].k_stages * C::STAGE_K / 64;
+          if constexpr (C::PAIR) {
+            if (rank == 0) mbar_arrive_expect_tx(bfull, (uint32_t)(2 * nbox * C::B_ROWS * 128));
+            for (int bx = 0; bx < nbox; ++bx)
+              tma_load_2d_pair(bres + bx * C::B_ROWS * 128, &p.tm_b, bx * 64, ti.row0 + (int)rank * C::B_ROWS,
+                               leader(bfull));
+          } else {
+            mbar_arrive_expect_tx(bfull, (uint32_t)(nbox * NT * 128));
+            for (int bx = 0; bx < nbox; ++bx) tma_load_2d(bres + bx * NT * 128, &p.tm_b, bx * 64, ti.row0, bfull);
+          }
+        }
+        __syncwarp();
+        ++unit_seq;
+      }
       const bool dn = ti.mode == MODE_DOWN;
       const bool dn_fused = C::FUSED && dn;
       const GemmGroup& gg = dn_fused ? p.grp_dn[ti.group] : p.grp[ti.group];
@@ -479,16 +597,20 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
             // weights count on this CTA's full[s]; both CTAs' activation halves on the leader's
             // full_b[s] (its expected bytes are armed by the leader alone)
             mbar_arrive_expect_tx(&full[s], C::MATS * C::W_BYTES);
-            if (rank == 0) mbar_arrive_expect_tx(&full_b[s], 2 * C::B_BYTES);
+            if constexpr (!C::BRES) {
+              if (rank == 0) mbar_arrive_expect_tx(&full_b[s], 2 * C::B_BYTES);
 #pragma unroll
-            for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
-              tma_load_2d_pair(stage_ptr(s) + bx * C::B_ROWS * 128, tmb, kc * C::STAGE_K + bx * 64,
-                               ti.row0 + (int)rank * C::B_ROWS, leader(&full_b[s]));
+              for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
+                tma_load_2d_pair(stage_ptr(s) + bx * C::B_ROWS * 128, tmb, kc * C::STAGE_K + bx * 64,
+                                 ti.row0 + (int)rank * C::B_ROWS, leader(&full_b[s]));
+            }
           } else {
             mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+            if constexpr (!C::BRES) {
 #pragma unroll
-            for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
-              tma_load_2d(stage_ptr(s) + bx * NT * 128, tmb, kc * C::STAGE_K + bx * 64, ti.row0, &full[s]);
+              for (int bx = 0; bx < C::STAGE_K / 64; ++bx)
+                tma_load_2d(stage_ptr(s) + bx * NT * 128, tmb, kc * C::STAGE_K + bx * 64, ti.row0, &full[s]);
+            }
           }
 #pragma unroll
           for (int m = 0; m < C::MATS; ++m) {
@@ -524,12 +646,17 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     // memory) halves at the same addresses and write both CTAs' accumulators, and its commits
     // arrive on the barriers of both CTAs.
     constexpr uint32_t idesc = idesc_f16_f32(C::PAIR ? 256 : 128, NT);
-    uint32_t stage_seq = 0, tile_seq = 0;
+    uint32_t stage_seq = 0, tile_seq = 0, unit_seq = 0;
     for (int t = t_first; t < total && !warp_abort(abort_flag) && (!C::PAIR || rank == 0); t += t_step) {
-      const TileInfo ti = decode_tile<MODE, NT>(p, t);
+      const TileInfo ti = decode(t);
+      if (ti.skip) continue;
       const int ab = tile_seq % C::ACC_BUFS;
       const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
       if (!wbwait(&accempty[ab], aph ^ 1u, ERRBIT_TIMEOUT_TMEM)) break;
+      if (C::BRES && ti.bfirst) {
+        if (!wbwait(bfull, unit_seq & 1u, ERRBIT_TIMEOUT_FULL)) break;
+        ++unit_seq;
+      }
       tc_fence_after();
       const uint32_t dbase = tbase + ab * C::ACC_COLS;
       bool first = true;
@@ -537,11 +664,17 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
       for (int kc = ti.k0; kc < ti.k1 && ok; ++kc) {
         const int s = stage_seq % C::STAGES;
         const uint32_t ph = (stage_seq / C::STAGES) & 1u;
-        if (!wbwait(C::PAIR ? &full_b[s] : &full[s], ph, ERRBIT_TIMEOUT_FULL)) { ok = false; break; }
+        // a pair's stage carries only weights under BRES, which reach the MMA through the dequant
+        // warps' afull arrivals: nothing to wait for here
+        if constexpr (!(C::PAIR && C::BRES)) {
+          if (!wbwait(C::PAIR ? &full_b[s] : &full[s], ph, ERRBIT_TIMEOUT_FULL)) { ok = false; break; }
+        }
         tc_fence_after();
         // Shared-memory descriptors are built once per stage; each (k-block, k-step) slice adds
         // a compile-time offset to the 14-bit start-address field (no carry: smem < 256 KB).
-        const uint64_t bdesc0 = sdesc_sw128(smem_u32(stage_ptr(s)), 1024);
+        // BRES: the stage's K range of the resident tile (boxes of 64 K, B_ROWS rows each).
+        const uint64_t bdesc0 = sdesc_sw128(
+            C::BRES ? smem_u32(bres + kc * (C::STAGE_K / 64) * C::B_ROWS * 128) : smem_u32(stage_ptr(s)), 1024);
         const uint32_t acc_first = first ? 0u : 1u;
         if constexpr (C::QUANT) {
 #pragma unroll
@@ -601,6 +734,11 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
       if (elect_one()) {
         if constexpr (C::PAIR) mma_commit_pair(&accfull[ab]);
         else mma_commit(&accfull[ab]);
+        // BRES: after the unit's last m-tile the resident tile may be overwritten
+        if (C::BRES && ti.blast) {
+          if constexpr (C::PAIR) mma_commit_pair(bempty);  // both CTAs' halves are free
+          else mma_commit(bempty);
+        }
       }
       __syncwarp();
       ++tile_seq;
@@ -617,7 +755,8 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint32_t tile_seq = 0;
     for (int t = t_first; t < total && !*abort_flag; t += t_step) {
-      const TileInfo ti = decode_tile<MODE, NT>(p, t);
+      const TileInfo ti = decode(t);
+      if (ti.skip) continue;
       const int ab = tile_seq % C::ACC_BUFS;
       const uint32_t aph = (tile_seq / C::ACC_BUFS) & 1u;
       float wv[NWR];
@@ -760,7 +899,8 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
     uint32_t stage_seq = 0;
     bool ok = true;
     for (int t = t_first; t < total && ok && !*abort_flag; t += t_step) {
-      const TileInfo ti = decode_tile<MODE, NT>(p, t);
+      const TileInfo ti = decode(t);
+      if (ti.skip) continue;
       for (int kc = ti.k0; kc < ti.k1; ++kc) {
         const int s = stage_seq % C::STAGES;
         const uint32_t ph = (stage_seq / C::STAGES) & 1u;
@@ -816,10 +956,10 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR>::THREADS, 1)
 // ------------------------------------------------------------------------------------------
 // launcher
 // ------------------------------------------------------------------------------------------
-template <int WT, int MODE, int NT, int NDQ, bool PAIR>
+template <int WT, int MODE, int NT, int NDQ, bool PAIR, bool BRES = false>
 static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t st) {
-  using C = GemmCfg<WT, MODE, NT, NDQ, PAIR>;
-  auto kern = moe_gemm_kernel<WT, MODE, NT, NDQ, PAIR>;
+  using C = GemmCfg<WT, MODE, NT, NDQ, PAIR, BRES>;
+  auto kern = moe_gemm_kernel<WT, MODE, NT, NDQ, PAIR, BRES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   if constexpr (!PAIR) {
@@ -916,6 +1056,28 @@ cudaError_t launch_moe_gemm(int wtype, int mode, int nt, int ndq, bool pair, con
 }
 
 bool gemm_pair_ok(int wtype, int mode, int nt) { return wtype != WT_F16 && mode != MODE_FUSED && nt == 128; }
+
+cudaError_t launch_moe_gemm_bres(int wtype, bool pair, int ndq, const GemmParams& p, int grid, cudaStream_t st) {
+  if (p.ksplit != 1 || p.tile_div < 1 || p.bres_chunks < 1) return cudaErrorInvalidValue;
+  if (pair) {
+    // NT = 128 split over the pair, one 128-row block per CTA: the A ring has room for 4 dequant
+    // warpgroups
+    switch (wtype) {
+      case WT_Q4_K:
+        return ndq >= 4 ? launch_one<WT_Q4_K, MODE_DOWN, 2 * kBresNT, 4, true, true>(p, grid, st)
+                        : launch_one<WT_Q4_K, MODE_DOWN, 2 * kBresNT, 2, true, true>(p, grid, st);
+      case WT_Q8_0:
+        return ndq >= 4 ? launch_one<WT_Q8_0, MODE_DOWN, 2 * kBresNT, 4, true, true>(p, grid, st)
+                        : launch_one<WT_Q8_0, MODE_DOWN, 2 * kBresNT, 2, true, true>(p, grid, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  switch (wtype) {
+    case WT_Q4_K: return launch_one<WT_Q4_K, MODE_DOWN, kBresNT, 2, false, true>(p, grid, st);
+    case WT_Q8_0: return launch_one<WT_Q8_0, MODE_DOWN, kBresNT, 2, false, true>(p, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 int gemm_stage_k(int wtype) { return wtype == WT_Q4_K ? 256 : 128; }
 

@@ -268,3 +268,263 @@ def test_pair_model_catches_a_short_ring():
     cfg = dict(stages=3, na=2, ndq=4, kb=2, acc_bufs=1, quant=True, ring_ok=False)
     results = [run(cfg, [16, 16], seed, pair=True) for seed in range(25)]
     assert any(r and "alias" in r for r in results)
+
+
+def gemm_cfg_bres(wt):
+    """GemmCfg<WT, MODE_DOWN, 64, 2, false, BRES = true>: the resident activation tile (64 rows x
+    1024 K fp16 = 128 KB) comes off the shared-memory budget, the stages carry weights only."""
+    stage_k = 256 if wt == Q4_K else 128
+    w_bytes = 128 * 144 if wt == Q4_K else 128 * 128 + 128 * 16
+    stages = min(6, (227 * 1024 - 2048 - 1024 * 64 * 2) // (2 * w_bytes))
+    na = min(4, (512 - 2 * 128) // 128)
+    return dict(stages=stages, na=na, ndq=2, kb=stage_k // 128, acc_bufs=2, quant=True, ring_ok=na >= 2)
+
+
+def roles_bres(cfg, units):
+    """The single-CTA roles plus the resident tile: `units` is a list of (m-tiles, k-stages per
+    m-tile). The producer waits bempty before each unit's activation load and arrives (TMA bytes)
+    on bfull; the MMA waits bfull before a unit's first m-tile and commits bempty after its last."""
+    S, NA, NDQ, KB, ACCB = cfg["stages"], cfg["na"], cfg["ndq"], cfg["kb"], cfg["acc_bufs"]
+    full = [Bar(f"full{i}", 1) for i in range(S)]
+    empty = [Bar(f"empty{i}", 1 + 4 * NDQ) for i in range(S)]
+    afull = [Bar(f"afull{i}", 4) for i in range(NA)]
+    aempty = [Bar(f"aempty{i}", 1) for i in range(NA)]
+    accfull = [Bar(f"accfull{i}", 1) for i in range(ACCB)]
+    accempty = [Bar(f"accempty{i}", 4) for i in range(ACCB)]
+    bfull, bempty = Bar("bfull", 1), Bar("bempty", 1)
+    tiles = [(mt == 0, mt == m - 1, k) for m, k in units for mt in range(m)]
+
+    def producer():
+        seq = useq = 0
+        for first, _, k in tiles:
+            if first:
+                yield bempty, useq  # parity (useq & 1) ^ 1: the previous unit's release
+                bfull.arrive()
+                useq += 1
+            for _ in range(k):
+                s = seq % S
+                yield empty[s], seq // S
+                full[s].arrive()
+                seq += 1
+
+    def mma():
+        seq = tseq = useq = 0
+        for first, last, k in tiles:
+            ab = tseq % ACCB
+            yield accempty[ab], tseq // ACCB
+            if first:
+                yield bfull, useq + 1
+                useq += 1
+            for _ in range(k):
+                s = seq % S
+                yield full[s], seq // S + 1
+                for kb in range(KB):
+                    kbs = seq * KB + kb
+                    a, u = kbs % NA, kbs // NA
+                    yield afull[a], u + 1
+                    aempty[a].arrive()
+                empty[s].arrive()
+                seq += 1
+            accfull[ab].arrive()
+            if last:
+                bempty.arrive()
+            tseq += 1
+
+    def epilogue():
+        tseq = 0
+        for _ in tiles:
+            ab = tseq % ACCB
+            yield accfull[ab], tseq // ACCB + 1
+            accempty[ab].arrive()
+            tseq += 1
+
+    def dequant(g):
+        seq = 0
+        for _, _, k in tiles:
+            for _ in range(k):
+                s = seq % S
+                yield full[s], seq // S + 1
+                for kb in range(KB):
+                    kbs = seq * KB + kb
+                    if kbs % NDQ != g:
+                        continue
+                    a, u = kbs % NA, kbs // NA
+                    yield aempty[a], u
+                    afull[a].arrive()
+                empty[s].arrive()
+                seq += 1
+
+    rs = [producer(), mma()] + [epilogue() for _ in range(4)]
+    rs += [dequant(g) for g in range(NDQ) for _ in range(4)]
+    return rs
+
+
+def run_roles(rs, seed):
+    rng = random.Random(seed)
+    cur = [None] * len(rs)
+    alive = set(range(len(rs)))
+    while alive:
+        changed = True
+        while changed:
+            changed = False
+            for i in list(alive):
+                if cur[i] is None:
+                    try:
+                        cur[i] = next(rs[i])
+                    except StopIteration:
+                        alive.discard(i)
+                    changed = True
+        if not alive:
+            return None
+        ready = []
+        for i in alive:
+            bar, k = cur[i]
+            if bar.phase < k - 1 or bar.phase > k:
+                return f"parity alias on {bar.name}: needs completion {k}, at phase {bar.phase}"
+            if bar.phase >= k:
+                ready.append(i)
+        if not ready:
+            return "deadlock"
+        cur[rng.choice(ready)] = None
+    return None
+
+
+@pytest.mark.parametrize("wt", [Q8_0, Q4_K])
+def test_resident_tile_configs_are_safe(wt):
+    cfg = gemm_cfg_bres(wt)
+    assert cfg["stages"] >= 2 and cfg["na"] >= 2 and cfg["ring_ok"]
+    kst = 1024 // (256 if wt == Q4_K else 128)
+    # whole token tiles (16 m-tiles), chunked ones, a shared group of another K, single m-tiles
+    for units in ([(16, kst)] * 3, [(4, kst)] * 5, [(8, kst // 2), (8, kst), (8, kst)], [(1, kst)] * 4):
+        for seed in range(10):
+            assert run_roles(roles_bres(cfg, units), seed) is None, (cfg, units, seed)
+
+
+def test_resident_tile_model_catches_an_early_reload():
+    """The model is sharp: a producer that reloads the resident tile without waiting for the
+    previous unit's release is caught (it runs ahead of the MMA's bfull waits)."""
+    cfg = gemm_cfg_bres(Q4_K)
+
+    def no_wait_roles(units):
+        rs = roles_bres(cfg, units)
+        prod = rs[0]
+
+        def eager():
+            for bar, k in prod:
+                if bar.name == "bempty":
+                    continue  # skip the wait: the arrival on bfull follows at once
+                yield bar, k
+        rs[0] = eager()
+        return rs
+
+    results = [run_roles(no_wait_roles([(1, 1)] * 8), seed) for seed in range(30)]
+    assert any(r and "alias" in r for r in results)
+
+
+def gemm_cfg_bres_pair(wt, ndq):
+    """GemmCfg<WT, MODE_DOWN, 128, NDQ, PAIR = true, BRES = true>: each CTA keeps its 64 token rows
+    resident (128 KB); one 128-row block per CTA, so the stages hold one weight tile each."""
+    stage_k = 256 if wt == Q4_K else 128
+    w_bytes = 128 * 144 if wt == Q4_K else 128 * 128 + 128 * 16
+    stages = min(6, (227 * 1024 - 2048 - 1024 * 64 * 2) // w_bytes)
+    na = min(4, (512 - 2 * 128) // 64)
+    return dict(stages=stages, na=na, ndq=ndq, kb=stage_k // 128, acc_bufs=2, quant=True, ring_ok=na >= ndq)
+
+
+def roles_bres_pair(cfg, units):
+    """The pair's roles with resident tiles: each CTA's producer waits its own bempty and its
+    activation half counts on the leader's bfull; the leader's MMA waits bfull before a unit's
+    first m-tile (and no per-stage activation barrier), and its commit after the unit's last
+    m-tile arrives on both CTAs' bempty."""
+    S, NA, NDQ, KB, ACCB = cfg["stages"], cfg["na"], cfg["ndq"], cfg["kb"], cfg["acc_bufs"]
+    cta = []
+    for r in range(2):
+        cta.append(dict(
+            full=[Bar(f"full{i}.{r}", 1) for i in range(S)],
+            empty=[Bar(f"empty{i}.{r}", 1 + 4 * NDQ) for i in range(S)],
+            aempty=[Bar(f"aempty{i}.{r}", 1) for i in range(NA)],
+            accfull=[Bar(f"accfull{i}.{r}", 1) for i in range(ACCB)],
+            bempty=Bar(f"bempty.{r}", 1),
+        ))
+    bfull = Bar("bfull", 2)  # both halves' bytes (leader's barrier)
+    afull = [Bar(f"afull{i}", 8) for i in range(NA)]
+    accempty = [Bar(f"accempty{i}", 8) for i in range(ACCB)]
+    tiles = [(mt == 0, mt == m - 1, k) for m, k in units for mt in range(m)]
+
+    def producer(r):
+        seq = useq = 0
+        for first, _, k in tiles:
+            if first:
+                yield cta[r]["bempty"], useq
+                bfull.arrive()
+                useq += 1
+            for _ in range(k):
+                s = seq % S
+                yield cta[r]["empty"][s], seq // S
+                cta[r]["full"][s].arrive()
+                seq += 1
+
+    def mma():
+        seq = tseq = useq = 0
+        for first, last, k in tiles:
+            ab = tseq % ACCB
+            yield accempty[ab], tseq // ACCB
+            if first:
+                yield bfull, useq + 1
+                useq += 1
+            for _ in range(k):
+                s = seq % S
+                for kb in range(KB):
+                    kbs = seq * KB + kb
+                    a, u = kbs % NA, kbs // NA
+                    yield afull[a], u + 1
+                    for r in range(2):
+                        cta[r]["aempty"][a].arrive()
+                for r in range(2):
+                    cta[r]["empty"][s].arrive()
+                seq += 1
+            for r in range(2):
+                cta[r]["accfull"][ab].arrive()
+                if last:
+                    cta[r]["bempty"].arrive()
+            tseq += 1
+
+    def epilogue(r):
+        tseq = 0
+        for _ in tiles:
+            ab = tseq % ACCB
+            yield cta[r]["accfull"][ab], tseq // ACCB + 1
+            accempty[ab].arrive()
+            tseq += 1
+
+    def dequant(r, g):
+        seq = 0
+        for _, _, k in tiles:
+            for _ in range(k):
+                s = seq % S
+                yield cta[r]["full"][s], seq // S + 1
+                for kb in range(KB):
+                    kbs = seq * KB + kb
+                    if kbs % NDQ != g:
+                        continue
+                    a, u = kbs % NA, kbs // NA
+                    yield cta[r]["aempty"][a], u
+                    afull[a].arrive()
+                cta[r]["empty"][s].arrive()
+                seq += 1
+
+    rs = [mma()]
+    for r in range(2):
+        rs += [producer(r)] + [epilogue(r) for _ in range(4)]
+        rs += [dequant(r, g) for g in range(NDQ) for _ in range(4)]
+    return rs
+
+
+@pytest.mark.parametrize("wt,ndq", [(Q8_0, 2), (Q8_0, 4), (Q4_K, 2), (Q4_K, 4)])
+def test_resident_tile_pair_configs_are_safe(wt, ndq):
+    cfg = gemm_cfg_bres_pair(wt, ndq)
+    assert cfg["stages"] >= 2 and cfg["ring_ok"]
+    kst = 1024 // (256 if wt == Q4_K else 128)
+    for units in ([(16, kst)] * 2, [(4, kst)] * 4, [(8, kst // 2), (8, kst)], [(1, kst)] * 4, [(1, 1)] * 6):
+        for seed in range(8):
+            assert run_roles(roles_bres_pair(cfg, units), seed) is None, (cfg, units, seed)
