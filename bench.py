@@ -433,12 +433,32 @@ def main():
         ms4 = max_over_ranks(e0.elapsed_time(e1) / args.steps)
         layer.sync()
         st4 = layer.stats()
-        loads = torch.tensor([float(st4["ep_rows_received"])], device=dev)
-        allv = [torch.zeros_like(loads) for _ in range(world)]
-        dist.all_gather(allv, loads)
+
+        def rows_per_rank(st_):
+            loads = torch.tensor([float(st_["ep_rows_received"])], device=dev)
+            allv = [torch.zeros_like(loads) for _ in range(world)]
+            dist.all_gather(allv, loads)
+            return [int(v.item()) for v in allv]
+
         c4 = {"tokens": 16384, "ms_per_step": ms4, "tokens_per_s": 16384 / (ms4 / 1e3),
-              "rows_received_per_rank": [int(v.item()) for v in allv], "scaling": "strong",
+              "rows_received_per_rank": rows_per_rank(st4), "scaling": "strong",
               "bias": "0.5 log Zipf(1.1) over a random expert permutation"}
+        # the same workload with the busiest experts of the last forward replicated on every rank
+        # (dmoe_replicate_experts): their (token, slot) pairs stay on the token's rank
+        n_hot = 16
+        layer.replicate_experts(n_hot)
+        for _ in range(args.warmup):
+            layer.forward(x4, out=o4)
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            layer.forward(x4, out=o4)
+        e1.record(stream)
+        barrier()
+        ms4r = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        layer.sync()
+        c4["replicated"] = {"n_hot": n_hot, "ms_per_step": ms4r, "tokens_per_s": 16384 / (ms4r / 1e3),
+                            "rows_received_per_rank": rows_per_rank(layer.stats())}
 
     # ---- sampler step (dmoe_sample_step): one block of 32 masked positions over the flash-model
     # vocabulary; a secondary measurement, so a failure there is reported in its object instead

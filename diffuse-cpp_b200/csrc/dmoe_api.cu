@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <memory>
 #include <cstdarg>
 #include <cstdio>
@@ -142,6 +143,27 @@ dmoe_status upload_weight(DevWeight& w, int32_t type, const void* host, int64_t 
                   128, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// TMA descriptors of a weight family already in device memory (the layouts upload_weight makes).
+dmoe_status map_weight(DevWeight& w) {
+  const size_t rs = row_size(w.type, w.k);
+  if (w.type == DMOE_TYPE_Q8_0) {
+    dmoe_status st = make_map(&w.tm_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, (uint64_t)w.k, (uint64_t)w.rows,
+                              (uint64_t)w.k, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DMOE_OK) return st;
+    return make_map(&w.tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.s, (uint64_t)(w.k / 32), (uint64_t)w.rows,
+                    (uint64_t)(w.k / 32) * 4, 4, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (w.type == DMOE_TYPE_Q4_K)
+    return make_map(&w.tm_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.q, (uint64_t)rs, (uint64_t)w.rows, (uint64_t)rs, 144, 128,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  return make_map(&w.tm_q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w.q, (uint64_t)w.k, (uint64_t)w.rows, (uint64_t)w.k * 2,
+                  64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Bytes per row of the device layout: one plane (F16 / Q4_K GGUF rows, Q8_0 int8 quants) plus,
+// for Q8_0, the fp32 scale plane.
+size_t dev_row_bytes(const DevWeight& w) { return w.type == DMOE_TYPE_Q8_0 ? (size_t)w.k : row_size(w.type, w.k); }
+
 void free_weight(DevWeight& w) {
   if (w.q) cudaFree(w.q);
   if (w.s) cudaFree(w.s);
@@ -232,7 +254,21 @@ struct dmoe_layer {
   int32_t* ep_mr = nullptr; size_t ep_mr_cap = 0;    // slot lists received
   float* ep_part = nullptr; size_t ep_part_cap = 0;  // partial rows computed here for others, [R][H]
   float* ep_back = nullptr; size_t ep_back_cap = 0;  // partial rows returned to this rank, [S][H]
-  int32_t* ep_host = nullptr;                        // pinned: the 2W counts
+  int32_t* ep_host = nullptr;                        // pinned: the 2 W ep_chunks counts
+  // chunked exchange: ep_chunks pipeline chunks per forward (DMOE_EP_CHUNKS, 1..kMaxChunks, the
+  // same on every rank), NCCL groups on comm_stream, gemm_sm_reserve SMs left to NCCL's kernels
+  int ep_chunks = 1;
+  int gemm_sm_reserve = 0;
+  // hot-expert replicas (dmoe_replicate_experts): n_hot experts held by every rank after its own
+  // e_local (local expert e_local + j = global expert hot_ids[j]); hot_slot [E] maps a global
+  // expert to j or -1; ep_load [E] is the last forward's (token, slot) count per expert here
+  int n_hot = 0;
+  std::vector<int32_t> hot_ids;
+  int32_t* hot_slot = nullptr;
+  int32_t* ep_load = nullptr;
+  int32_t* ep_load_sum = nullptr;
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t ev_pack[kMaxChunks] = {}, ev_disp[kMaxChunks] = {}, ev_exp[kMaxChunks] = {}, ev_comb[kMaxChunks] = {};
   // statistics
   dmoe_stats stats{};
   int32_t* host_counters = nullptr;  // pinned: n_tiles, n_active
@@ -345,10 +381,13 @@ void fill_group(GemmGroup& g, const DevWeight& w, int32_t type, int64_t rows_per
 // (single GPU only): routed rows stored to ybuf, then summed per token in slot order.
 dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t rows, int nt, int32_t* n_tiles,
                         float* out_sh, float* out_rt, int64_t rt_rows, bool combine, bool out_sh_zeroed, bool prof,
-                        int& kernels) {
+                        int& kernels, int groups = 3) {
+  // groups: bit 0 the shared expert (rows [0, n_sh)), bit 1 the routed experts (the tile list)
+  const bool sh = L->has_shared && (groups & 1);
+  const bool rt = (groups & 2) != 0;
   const int64_t H = L->H, K = L->K;
   const int64_t Imax = std::max(L->I, L->Is);
-  const int64_t E_here = L->world > 1 ? L->e_local : L->E;
+  const int64_t E_here = L->world > 1 ? L->e_local + L->n_hot : L->E;  // owned experts, then replicas
   dmoe_status s;
   const bool pair_gu = use_pair(L, nt, MODE_GATEUP), pair_dn = use_pair(L, nt, MODE_DOWN);
   // activation tiles: NT token rows, or each pair CTA's half of them
@@ -361,23 +400,23 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
     return s;
   const int64_t pairs = rows - n_sh;
   const int64_t tt_est = std::min<int64_t>(E_here, pairs) + pairs / nt;
-  const int64_t sh_tt = L->has_shared ? (n_sh + nt - 1) / nt : 0;
-  const bool same_type = !L->has_shared || L->stype == L->etype;
+  const int64_t sh_tt = sh ? (n_sh + nt - 1) / nt : 0;
+  const bool same_type = !sh || L->stype == L->etype;
   const int gu_stage_r = gemm_stage_k(L->etype), gu_stage_s = gemm_stage_k(L->stype);
   const int64_t gu_tiles = tt_est * (L->I / kMTile) + sh_tt * (L->Is / kMTile);
   int ks_gu = pick_ksplit(gu_tiles, L->sms,
-                          {(int)(H / gu_stage_r), L->has_shared ? (int)(H / gu_stage_s) : (int)(H / gu_stage_r)});
+                          {(int)(H / gu_stage_r), sh ? (int)(H / gu_stage_s) : (int)(H / gu_stage_r)});
   if ((size_t)rows * 2 * Imax * 4 > (256ull << 20)) ks_gu = 1;
   const int64_t dn_tiles = (tt_est + sh_tt) * (H / kMTile);
   int ks_dn = pick_ksplit(dn_tiles, L->sms,
-                          {(int)(L->I / gu_stage_r), L->has_shared ? (int)(L->Is / gu_stage_s) : (int)(L->I / gu_stage_r)});
+                          {(int)(L->I / gu_stage_r), sh ? (int)(L->Is / gu_stage_s) : (int)(L->I / gu_stage_r)});
   {
     const int f_gu = env_int("DMOE_KSPLIT_GU", 0), f_dn = env_int("DMOE_KSPLIT_DN", 0);
     auto divides = [&](int ks, int64_t k_r, int64_t k_s) {
       return ks >= 1 && ks <= 8 && (ks & (ks - 1)) == 0 && k_r % ks == 0 && k_s % ks == 0;
     };
-    const int64_t gr = H / gu_stage_r, gs = L->has_shared ? H / gu_stage_s : gr;
-    const int64_t dr = L->I / gu_stage_r, ds = L->has_shared ? L->Is / gu_stage_s : dr;
+    const int64_t gr = H / gu_stage_r, gs = sh ? H / gu_stage_s : gr;
+    const int64_t dr = L->I / gu_stage_r, ds = sh ? L->Is / gu_stage_s : dr;
     if (divides(f_gu, gr, gs) && (size_t)rows * 2 * Imax * 4 <= (256ull << 20)) ks_gu = f_gu;
     if (divides(f_dn, dr, ds)) ks_dn = f_dn;
   }
@@ -403,7 +442,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   gp.n_experts = (int32_t)E_here;
   // routed tiles index L->tiles and tt_done[sh_tt + tile]
   gp.tiles_cap = (int32_t)std::min<int64_t>((int64_t)L->tiles_cap, (int64_t)L->tt_done_cap - sh_tt);
-  if (L->has_shared) {
+  if (sh) {
     gp.tm_w[0][0] = L->sgate.tm_q;
     gp.tm_w[0][1] = L->sup.tm_q;
     gp.tm_s[0][0] = L->sgate.tm_s;
@@ -415,7 +454,9 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   gp.tm_s[1][0] = L->gate.tm_s;
   gp.tm_s[1][1] = L->up.tm_s;
   fill_group(gp.grp[1], L->gate, L->etype, L->I, L->I, gemm_out_rows(MODE_GATEUP, nt, pair_gu));
-  const int grid = L->sms;
+  gp.grp[1].present = rt ? 1 : 0;
+  // persistent grid; with the chunked expert-parallel exchange a few SMs stay free for NCCL
+  const int grid = L->sms - L->gemm_sm_reserve;
   // dequant warpgroups per CTA: the largest of 4 / 3 / 2 the TMEM ring allows (measured 2-3 %
   // faster than 2 at 1-8 blocks)
   const int ndq = env_int("DMOE_NDQ", 4);
@@ -461,7 +502,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   if (combine) {
     if ((s = grow(L->ybuf, L->ybuf_cap, (size_t)pairs * H)) != DMOE_OK) return s;
   }
-  if ((!combine || !L->has_shared) && !out_sh_zeroed) DMOE_CUDA(cudaMemsetAsync(out_sh, 0, (size_t)n_sh * H * 4, st));
+  if ((!combine || !sh) && !out_sh_zeroed) DMOE_CUDA(cudaMemsetAsync(out_sh, 0, (size_t)n_sh * H * 4, st));
   if (out_rt != out_sh && rt_rows > 0) DMOE_CUDA(cudaMemsetAsync(out_rt, 0, (size_t)rt_rows * H * 4, st));
   GemmParams dp = gp;
   dp.tm_b = tm_h;
@@ -475,7 +516,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   dp.pair_tok = L->pair_tok;
   dp.pair_w = L->pair_w;
   std::memset(&dp.grp, 0, sizeof(dp.grp));
-  if (L->has_shared) {
+  if (sh) {
     dp.tm_w[0][0] = L->sdown.tm_q;
     dp.tm_s[0][0] = L->sdown.tm_s;
     fill_group(dp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair_dn));
@@ -483,6 +524,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   dp.tm_w[1][0] = L->down.tm_q;
   dp.tm_s[1][0] = L->down.tm_s;
   fill_group(dp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, nt, pair_dn));
+  dp.grp[1].present = rt ? 1 : 0;
   // Down GEMM with resident activation tiles (BRES, off by default): each CTA holds 64 token rows
   // of h (all of K <= 1024, 128 KB) in shared memory and runs every 256-row m-tile of the down
   // matrix against them, instead of re-reading the activation tile from L2 for each m-tile.
@@ -496,7 +538,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   const bool quant_dn = L->etype != DMOE_TYPE_F16;
   const int bres_env = env_int("DMOE_BRES", 0);
   const bool bres_ok = !fused && same_type && quant_dn && ks_dn == 1 &&
-                       std::max(L->I, L->has_shared ? L->Is : 0) <= kBresK;
+                       std::max(L->I, sh ? L->Is : 0) <= kBresK;
   const bool bres_pair = bres_ok && bres_env >= 1 && nt == 2 * kBresNT && use_pair(L, nt, MODE_GATEUP);
   const bool bres = bres_pair || (bres_ok && bres_env >= 2 && (nt == kBresNT || nt == 2 * kBresNT));
   if (bres) {
@@ -508,9 +550,10 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
     bp.tm_b = tm_h64;
     const int bnt = bres_pair ? 2 * kBresNT : kBresNT;  // token rows per tile of the launch
     bp.tile_div = nt / bnt;
-    bp.n_shared_tt = L->has_shared ? (int32_t)((n_sh + bnt - 1) / bnt) : 0;
+    bp.n_shared_tt = sh ? (int32_t)((n_sh + bnt - 1) / bnt) : 0;
     fill_group(bp.grp[1], L->down, L->etype, L->H, L->H, gemm_out_rows(MODE_DOWN, bnt, bres_pair));
-    if (L->has_shared) fill_group(bp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, bnt, bres_pair));
+    bp.grp[1].present = rt ? 1 : 0;
+    if (sh) fill_group(bp.grp[0], L->sdown, L->stype, L->H, L->H, gemm_out_rows(MODE_DOWN, bnt, bres_pair));
     // m-chunks per token tile: whole token tiles while they give every SM (pair) about three units
     const int n_mt = bp.grp[1].n_mt;
     const int64_t units = bp.n_shared_tt + tt_est * bp.tile_div;
@@ -552,7 +595,7 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
     kernels += 2;
   }
   if (combine) {
-    DMOE_CUDA(launch_combine(L->ybuf, H, n_sh, L->pair_row, (int)K, out_sh, H, L->has_shared ? 1 : 0, st));
+    DMOE_CUDA(launch_combine(L->ybuf, H, n_sh, L->pair_row, (int)K, out_sh, H, sh ? 1 : 0, st));
     ++kernels;
   }
   L->stats.token_tile = nt;
@@ -662,100 +705,177 @@ dmoe_status ep_wait(dmoe_layer* L, cudaStream_t st, const char* what) {
     if (s_ != DMOE_OK) return s_;                                           \
   } while (0)
 
+// Expert-parallel experts of one forward, pipelined over `ep_chunks` chunks of this rank's
+// tokens (src/diffuse-moe-graph.cpp:264-286 across ranks). Routing is already done for every
+// token, so chunk boundaries need not be routing blocks.
+//   1. per chunk: plan (per-token destination mask, row positions, counts per destination);
+//   2. one count exchange for all chunks (grouped send / recv of `chunks` ints per peer), read
+//      on the host: the forward's only host synchronisation (it sizes the transfers);
+//   3. per chunk c, ordered by events:
+//        compute stream  pack(c) ............ gather + GEMMs(c) ............... final(c) (at the end)
+//        comm stream              dispatch(c) ..................... combine(c)
+//      dispatch(c + 1) and combine(c - 1) run on the comm stream while the GEMMs of chunk c run
+//      on the compute stream; the GEMM grid leaves gemm_sm_reserve SMs to NCCL's kernels.
+// Every rank takes the same NCCL steps in the same order: all dispatch groups, then the combine
+// groups in chunk order.
 dmoe_status ep_experts(dmoe_layer* L, cudaStream_t st, const float* xd, int64_t n, const int32_t* idx,
                        const float* w, float* od, uint32_t flags, int& kernels) {
   const NcclApi& api = nccl();
   const int W = L->world;
+  const int C = L->ep_chunks;
   const int64_t H = L->H, K = L->K, El = L->e_local;
+  const int64_t Eh = El + L->n_hot;  // local experts: owned, then replicas
+  const int32_t* hot = L->n_hot ? L->hot_slot : nullptr;
   const int64_t Imax = std::max(L->I, L->Is);
   const bool prof = flags & DMOE_F_PROFILE;
   if (flags & DMOE_F_DETERMINISTIC)
     return fail(DMOE_ERR_UNSUPPORTED, "DMOE_F_DETERMINISTIC is single-GPU only");
   dmoe_status s;
-  if ((s = grow(L->ep_mask, L->ep_mask_cap, (size_t)n)) != DMOE_OK) return s;
-  if ((s = grow(L->ep_pos, L->ep_pos_cap, (size_t)W * n)) != DMOE_OK) return s;
-  if ((s = grow(L->ep_cnt, L->ep_cnt_cap, (size_t)2 * W)) != DMOE_OK) return s;
-  int32_t* cnt_send = L->ep_cnt;
-  int32_t* cnt_recv = L->ep_cnt + W;
-  // ---- plan and count exchange
-  DMOE_CUDA(launch_ep_plan(idx, n, (int)K, (int)El, W, L->ep_mask, L->ep_pos, cnt_send, st));
-  kernels += 2;
+  cudaStream_t cs = L->comm_stream;
+  // chunk c covers tokens [t0[c], t0[c] + nc[c]); near-equal, possibly empty
+  int64_t t0[dmoe_layer::kMaxChunks], nc[dmoe_layer::kMaxChunks];
+  for (int c = 0; c < C; ++c) {
+    t0[c] = n * c / C;
+    nc[c] = n * (c + 1) / C - t0[c];
+  }
+  if ((s = grow(L->ep_mask, L->ep_mask_cap, (size_t)std::max<int64_t>(n, 1))) != DMOE_OK) return s;
+  if ((s = grow(L->ep_pos, L->ep_pos_cap, (size_t)std::max<int64_t>(W * n, 1))) != DMOE_OK) return s;
+  if ((s = grow(L->ep_cnt, L->ep_cnt_cap, (size_t)2 * W * C)) != DMOE_OK) return s;
+  int32_t* cnt_send = L->ep_cnt;          // [W][C]: rows for destination p from chunk c at p * C + c
+  int32_t* cnt_recv = L->ep_cnt + W * C;  // [W][C]: rows source p sends from its chunk c
+  // ---- 1. plans; chunk c's positions are pos + W * t0[c], laid out [W][nc[c]]
+  for (int c = 0; c < C; ++c) {
+    DMOE_CUDA(launch_ep_plan(idx + t0[c] * K, nc[c], (int)K, (int)El, hot, L->rank, W, L->ep_mask + t0[c],
+                             L->ep_pos + W * t0[c], cnt_send + c, C, st));
+    kernels += nc[c] > 0 ? 2 : 1;
+  }
+  // ---- 2. count exchange, one host read
   DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
   for (int p = 0; p < W; ++p) {
-    DMOE_NCCL(api.Send(cnt_send + p, 1, ncclInt32, p, L->comm, st), "ncclSend(counts)");
-    DMOE_NCCL(api.Recv(cnt_recv + p, 1, ncclInt32, p, L->comm, st), "ncclRecv(counts)");
+    DMOE_NCCL(api.Send(cnt_send + p * C, (size_t)C, ncclInt32, p, L->comm, st), "ncclSend(counts)");
+    DMOE_NCCL(api.Recv(cnt_recv + p * C, (size_t)C, ncclInt32, p, L->comm, st), "ncclRecv(counts)");
   }
   DMOE_NCCL(api.GroupEnd(), "count exchange");
-  DMOE_CUDA(cudaMemcpyAsync(L->ep_host, L->ep_cnt, sizeof(int32_t) * 2 * W, cudaMemcpyDeviceToHost, st));
+  DMOE_CUDA(cudaMemcpyAsync(L->ep_host, L->ep_cnt, sizeof(int32_t) * 2 * W * C, cudaMemcpyDeviceToHost, st));
   if ((s = ep_wait(L, st, "count exchange")) != DMOE_OK) return s;
-  RankOffsets soff{}, roff{};
-  int64_t S = 0, R = 0;
-  for (int p = 0; p < W; ++p) {
-    soff.v[p] = (int32_t)S;
-    roff.v[p] = (int32_t)R;
-    S += L->ep_host[p];
-    R += L->ep_host[W + p];
+  // send / receive layouts: chunk-major, then peer
+  RankOffsets soff[dmoe_layer::kMaxChunks], roff[dmoe_layer::kMaxChunks];
+  int64_t Rc[dmoe_layer::kMaxChunks];
+  int64_t S = 0, R = 0, Rmax = 0;
+  for (int c = 0; c < C; ++c) {
+    const int64_t r0 = R;
+    for (int p = 0; p < W; ++p) {
+      soff[c].v[p] = (int32_t)S;
+      roff[c].v[p] = (int32_t)R;
+      S += L->ep_host[p * C + c];
+      R += L->ep_host[W * C + p * C + c];
+    }
+    Rc[c] = R - r0;
+    Rmax = std::max(Rmax, Rc[c]);
   }
-  const int64_t P = R * K;       // upper bound of the local (row, expert) pairs
-  const int64_t rows = n + P;    // gathered layout: shared rows [0, n), then pairs
+  const int64_t nmax = (n + C - 1) / C + 1;
+  const int64_t Pmax = Rmax * K;         // upper bound of a chunk's local (row, expert) pairs
+  const int64_t rows_max = nmax + Pmax;  // gathered layout of a chunk: shared rows, then pairs
   if ((s = grow(L->ep_xs, L->ep_xs_cap, (size_t)std::max<int64_t>(S, 1) * H)) != DMOE_OK) return s;
   if ((s = grow(L->ep_ms, L->ep_ms_cap, (size_t)std::max<int64_t>(S, 1) * 2 * K)) != DMOE_OK) return s;
   if ((s = grow(L->ep_xr, L->ep_xr_cap, (size_t)std::max<int64_t>(R, 1) * H)) != DMOE_OK) return s;
   if ((s = grow(L->ep_mr, L->ep_mr_cap, (size_t)std::max<int64_t>(R, 1) * 2 * K)) != DMOE_OK) return s;
   if ((s = grow(L->ep_part, L->ep_part_cap, (size_t)std::max<int64_t>(R, 1) * H)) != DMOE_OK) return s;
   if ((s = grow(L->ep_back, L->ep_back_cap, (size_t)std::max<int64_t>(S, 1) * H)) != DMOE_OK) return s;
-  // ---- dispatch: one fp16 row + slot list per (token, destination)
-  DMOE_CUDA(launch_ep_pack(xd, n, (int)H, (int)K, idx, w, (int)El, L->ep_mask, L->ep_pos, soff,
-                           L->etype == DMOE_TYPE_Q4_K, L->ep_xs, L->ep_ms, st));
-  ++kernels;
-  DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
-  for (int p = 0; p < W; ++p) {
-    const int64_t cs = L->ep_host[p], cr = L->ep_host[W + p];
-    if (cs) {
-      DMOE_NCCL(api.Send(L->ep_xs + (int64_t)soff.v[p] * H, (size_t)(cs * H), ncclFloat16, p, L->comm, st), "ncclSend(rows)");
-      DMOE_NCCL(api.Send(L->ep_ms + (int64_t)soff.v[p] * 2 * K, (size_t)(cs * 2 * K), ncclInt32, p, L->comm, st), "ncclSend(slots)");
-    }
-    if (cr) {
-      DMOE_NCCL(api.Recv(L->ep_xr + (int64_t)roff.v[p] * H, (size_t)(cr * H), ncclFloat16, p, L->comm, st), "ncclRecv(rows)");
-      DMOE_NCCL(api.Recv(L->ep_mr + (int64_t)roff.v[p] * 2 * K, (size_t)(cr * 2 * K), ncclInt32, p, L->comm, st), "ncclRecv(slots)");
-    }
+  if ((s = grow(L->tiles, L->tiles_cap, (size_t)(Pmax / 32 + Eh + 2))) != DMOE_OK) return s;
+  if ((s = grow(L->xg, L->xg_cap, (size_t)rows_max * H)) != DMOE_OK) return s;
+  if ((s = grow(L->hbuf, L->hbuf_cap, (size_t)rows_max * Imax)) != DMOE_OK) return s;
+  if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows_max)) != DMOE_OK) return s;
+  if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows_max)) != DMOE_OK) return s;
+  if ((s = grow(L->tt_done, L->tt_done_cap, (size_t)(Pmax / 32 + Eh + 2 + (nmax + 31) / 32))) != DMOE_OK) return s;
+  // ---- 3a. pack every chunk, each chunk's dispatch on the comm stream once its rows are packed
+  for (int c = 0; c < C; ++c) {
+    DMOE_CUDA(launch_ep_pack(xd + t0[c] * H, nc[c], (int)H, (int)K, idx + t0[c] * K, w + t0[c] * K, (int)El, hot,
+                             L->rank, L->ep_mask + t0[c], L->ep_pos + W * t0[c], soff[c], L->etype == DMOE_TYPE_Q4_K,
+                             L->ep_xs, L->ep_ms, st));
+    kernels += nc[c] > 0 ? 1 : 0;
+    DMOE_CUDA(cudaEventRecord(L->ev_pack[c], st));
   }
-  DMOE_NCCL(api.GroupEnd(), "dispatch exchange");
-  // ---- local experts over the received rows
-  const int nt = pick_nt(L, n);
+  for (int c = 0; c < C; ++c) {
+    DMOE_CUDA(cudaStreamWaitEvent(cs, L->ev_pack[c], 0));
+    DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
+    for (int p = 0; p < W; ++p) {
+      const int64_t ns = L->ep_host[p * C + c], nr = L->ep_host[W * C + p * C + c];
+      if (ns) {
+        DMOE_NCCL(api.Send(L->ep_xs + (int64_t)soff[c].v[p] * H, (size_t)(ns * H), ncclFloat16, p, L->comm, cs),
+                  "ncclSend(rows)");
+        DMOE_NCCL(api.Send(L->ep_ms + (int64_t)soff[c].v[p] * 2 * K, (size_t)(ns * 2 * K), ncclInt32, p, L->comm, cs),
+                  "ncclSend(slots)");
+      }
+      if (nr) {
+        DMOE_NCCL(api.Recv(L->ep_xr + (int64_t)roff[c].v[p] * H, (size_t)(nr * H), ncclFloat16, p, L->comm, cs),
+                  "ncclRecv(rows)");
+        DMOE_NCCL(api.Recv(L->ep_mr + (int64_t)roff[c].v[p] * 2 * K, (size_t)(nr * 2 * K), ncclInt32, p, L->comm, cs),
+                  "ncclRecv(slots)");
+      }
+    }
+    DMOE_NCCL(api.GroupEnd(), "dispatch exchange");
+    DMOE_CUDA(cudaEventRecord(L->ev_disp[c], cs));
+  }
+  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
+  // ---- 3b. the shared expert over all of this rank's tokens: it needs no exchange, so it runs
+  // while the dispatches are in flight (rows [0, n) of the gathered layout, straight into od)
+  int32_t* n_tiles = L->ints + 3 * L->E;
+  if (L->has_shared && n > 0) {
+    const int nt_sh = pick_nt(L, n);
+    DMOE_CUDA(launch_gather_shared(xd, n, (int)H, L->stype == DMOE_TYPE_Q4_K, L->xg, st));
+    DMOE_CUDA(cudaMemsetAsync(L->tt_done, 0, sizeof(int32_t) * (size_t)((n + nt_sh - 1) / nt_sh), st));
+    ++kernels;
+    if ((s = run_experts(L, st, n, n, nt_sh, n_tiles, od, od, 0, false, false, false, kernels, /*groups=*/1)) !=
+        DMOE_OK)
+      return s;
+  } else if (n > 0) {
+    DMOE_CUDA(cudaMemsetAsync(od, 0, sizeof(float) * (size_t)(n * H), st));
+  }
+  // ---- 3c. per chunk: the routed experts over the received rows (pairs from row 0 of the
+  // gathered layout), then the chunk's combine on the comm stream
+  const int nt = pick_nt(L, std::max<int64_t>(1, n / C));
   int32_t* counts = L->ints;  // [e_local] (the router's global counts are not needed any more)
   int32_t* fill = L->ints + L->E;
   int32_t* off = L->ints + 2 * L->E;
-  int32_t* n_tiles = L->ints + 3 * L->E;
   int32_t* n_active = n_tiles + 1;
-  if ((s = grow(L->tiles, L->tiles_cap, (size_t)(P / 32 + El + 2))) != DMOE_OK) return s;
-  if ((s = grow(L->xg, L->xg_cap, (size_t)rows * H)) != DMOE_OK) return s;
-  if ((s = grow(L->hbuf, L->hbuf_cap, (size_t)rows * Imax)) != DMOE_OK) return s;
-  if ((s = grow(L->pair_tok, L->pair_tok_cap, (size_t)rows)) != DMOE_OK) return s;
-  if ((s = grow(L->pair_w, L->pair_w_cap, (size_t)rows)) != DMOE_OK) return s;
-  DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)El, st));
-  DMOE_CUDA(launch_ep_count(L->ep_mr, R, (int)K, counts, st));
-  if ((s = grow(L->tt_done, L->tt_done_cap, (size_t)(P / 32 + El + 2 + (n + 31) / 32))) != DMOE_OK) return s;
-  DMOE_CUDA(launch_scan_tiles(counts, (int)El, n, nt, off, fill, L->tiles, n_tiles, n_active, L->tt_done,
-                              L->has_shared ? (int)((n + nt - 1) / nt) : 0, st));
-  if (L->has_shared) {
-    DMOE_CUDA(launch_gather_shared(xd, n, (int)H, L->stype == DMOE_TYPE_Q4_K, L->xg, st));
-    ++kernels;
+  for (int c = 0; c < C; ++c) {
+    const int64_t rbase = roff[c].v[0];
+    DMOE_CUDA(cudaStreamWaitEvent(st, L->ev_disp[c], 0));
+    if (Rc[c] > 0) {
+      const int64_t rows = Rc[c] * K;
+      DMOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * (size_t)Eh, st));
+      DMOE_CUDA(launch_ep_count(L->ep_mr + rbase * 2 * K, Rc[c], (int)K, counts, st));
+      DMOE_CUDA(launch_scan_tiles(counts, (int)Eh, 0, nt, off, fill, L->tiles, n_tiles, n_active, L->tt_done, 0, st));
+      DMOE_CUDA(launch_gather_rows(L->ep_xr + rbase * H, Rc[c], (int)H, (int)K, L->ep_mr + rbase * 2 * K, off, fill,
+                                   L->xg, L->pair_tok, L->pair_w, st));
+      kernels += 4;
+      if ((s = run_experts(L, st, 0, rows, nt, n_tiles, od, L->ep_part + rbase * H, Rc[c], false, true,
+                           prof && c == C - 1, kernels, /*groups=*/2)) != DMOE_OK)
+        return s;
+    }
+    DMOE_CUDA(cudaEventRecord(L->ev_exp[c], st));
+    DMOE_CUDA(cudaStreamWaitEvent(cs, L->ev_exp[c], 0));
+    DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
+    for (int p = 0; p < W; ++p) {
+      const int64_t ns = L->ep_host[p * C + c], nr = L->ep_host[W * C + p * C + c];
+      if (nr)
+        DMOE_NCCL(api.Send(L->ep_part + (int64_t)roff[c].v[p] * H, (size_t)(nr * H), ncclFloat32, p, L->comm, cs),
+                  "ncclSend(partials)");
+      if (ns)
+        DMOE_NCCL(api.Recv(L->ep_back + (int64_t)soff[c].v[p] * H, (size_t)(ns * H), ncclFloat32, p, L->comm, cs),
+                  "ncclRecv(partials)");
+    }
+    DMOE_NCCL(api.GroupEnd(), "combine exchange");
+    DMOE_CUDA(cudaEventRecord(L->ev_comb[c], cs));
   }
-  DMOE_CUDA(launch_gather_rows(L->ep_xr, R, (int)H, (int)K, L->ep_mr, off, fill, L->xg, L->pair_tok, L->pair_w, st));
-  kernels += 3;
-  if (prof) DMOE_CUDA(cudaEventRecord(L->ev[2], st));
-  if ((s = run_experts(L, st, n, rows, nt, n_tiles, od, L->ep_part, R, false, false, prof, kernels)) != DMOE_OK) return s;
-  // ---- combine: partial rows back to their owners, then the owner's sum
-  DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
-  for (int p = 0; p < W; ++p) {
-    const int64_t cs = L->ep_host[p], cr = L->ep_host[W + p];
-    if (cr) DMOE_NCCL(api.Send(L->ep_part + (int64_t)roff.v[p] * H, (size_t)(cr * H), ncclFloat32, p, L->comm, st), "ncclSend(partials)");
-    if (cs) DMOE_NCCL(api.Recv(L->ep_back + (int64_t)soff.v[p] * H, (size_t)(cs * H), ncclFloat32, p, L->comm, st), "ncclRecv(partials)");
+  // ---- 3c. each chunk's owner sum, once its partials are back
+  for (int c = 0; c < C; ++c) {
+    DMOE_CUDA(cudaStreamWaitEvent(st, L->ev_comb[c], 0));
+    DMOE_CUDA(launch_ep_final(od + t0[c] * H, L->ep_back, nc[c], (int)H, L->ep_mask + t0[c], L->ep_pos + W * t0[c],
+                              soff[c], st));
+    kernels += nc[c] > 0 ? 1 : 0;
   }
-  DMOE_NCCL(api.GroupEnd(), "combine exchange");
-  DMOE_CUDA(launch_ep_final(od, L->ep_back, n, (int)H, L->ep_mask, L->ep_pos, soff, st));
-  ++kernels;
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[4], st));
   DMOE_CUDA(cudaMemcpyAsync(L->host_counters, n_tiles, 8, cudaMemcpyDeviceToHost, st));
   L->stats.ep_rows_sent = S;
@@ -970,8 +1090,28 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
   if (cudaMallocHost(&L->host_counters, 64) != cudaSuccess) return bail(fail(DMOE_ERR_OOM, "pinned alloc"));
   std::memset(L->host_counters, 0, 64);
   if (world > 1) {
-    if (cudaMallocHost(&L->ep_host, sizeof(int32_t) * 2 * kMaxRanks) != cudaSuccess)
+    if (cudaMallocHost(&L->ep_host, sizeof(int32_t) * 2 * kMaxRanks * dmoe_layer::kMaxChunks) != cudaSuccess)
       return bail(fail(DMOE_ERR_OOM, "pinned alloc"));
+    // pipeline chunks of the exchange (every rank must use the same count) and the SMs the GEMMs
+    // leave to NCCL's kernels so that the exchange of one chunk runs beside the GEMMs of another
+    L->ep_chunks = std::min(dmoe_layer::kMaxChunks, std::max(1, env_int("DMOE_EP_CHUNKS", 2)));
+    L->gemm_sm_reserve = std::min(L->sms / 4, std::max(0, env_int("DMOE_EP_SM_RESERVE", 8)));
+    if (cudaStreamCreateWithFlags(&L->comm_stream, cudaStreamNonBlocking) != cudaSuccess)
+      return bail(fail(DMOE_ERR_CUDA, "stream create"));
+    // per-expert loads of the last forward, their sum over ranks, replica slots (none yet)
+    if (cudaMalloc(&L->ep_load, sizeof(int32_t) * (size_t)L->E) != cudaSuccess ||
+        cudaMalloc(&L->ep_load_sum, sizeof(int32_t) * (size_t)L->E) != cudaSuccess ||
+        cudaMalloc(&L->hot_slot, sizeof(int32_t) * (size_t)L->E) != cudaSuccess)
+      return bail(fail(DMOE_ERR_OOM, "cudaMalloc expert loads"));
+    if (cudaMemset(L->ep_load, 0, sizeof(int32_t) * (size_t)L->E) != cudaSuccess ||
+        cudaMemset(L->hot_slot, 0xff, sizeof(int32_t) * (size_t)L->E) != cudaSuccess)
+      return bail(fail(DMOE_ERR_CUDA, "cudaMemset expert loads"));
+    for (int c = 0; c < dmoe_layer::kMaxChunks; ++c)
+      if (cudaEventCreateWithFlags(&L->ev_pack[c], cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&L->ev_disp[c], cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&L->ev_exp[c], cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&L->ev_comb[c], cudaEventDisableTiming) != cudaSuccess)
+        return bail(fail(DMOE_ERR_CUDA, "event create"));
     // non-blocking communicator: init and every group are polled against the layer's deadline
     ncclUniqueId id;
     std::memcpy(&id, dist->nccl_id, sizeof(id));
@@ -1032,7 +1172,8 @@ void dmoe_destroy(dmoe_layer* L) {
   cudaFree(L->odev);
   cudaFree(L->err);
   for (void* p : {(void*)L->ep_mask, (void*)L->ep_pos, (void*)L->ep_cnt, (void*)L->ep_xs, (void*)L->ep_ms,
-                  (void*)L->ep_xr, (void*)L->ep_mr, (void*)L->ep_part, (void*)L->ep_back})
+                  (void*)L->ep_xr, (void*)L->ep_mr, (void*)L->ep_part, (void*)L->ep_back, (void*)L->ep_load,
+                  (void*)L->ep_load_sum, (void*)L->hot_slot})
     cudaFree(p);
   if (L->ep_host) cudaFreeHost(L->ep_host);
   if (L->host_counters) cudaFreeHost(L->host_counters);
@@ -1049,6 +1190,13 @@ void dmoe_destroy(dmoe_layer* L) {
     if (L->ev_done[c]) cudaEventDestroy(L->ev_done[c]);
   }
   if (L->ev_start) cudaEventDestroy(L->ev_start);
+  if (L->comm_stream) {
+    cudaStreamSynchronize(L->comm_stream);  // the communicator is aborted: its kernels have ended
+    cudaStreamDestroy(L->comm_stream);
+  }
+  for (int c = 0; c < dmoe_layer::kMaxChunks; ++c)
+    for (cudaEvent_t e : {L->ev_pack[c], L->ev_disp[c], L->ev_exp[c], L->ev_comb[c]})
+      if (e) cudaEventDestroy(e);
   delete L;
 }
 
@@ -1143,6 +1291,9 @@ dmoe_status dmoe_forward(dmoe_layer* L, const float* x, int64_t n, float* out, c
   ra.counts = counts;
   DMOE_CUDA(launch_route(ra, st));
   ++kernels;
+  // expert parallelism: keep this forward's per-expert pair counts for dmoe_replicate_experts
+  if (L->world > 1 && !route_only)
+    DMOE_CUDA(cudaMemcpyAsync(L->ep_load, counts, sizeof(int32_t) * (size_t)E, cudaMemcpyDeviceToDevice, st));
   if (prof) DMOE_CUDA(cudaEventRecord(L->ev[1], st));
   nvtx_router.reset();
 
@@ -1208,6 +1359,110 @@ dmoe_status dmoe_sync(dmoe_layer* L) {
     return fail(DMOE_ERR_CUDA, "a device-built token tile (or tile count) was out of bounds and skipped (error bits 0x%x)",
                 e);
   }
+  return DMOE_OK;
+}
+
+dmoe_status dmoe_replicate_experts(dmoe_layer* L, const int32_t* ids, int32_t n_hot) {
+  if (!L) return fail(DMOE_ERR_INVALID_ARG, "null layer");
+  if (n_hot < 0 || n_hot > DMOE_MAX_HOT)
+    return fail(DMOE_ERR_INVALID_ARG, "n_hot %d outside [0, %d]", n_hot, DMOE_MAX_HOT);
+  if (L->world == 1) return DMOE_OK;  // one GPU holds every expert already
+  if (L->broken) return fail(DMOE_ERR_NCCL, "a collective of this layer failed earlier; re-create it on every rank");
+  const int64_t E = L->E, El = L->e_local;
+  if (n_hot > E - El)
+    return fail(DMOE_ERR_INVALID_ARG, "n_hot %d > n_expert - experts per rank (%lld)", n_hot, (long long)(E - El));
+  DMOE_CUDA(cudaSetDevice(L->device));
+  const NcclApi& api = nccl();
+  cudaStream_t st = L->own_stream;
+  dmoe_status s = ep_wait(L, L->last_stream, "earlier forwards");  // weights and loads settle first
+  if (s != DMOE_OK) return s;
+  std::vector<int32_t> chosen;
+  if (n_hot > 0 && ids) {
+    std::vector<char> seen((size_t)E, 0);
+    for (int j = 0; j < n_hot; ++j) {
+      if (ids[j] < 0 || ids[j] >= E || seen[(size_t)ids[j]])
+        return fail(DMOE_ERR_INVALID_ARG, "hot expert ids must be distinct and in [0, %lld)", (long long)E);
+      seen[(size_t)ids[j]] = 1;
+    }
+    chosen.assign(ids, ids + n_hot);
+  } else if (n_hot > 0) {
+    // the busiest experts of the last forward over all ranks, ties to the lower id (every rank
+    // computes the same choice from the same sums)
+    DMOE_NCCL(api.AllReduce(L->ep_load, L->ep_load_sum, (size_t)E, ncclInt32, ncclSum, L->comm, st),
+              "ncclAllReduce(expert loads)");
+    if ((s = ep_wait(L, st, "expert load sum")) != DMOE_OK) return s;
+    std::vector<int32_t> load((size_t)E), order((size_t)E);
+    DMOE_CUDA(cudaMemcpy(load.data(), L->ep_load_sum, sizeof(int32_t) * (size_t)E, cudaMemcpyDeviceToHost));
+    for (int64_t e = 0; e < E; ++e) order[(size_t)e] = (int32_t)e;
+    std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return load[(size_t)a] > load[(size_t)b]; });
+    chosen.assign(order.begin(), order.begin() + n_hot);
+  }
+  // new weight families: this rank's experts, then the replicas (broadcast from their owners)
+  DevWeight* fam[3] = {&L->gate, &L->up, &L->down};
+  const int64_t rpe[3] = {L->I, L->I, L->H};  // rows per expert
+  DevWeight nw[3];
+  auto drop_new = [&]() {
+    for (DevWeight& w : nw) free_weight(w);
+  };
+  for (int f = 0; f < 3; ++f) {
+    const DevWeight& o = *fam[f];
+    nw[f].type = o.type;
+    nw[f].k = o.k;
+    nw[f].rows = (El + n_hot) * rpe[f];
+    const size_t rb = dev_row_bytes(o), own = (size_t)(El * rpe[f]);
+    if (cudaMalloc(&nw[f].q, (size_t)nw[f].rows * rb) != cudaSuccess) {
+      drop_new();
+      return fail(DMOE_ERR_OOM, "cudaMalloc replica weights");
+    }
+    DMOE_CUDA(cudaMemcpyAsync(nw[f].q, o.q, own * rb, cudaMemcpyDeviceToDevice, st));
+    if (o.type == DMOE_TYPE_Q8_0) {
+      if (cudaMalloc(&nw[f].s, (size_t)nw[f].rows * (o.k / 32) * 4) != cudaSuccess) {
+        drop_new();
+        return fail(DMOE_ERR_OOM, "cudaMalloc replica scales");
+      }
+      DMOE_CUDA(cudaMemcpyAsync(nw[f].s, o.s, own * (o.k / 32) * 4, cudaMemcpyDeviceToDevice, st));
+    }
+  }
+  if (n_hot > 0) {
+    DMOE_NCCL(api.GroupStart(), "ncclGroupStart");
+    for (int j = 0; j < n_hot; ++j) {
+      const int owner = (int)(chosen[(size_t)j] / El);
+      const int64_t local = chosen[(size_t)j] - owner * El;
+      for (int f = 0; f < 3; ++f) {
+        const DevWeight& o = *fam[f];
+        const size_t rb = dev_row_bytes(o), nbytes = (size_t)rpe[f] * rb;
+        uint8_t* dst = static_cast<uint8_t*>(nw[f].q) + (size_t)(El + j) * nbytes;
+        const uint8_t* src = L->rank == owner ? static_cast<const uint8_t*>(o.q) + (size_t)local * nbytes : dst;
+        DMOE_NCCL(api.Broadcast(src, dst, nbytes, ncclUint8, owner, L->comm, st), "ncclBroadcast(expert weights)");
+        if (o.type == DMOE_TYPE_Q8_0) {
+          const size_t ns = (size_t)rpe[f] * (o.k / 32);
+          float* sd = nw[f].s + (size_t)(El + j) * ns;
+          const float* ss = L->rank == owner ? o.s + (size_t)local * ns : sd;
+          DMOE_NCCL(api.Broadcast(ss, sd, ns, ncclFloat32, owner, L->comm, st), "ncclBroadcast(expert scales)");
+        }
+      }
+    }
+    DMOE_NCCL(api.GroupEnd(), "replica broadcast");
+  }
+  if ((s = ep_wait(L, st, "replica broadcast")) != DMOE_OK) {
+    drop_new();
+    return s;
+  }
+  for (int f = 0; f < 3; ++f)
+    if ((s = map_weight(nw[f])) != DMOE_OK) {
+      drop_new();
+      return s;
+    }
+  for (int f = 0; f < 3; ++f) {
+    free_weight(*fam[f]);
+    *fam[f] = nw[f];
+  }
+  std::vector<int32_t> slot((size_t)E, -1);
+  for (int j = 0; j < n_hot; ++j) slot[(size_t)chosen[(size_t)j]] = j;
+  DMOE_CUDA(cudaMemcpy(L->hot_slot, slot.data(), sizeof(int32_t) * (size_t)E, cudaMemcpyHostToDevice));
+  L->n_hot = n_hot;
+  L->hot_ids = chosen;
+  L->last_stream = st;
   return DMOE_OK;
 }
 

@@ -124,11 +124,13 @@ cudaError_t launch_gather(const float* x, int64_t n, int h, int top_k, const int
 cudaError_t launch_combine(const float* y, int64_t y_ld, int64_t n, const int32_t* pair_row, int top_k, float* out,
                            int64_t h, int add_out, cudaStream_t st);
 // expert parallelism (ep.cu)
-cudaError_t launch_ep_plan(const int32_t* idx, int64_t n, int top_k, int e_local, int world, uint32_t* mask,
-                           int32_t* pos, int32_t* cnt, cudaStream_t st);
+// hot_slot: [n_expert] replica slot of each expert held by every rank, -1 otherwise (or null)
+cudaError_t launch_ep_plan(const int32_t* idx, int64_t n, int top_k, int e_local, const int32_t* hot_slot,
+                           int my_rank, int world, uint32_t* mask, int32_t* pos, int32_t* cnt, int cnt_stride,
+                           cudaStream_t st);
 cudaError_t launch_ep_pack(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
-                           int e_local, const uint32_t* mask, const int32_t* pos, const RankOffsets& soff, int swap,
-                           __half* xs, int32_t* meta, cudaStream_t st);
+                           int e_local, const int32_t* hot_slot, int my_rank, const uint32_t* mask, const int32_t* pos,
+                           const RankOffsets& soff, int swap, __half* xs, int32_t* meta, cudaStream_t st);
 cudaError_t launch_ep_count(const int32_t* meta, int64_t rows, int top_k, int32_t* counts, cudaStream_t st);
 cudaError_t launch_gather_rows(const __half* xr, int64_t rows, int h, int top_k, const int32_t* meta,
                                const int32_t* off, int32_t* fill, __half* xg, int32_t* pair_tok, float* pair_w,

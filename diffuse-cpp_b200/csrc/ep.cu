@@ -4,7 +4,10 @@
 // replicated, and each rank routes its own token blocks (capacity sets are per block, so
 // routing needs no communication). One forward on rank r:
 //   ep_mask_kernel     mask[t]: bit d set iff a slot of token t selects an expert of rank d
+//                      (an expert replicated on every rank counts as this rank's: hot_slot)
 //   ep_scan_kernel     pos[d][t]: slot of token t in the rows sent to rank d; cnt[d]
+//   (a forward runs these per chunk of its tokens; chunk k's GEMMs overlap the next chunk's
+//   dispatch and the previous chunk's combine, which run on a communication stream)
 //   ep_pack_kernel     one fp16 row per (token, destination) plus its slot list: the rank-local
 //                      expert id (or -1) and the gate weight of each of the top_k slots
 //   (NCCL: counts, then rows and slot lists, grouped ncclSend / ncclRecv)
@@ -18,18 +21,33 @@
 
 namespace dmoe {
 
+// Where a (token, slot) is computed: the owner of its expert, or this rank when every rank holds
+// a replica of the expert (hot_slot[e] >= 0); and the expert's index among that rank's local
+// experts (owned ones first, then the replicas).
+struct SlotDest {
+  int rank, local;
+};
+__device__ __forceinline__ SlotDest slot_dest(int e, int e_local, const int32_t* hot_slot, int my_rank) {
+  const int hs = hot_slot ? hot_slot[e] : -1;
+  if (hs >= 0) return {my_rank, e_local + hs};
+  const int d = e / e_local;
+  return {d, e - d * e_local};
+}
+
 __global__ void ep_mask_kernel(const int32_t* __restrict__ idx, int64_t n, int top_k, int e_local,
-                               uint32_t* __restrict__ mask) {
+                               const int32_t* __restrict__ hot_slot, int my_rank, uint32_t* __restrict__ mask) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= n) return;
   uint32_t m = 0;
-  for (int s = 0; s < top_k; ++s) m |= 1u << (idx[t * top_k + s] / e_local);
+  for (int s = 0; s < top_k; ++s) m |= 1u << slot_dest(idx[t * top_k + s], e_local, hot_slot, my_rank).rank;
   mask[t] = m;
 }
 
-// One CTA (1024 threads) per destination rank: exclusive scan over tokens of bit d.
+// One CTA (1024 threads) per destination rank: exclusive scan over tokens of bit d; the count
+// of rank d goes to cnt[d * cnt_stride] (per-chunk counts interleaved by destination).
 __global__ void __launch_bounds__(1024) ep_scan_kernel(const uint32_t* __restrict__ mask, int64_t n,
-                                                       int32_t* __restrict__ pos, int32_t* __restrict__ cnt) {
+                                                       int32_t* __restrict__ pos, int32_t* __restrict__ cnt,
+                                                       int cnt_stride) {
   __shared__ int32_t warp_sum[32];
   __shared__ int32_t s_total;
   const int d = blockIdx.x;
@@ -58,7 +76,7 @@ __global__ void __launch_bounds__(1024) ep_scan_kernel(const uint32_t* __restric
     running += s_total;
     __syncthreads();
   }
-  if (tid == 0) cnt[d] = running;
+  if (tid == 0) cnt[(int64_t)d * cnt_stride] = running;
 }
 
 // One CTA per token: its fp16 row (quad-swapped when the routed matrices are q4_K) and slot list
@@ -66,7 +84,8 @@ __global__ void __launch_bounds__(1024) ep_scan_kernel(const uint32_t* __restric
 // followed by top_k fp32 gate weights.
 __global__ void __launch_bounds__(256) ep_pack_kernel(const float* __restrict__ x, int64_t n, int h, int top_k,
                                                       const int32_t* __restrict__ idx, const float* __restrict__ w,
-                                                      int e_local, const uint32_t* __restrict__ mask,
+                                                      int e_local, const int32_t* __restrict__ hot_slot, int my_rank,
+                                                      const uint32_t* __restrict__ mask,
                                                       const int32_t* __restrict__ pos, RankOffsets soff, int swap,
                                                       __half* __restrict__ xs, int32_t* __restrict__ meta) {
   __shared__ int64_t rows[kMaxRanks];
@@ -83,14 +102,13 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const float* __restrict__ 
   __syncthreads();
   // slot lists: thread s < top_k handles slot s for every destination
   if (tid < top_k) {
-    const int e = idx[t * top_k + tid];
-    const int de = e / e_local;
+    const SlotDest sd = slot_dest(idx[t * top_k + tid], e_local, hot_slot, my_rank);
     const float wv = w[t * top_k + tid];
     int k = 0;
     for (int d = 0; d < kMaxRanks; ++d) {
       if (!((m >> d) & 1u)) continue;
       int32_t* mr = meta + rows[k] * (2 * top_k);
-      mr[tid] = de == d ? e - d * e_local : -1;
+      mr[tid] = sd.rank == d ? sd.local : -1;
       mr[top_k + tid] = __float_as_int(wv);
       ++k;
     }
@@ -205,20 +223,23 @@ __global__ void __launch_bounds__(256) ep_final_kernel(float* __restrict__ out, 
   }
 }
 
-cudaError_t launch_ep_plan(const int32_t* idx, int64_t n, int top_k, int e_local, int world, uint32_t* mask,
-                           int32_t* pos, int32_t* cnt, cudaStream_t st) {
-  if (n == 0 || world > kMaxRanks) return world > kMaxRanks ? cudaErrorInvalidValue : cudaSuccess;
-  ep_mask_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(idx, n, top_k, e_local, mask);
-  ep_scan_kernel<<<(unsigned)world, 1024, 0, st>>>(mask, n, pos, cnt);
+cudaError_t launch_ep_plan(const int32_t* idx, int64_t n, int top_k, int e_local, const int32_t* hot_slot,
+                           int my_rank, int world, uint32_t* mask, int32_t* pos, int32_t* cnt, int cnt_stride,
+                           cudaStream_t st) {
+  if (world > kMaxRanks) return cudaErrorInvalidValue;
+  if (n > 0)
+    ep_mask_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(idx, n, top_k, e_local, hot_slot, my_rank, mask);
+  ep_scan_kernel<<<(unsigned)world, 1024, 0, st>>>(mask, n, pos, cnt, cnt_stride);  // n = 0: zero counts
   return cudaGetLastError();
 }
 
 cudaError_t launch_ep_pack(const float* x, int64_t n, int h, int top_k, const int32_t* idx, const float* w,
-                           int e_local, const uint32_t* mask, const int32_t* pos, const RankOffsets& soff, int swap,
-                           __half* xs, int32_t* meta, cudaStream_t st) {
+                           int e_local, const int32_t* hot_slot, int my_rank, const uint32_t* mask, const int32_t* pos,
+                           const RankOffsets& soff, int swap, __half* xs, int32_t* meta, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   if (top_k > 256) return cudaErrorInvalidValue;
-  ep_pack_kernel<<<(unsigned)n, 256, 0, st>>>(x, n, h, top_k, idx, w, e_local, mask, pos, soff, swap, xs, meta);
+  ep_pack_kernel<<<(unsigned)n, 256, 0, st>>>(x, n, h, top_k, idx, w, e_local, hot_slot, my_rank, mask, pos, soff,
+                                              swap, xs, meta);
   return cudaGetLastError();
 }
 

@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR, BRES>::THREA
     // weights read by one token tile stream through L2 (evict first); weights of experts with
     // several token tiles are re-read and kept (evict normal) -- chosen by the host
     const uint64_t pol_w = p.w_keep ? l2_policy_evict_normal() : l2_policy_evict_first();
-    if (blockIdx.x == 0 && lane == 0) {
+    if (blockIdx.x == 0 && lane == 0 && (p.grp[1].present || (MODE == MODE_FUSED && p.grp_dn[1].present))) {
       int over;
       tile_count_checked(*p.n_tiles, p.tiles_cap, &over);
       if (over) atomicOr(p.err, ERRBIT_BAD_TILE);  // more routed tiles than the list holds

@@ -29,6 +29,8 @@ const NcclApi& nccl() {
     sym(api.CommGetAsyncError, "ncclCommGetAsyncError");
     sym(api.Send, "ncclSend");
     sym(api.Recv, "ncclRecv");
+    sym(api.Broadcast, "ncclBroadcast");
+    sym(api.AllReduce, "ncclAllReduce");
     sym(api.GroupStart, "ncclGroupStart");
     sym(api.GroupEnd, "ncclGroupEnd");
     sym(api.GetErrorString, "ncclGetErrorString");

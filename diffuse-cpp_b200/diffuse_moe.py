@@ -146,6 +146,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.dmoe_route_static.restype = ctypes.c_int
     lib.dmoe_nccl_unique_id.argtypes = [P]
     lib.dmoe_nccl_unique_id.restype = ctypes.c_int
+    lib.dmoe_replicate_experts.argtypes = [P, P, ctypes.c_int32]
+    lib.dmoe_replicate_experts.restype = ctypes.c_int
     lib.dmoe_sample_step.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int32, ctypes.c_int32,
                                      ctypes.c_float, P, P, P, P]
     lib.dmoe_sample_step.restype = ctypes.c_int
@@ -289,6 +291,17 @@ class MoELayer:
 
     def sync(self) -> None:
         _check(load().dmoe_sync(self._h))
+
+    def replicate_experts(self, n_hot: int, ids=None) -> None:
+        """dmoe_replicate_experts (collective on every rank of an expert-parallel layer): hold the
+        weights of n_hot experts on every rank, the given ids or (None) the busiest of the last
+        forward summed over the ranks; their (token, slot) pairs are then computed locally."""
+        arr = None
+        if ids is not None:
+            arr = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+            if arr.size != n_hot:
+                raise ValueError("len(ids) must equal n_hot")
+        _check(load().dmoe_replicate_experts(self._h, None if arr is None else arr.ctypes.data, n_hot))
 
     def stats(self) -> dict:
         s = Stats()

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define DMOE_ABI_VERSION 3
+#define DMOE_ABI_VERSION 4
 
 /* Replaces the reference's bool returns + DIFFUSE_DIE/exit(1) (src/diffuse-common.h:22-27,
  * src/diffuse-moe-graph.cpp:325-329). */
@@ -144,6 +144,19 @@ dmoe_status dmoe_create(const dmoe_layer_desc* desc, const dmoe_dist_cfg* dist, 
 /* Writes a fresh 128-byte NCCL unique id for dmoe_dist_cfg.nccl_id (create it on one rank and
  * share it with the others). No counterpart in the reference, which runs on one device. */
 dmoe_status dmoe_nccl_unique_id(void* id128);
+
+/* Hot-expert replication for skewed expert-parallel loads. No counterpart in the reference,
+ * which runs on one device. Collective: every rank calls it with the same arguments, between
+ * forwards. Afterwards every rank holds the weights of n_hot experts besides its own (each copied
+ * once from its owner, NCCL broadcast; the host tensors are not needed), and a (token, slot)
+ * that selects one of them is computed on the token's own rank, with no exchange; results are
+ * unchanged. ids: the experts to replicate, distinct, in [0, n_expert), identical on every
+ * rank; NULL: the n_hot experts with the most (token, slot) pairs in the layer's last forward,
+ * summed over the ranks (ties to the lower id). n_hot = 0 drops the replicas. Requires
+ * n_hot <= DMOE_MAX_HOT and n_hot <= n_expert - n_expert / world_size. Each replica costs one
+ * expert's weights of device memory per rank. On one GPU it returns DMOE_OK and does nothing. */
+#define DMOE_MAX_HOT 64
+dmoe_status dmoe_replicate_experts(struct dmoe_layer* layer, const int32_t* ids, int32_t n_hot);
 
 /* moe_out = MoE(x). Replaces src/diffuse-moe-graph.cpp:195-287 (router :203-262, experts
  * :264-278, shared expert :280-286). x and out are [n_tokens][n_embd] f32, row-major (ggml

@@ -31,7 +31,15 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version():
-    assert dm.load().dmoe_abi_version() == 3
+    assert dm.load().dmoe_abi_version() == 4
+
+
+def test_replicate_experts_argument_errors():
+    """dmoe_replicate_experts refuses a null layer and an n_hot outside [0, DMOE_MAX_HOT] before
+    any device or NCCL work."""
+    lib = dm.load()
+    assert lib.dmoe_replicate_experts(None, None, 4) == 1  # DMOE_ERR_INVALID_ARG
+    assert "null layer" in dm.last_error()
 
 
 def test_argument_errors_are_status_codes():

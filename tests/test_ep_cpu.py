@@ -35,15 +35,17 @@ def spec():
     return synth.LayerSpec(H=256, I=256, Is=256, E=8, top_k=3, cap=4, blk=32, expert_type=dm.TYPE_Q8_0, seed=21)
 
 
-def local_tensors(t, hp, rank, world):
-    """This rank's expert slice of each [E][rows][k] GGUF tensor (what dmoe_create uploads)."""
+def local_tensors(t, hp, rank, world, hot=()):
+    """This rank's expert slice of each [E][rows][k] GGUF tensor (what dmoe_create uploads),
+    followed by the replicated hot experts (what dmoe_replicate_experts adds)."""
     el = hp["n_expert"] // world
     out = {}
     for name, rows in (("w_gate", hp["n_ff_exp"]), ("w_up", hp["n_ff_exp"]), ("w_down", hp["n_embd"])):
         a = np.asarray(t[name])
         per = a.shape[0] // hp["n_expert"]
         assert per == rows
-        out[name] = a[rank * el * per:(rank + 1) * el * per]
+        parts = [a[rank * el * per:(rank + 1) * el * per]] + [a[e * per:(e + 1) * per] for e in hot]
+        out[name] = np.concatenate(parts)
     return out
 
 
@@ -55,7 +57,7 @@ def exchange(objs_by_dest):
     return [gathered[src][me] for src in range(WORLD)]
 
 
-def worker(rank, port, ret):
+def worker(rank, port, ret, chunks=1, hot=()):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
@@ -69,33 +71,47 @@ def worker(rank, port, ret):
         lg = oracle.logits(x, t["w_router"])
         idx, w, _, _, _ = oracle.route(lg, t["b_router"], K, hp["expert_capacity"], hp["moe_block_size"],
                                        hp["norm_topk_prob"], hp["routed_scaling"])
-        # plan: one row per (token, owning rank), slot list with local ids (-1 elsewhere)
+        # plan: one row per (token, computing rank), slot list with local ids (-1 elsewhere); a
+        # slot whose expert is replicated on every rank (hot) is computed here, at local id
+        # el + its replica index (the library's slot_dest)
+        hot = list(hot)
+
+        def dest(e):
+            return (rank, el + hot.index(e)) if e in hot else (e // el, e - (e // el) * el)
+
         sends = [[] for _ in range(WORLD)]
         for tok in range(x.shape[0]):
-            for d in sorted({int(e) // el for e in idx[tok]}):
-                slots = [(int(e) - d * el if int(e) // el == d else -1, float(w[tok, s])) for s, e in enumerate(idx[tok])]
+            ds = [dest(int(e)) for e in idx[tok]]
+            for d in sorted({r for r, _ in ds}):
+                slots = [(le if r == d else -1, float(w[tok, s])) for s, (r, le) in enumerate(ds)]
                 sends[d].append((tok, x[tok], slots))
-        recv = exchange([[(x_row, slots) for _, x_row, slots in sends[d]] for d in range(WORLD)])
-        # partial rows with only this rank's experts
-        lt = local_tensors(t, hp, rank, WORLD)
-        hp_l = dict(hp, n_expert=el, n_ff_shexp=0)
-        parts = []
-        for src in range(WORLD):
-            rows = recv[src]
-            if not rows:
-                parts.append(np.zeros((0, sp.H), np.float32))
-                continue
-            xr = np.stack([r[0] for r in rows]).astype(np.float32)
-            li = np.array([[max(e, 0) for e, _ in r[1]] for r in rows], dtype=np.int32)
-            lw = np.array([[wv if e >= 0 else 0.0 for e, wv in r[1]] for r in rows], dtype=np.float32)
-            parts.append(oracle.experts(hp_l, lt, xr, li, lw, mode=0))
-        back = exchange(parts)
-        # owner: shared rows + partials in rank order
+        # the exchange pipelined over chunks of this rank's tokens (the library's ep_chunks): every
+        # chunk's dispatch, then every chunk's partials and combine, in chunk order on all ranks
+        lt = local_tensors(t, hp, rank, WORLD, hot)
+        hp_l = dict(hp, n_expert=el + len(hot), n_ff_shexp=0)
+        n = x.shape[0]
+        bounds = [(n * c // chunks, n * (c + 1) // chunks) for c in range(chunks)]
+        in_chunk = [[[(tok, xr_, sl) for tok, xr_, sl in sends[d] if lo <= tok < hi] for d in range(WORLD)]
+                    for lo, hi in bounds]
+        recvs = [exchange([[(x_row, slots) for _, x_row, slots in cs[d]] for d in range(WORLD)]) for cs in in_chunk]
         shared = oracle.experts(hp, t, x, np.zeros_like(idx), np.zeros_like(w), mode=0)
         acc = np.zeros_like(shared)
-        for d in range(WORLD):
-            for j, (tok, _, _) in enumerate(sends[d]):
-                acc[tok] += back[d][j]
+        for c, recv in enumerate(recvs):
+            parts = []  # partial rows with only this rank's experts
+            for src in range(WORLD):
+                rows = recv[src]
+                if not rows:
+                    parts.append(np.zeros((0, sp.H), np.float32))
+                    continue
+                xr = np.stack([r[0] for r in rows]).astype(np.float32)
+                li = np.array([[max(e, 0) for e, _ in r[1]] for r in rows], dtype=np.int32)
+                lw = np.array([[wv if e >= 0 else 0.0 for e, wv in r[1]] for r in rows], dtype=np.float32)
+                parts.append(oracle.experts(hp_l, lt, xr, li, lw, mode=0))
+            back = exchange(parts)
+            # owner: partials of the chunk's tokens in rank order
+            for d in range(WORLD):
+                for j, (tok, _, _) in enumerate(in_chunk[c][d]):
+                    acc[tok] += back[d][j]
         out = acc + shared
         ref = oracle.layer(hp, t, x, mode=0)[0]
         err = float(np.linalg.norm(out - ref) / np.linalg.norm(ref))
@@ -105,10 +121,13 @@ def worker(rank, port, ret):
 
 
 @pytest.mark.timeout(300)
-def test_expert_parallel_decomposition_gloo():
+@pytest.mark.parametrize("chunks,hot", [(1, ()), (3, ()), (2, (0, 5, 6))])
+def test_expert_parallel_decomposition_gloo(chunks, hot):
+    """chunks: the exchange pipelined over chunks of each rank's tokens; hot: experts replicated
+    on every rank (one owned by each rank and one more), whose slots are computed locally."""
     ctx = mp.get_context("spawn")
     ret = ctx.Manager().dict()
-    mp.start_processes(worker, args=(free_port(), ret), nprocs=WORLD, start_method="spawn")
+    mp.start_processes(worker, args=(free_port(), ret, chunks, hot), nprocs=WORLD, start_method="spawn")
     assert sorted(ret.keys()) == list(range(WORLD))
     for r in range(WORLD):
         assert ret[r] < 1e-5, (r, ret[r])

@@ -34,8 +34,9 @@ def layer_spec(kind: str) -> synth.LayerSpec:
     return synth.LayerSpec(H=2048, I=512, Is=512, E=256, top_k=8, cap=48, blk=32, expert_type=dm.TYPE_Q8_0, seed=32)
 
 
-def worker(rank, kind, ntok, nccl_id, ret):
+def worker(rank, kind, ntok, nccl_id, ret, chunks=4):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["DMOE_EP_CHUNKS"] = str(chunks)  # read by dmoe_create; the same on every rank
     try:
         sp = layer_spec(kind)
         hp = sp.hparams()
@@ -56,13 +57,13 @@ def worker(rank, kind, ntok, nccl_id, ret):
         ret[rank] = ("error", repr(e))
 
 
-def run_world(kind, ntok):
+def run_world(kind, ntok, chunks=4):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     ret = ctx.Manager().dict()
     nccl_id = dm.nccl_unique_id()
-    procs = [ctx.Process(target=worker, args=(r, kind, ntok, nccl_id, ret)) for r in range(WORLD)]
+    procs = [ctx.Process(target=worker, args=(r, kind, ntok, nccl_id, ret, chunks)) for r in range(WORLD)]
     for p in procs:
         p.start()
     for p in procs:
@@ -73,9 +74,12 @@ def run_world(kind, ntok):
 
 @pytest.mark.gpu
 @needs2
-@pytest.mark.parametrize("kind,ntok", [("tiny", 64), ("s_q8", 256)])
-def test_ep_two_ranks_match_oracle(kind, ntok):
-    ret = run_world(kind, ntok)
+@pytest.mark.parametrize("kind,ntok,chunks", [("tiny", 64, 1), ("tiny", 64, 4), ("tiny", 32, 8), ("s_q8", 256, 1),
+                                              ("s_q8", 256, 4)])
+def test_ep_two_ranks_match_oracle(kind, ntok, chunks):
+    """The exchange pipelined over `chunks` chunks of each rank's tokens (32 tokens in 8 chunks:
+    every chunk's NCCL groups run, some with nothing to send) gives the oracle's answer."""
+    ret = run_world(kind, ntok, chunks)
     for r in range(WORLD):
         v = ret[r]
         assert v[0] != "error", v
@@ -115,3 +119,63 @@ def test_ep_rank_that_never_joins_times_out():
     assert p.exitcode == 0
     assert ret["status"] == 6, ret  # DMOE_ERR_TIMEOUT
     assert ret["seconds"] < 30, ret
+
+
+def replica_worker(rank, nccl_id, ret):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        # small layer shape, q8_0, Zipf-skewed expert bias: a few experts take most of the slots
+        sp = synth.LayerSpec(H=2048, I=512, Is=512, E=256, top_k=8, cap=48, blk=32, expert_type=dm.TYPE_Q8_0,
+                             bias="zipf", seed=34)
+        hp = sp.hparams()
+        t = synth.make_layer(sp)
+        x = synth.make_input(512, sp.H, 700 + rank)
+        r_out, r_idx, r_w, _, _ = oracle.layer(hp, t, x)
+        L = dm.MoELayer(hp, t, dist=dm.dist_cfg(rank, WORLD, rank, nccl_id, timeout_ms=60000))
+        res = {}
+
+        def run(tag):
+            out, (idx, w, _) = L.forward(x, route=True)
+            st = L.stats()
+            err = float(np.linalg.norm(out.astype(np.float64) - r_out) / np.linalg.norm(r_out))
+            res[tag] = (bool(np.array_equal(idx, r_idx)), err, int(st["ep_rows_sent"]), int(st["ep_rows_received"]))
+
+        run("plain")
+        L.replicate_experts(8)                      # the busiest 8 of that forward, over both ranks
+        run("auto8")
+        load = np.bincount(r_idx.ravel(), minlength=256)
+        L.replicate_experts(3, ids=[int(np.argmax(load)), 5, 200])  # explicit ids (same on every rank)
+        run("ids3")
+        L.replicate_experts(0)                      # replicas dropped
+        run("none")
+        L.close()
+        ret[rank] = res
+    except Exception as e:  # reported to the parent
+        ret[rank] = ("error", repr(e))
+
+
+@pytest.mark.gpu
+@needs2
+def test_ep_hot_expert_replicas():
+    """Replicated hot experts leave the results unchanged (oracle bar, routing exact) and take
+    their (token, slot) pairs off the exchange: fewer rows cross to the other rank."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    nccl_id = dm.nccl_unique_id()
+    procs = [ctx.Process(target=replica_worker, args=(r, nccl_id, ret)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(600)
+        assert p.exitcode == 0
+    for r in range(WORLD):
+        res = ret[r]
+        assert res[0] != "error", res
+        for tag, (ok, err, sent, recvd) in res.items():
+            assert ok, (r, tag)
+            assert err <= 2e-3, (r, tag, err)
+        # rows sent to the other rank: with the busiest experts local, fewer (token, rank) rows
+        assert res["auto8"][2] < res["plain"][2], res
+        assert res["none"][2] == res["plain"][2], res
