@@ -172,7 +172,7 @@ def test_ep_hot_expert_replicas():
         assert p.exitcode == 0
     for r in range(WORLD):
         res = ret[r]
-        assert res[0] != "error", res
+        assert isinstance(res, dict), res  # the worker reports ("error", message) on failure
         for tag, (ok, err, sent, recvd) in res.items():
             assert ok, (r, tag)
             assert err <= 2e-3, (r, tag, err)
