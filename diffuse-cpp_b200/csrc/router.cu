@@ -59,9 +59,10 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Router logits. CTA = 128 threads on a (16 TM) token x 64 expert tile; thread (ty, tx) =
-// (tid / 8, tid % 8) owns tokens TM ty .. TM ty + TM - 1 and experts {4 tx .. 4 tx + 3} u
-// {32 + 4 tx .. 32 + 4 tx + 3}: TM x 8 independent fma chains. x [token][k] and the transposed
+// Router logits. CTA = 256 threads on a (16 TM) token x 64 expert tile; thread (ty, tx) =
+// (tid / 16, tid % 16) owns tokens TM ty .. TM ty + TM - 1 and experts 4 tx .. 4 tx + 3: TM x 4
+// independent fma chains (256 threads rather than 128 with 8 experts each: twice the warps per SM
+// to hide the shared-memory load latency at the same tile, shared-memory footprint and order). x [token][k] and the transposed
 // router weight wrt [k][expert] (transposed once at bind time) arrive in 32-k chunks through a
 // 3-deep cp.async ring.
 //   SPLIT = false: the CTA runs every 256-k segment and keeps tot = P_0 + P_1 + ...; writes
@@ -74,7 +75,8 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 // weight re-read a quarter as often), split by segment while whole-K TM = 8 tiles cannot fill the
 // GPU; TM = 2 split for the smallest N (more CTAs).
 // ------------------------------------------------------------------------------------------
-constexpr int RL_EXP = 64, RL_KC = 32, RL_THREADS = 128;
+constexpr int RL_EXP = 64, RL_KC = 32, RL_EPT = 4, RL_TX = RL_EXP / RL_EPT, RL_THREADS = 16 * RL_TX;
+static_assert(RL_EPT == 4, "a thread's experts are one 16-byte weight load and one float4 store per token");
 constexpr int RL_XP = RL_KC + 4;  // x tile row pitch (floats)
 
 template <int TM>
@@ -92,7 +94,7 @@ template <int TM>
 constexpr bool rl_tot_smem() { return TM >= 7; }
 template <int TM, bool SPLIT>
 constexpr int rl_smem() {
-  return rl_stages<TM, SPLIT>() * rl_stage_floats<TM>() * 4 + (rl_tot_smem<TM>() ? TM * 8 * RL_THREADS * 4 : 0);
+  return rl_stages<TM, SPLIT>() * rl_stage_floats<TM>() * 4 + (rl_tot_smem<TM>() ? TM * RL_EPT * RL_THREADS * 4 : 0);
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -126,7 +128,7 @@ __device__ __forceinline__ void lds2x64(uint32_t a, f32x2& lo, f32x2& hi) {
 }
 
 template <int TM, bool SPLIT>
-__global__ void __launch_bounds__(RL_THREADS, TM >= 7 ? 2 : 4) router_logits_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(RL_THREADS, 2) router_logits_kernel(const float* __restrict__ x,
                                                                    const float* __restrict__ wrt,
                                                                    float* __restrict__ part, int64_t n, int h, int e,
                                                                    int32_t* __restrict__ arrivals,
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(RL_THREADS, TM >= 7 ? 2 : 4) router_logits_ker
   constexpr int RL_STAGES = rl_stages<TM, SPLIT>();
   const uint32_t sm0 = smem_u32(rl_smem_f);
   const int tid = threadIdx.x;
-  const int ty = tid >> 3, tx = tid & 7;
+  const int ty = tid / RL_TX, tx = tid % RL_TX;
   const int64_t t0 = (int64_t)blockIdx.x * TT;
   const int e0 = blockIdx.y * RL_EXP;
   const int nseg = h / kRouterSeg;
@@ -170,19 +172,22 @@ __global__ void __launch_bounds__(RL_THREADS, TM >= 7 ? 2 : 4) router_logits_ker
   };
 
   constexpr bool TOT_SMEM = rl_tot_smem<TM>();
-  float tot[TOT_SMEM ? 1 : TM][8];
-  float* tot_s = rl_smem_f + RL_STAGES * rl_stage_floats<TM>();  // TOT_SMEM: [TM * 8][RL_THREADS]
-  f32x2 acc[TM][4];  // experts (2 jp, 2 jp + 1) of the thread's 8, packed
+  constexpr int NJP = RL_EPT / 2;
+  float tot[TOT_SMEM ? 1 : TM][RL_EPT];
+  float* tot_s = rl_smem_f + RL_STAGES * rl_stage_floats<TM>();  // TOT_SMEM: [TM * RL_EPT][RL_THREADS]
+  f32x2 acc[TM][NJP];  // experts (2 jp, 2 jp + 1) of the thread's RL_EPT, packed
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < RL_EPT; ++j)
       if (!TOT_SMEM) tot[i][j] = 0.0f;
 #pragma unroll
-    for (int jp = 0; jp < 4; ++jp) acc[i][jp] = 0ull;  // (+0.0f, +0.0f)
+    for (int jp = 0; jp < NJP; ++jp) acc[i][jp] = 0ull;  // (+0.0f, +0.0f)
   }
-  // tot[i][j] lives in tot_s[(8 i + j) * RL_THREADS + tid] when TOT_SMEM
-  auto tot_ref = [&](int i, int j) -> float& { return TOT_SMEM ? tot_s[(8 * i + j) * RL_THREADS + tid] : tot[TOT_SMEM ? 0 : i][j]; };
+  // tot[i][j] lives in tot_s[(RL_EPT i + j) * RL_THREADS + tid] when TOT_SMEM
+  auto tot_ref = [&](int i, int j) -> float& {
+    return TOT_SMEM ? tot_s[(RL_EPT * i + j) * RL_THREADS + tid] : tot[TOT_SMEM ? 0 : i][j];
+  };
 
 #pragma unroll
   for (int c = 0; c < RL_STAGES - 1; ++c) {
@@ -204,14 +209,13 @@ __global__ void __launch_bounds__(RL_THREADS, TM >= 7 ? 2 : 4) router_logits_ker
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t wrow = ws + ((4 * k4 + kk) * RL_EXP) * 4;
-        f32x2 wp[4];
-        lds2x64(wrow + (4 * tx) * 4, wp[0], wp[1]);
-        lds2x64(wrow + (32 + 4 * tx) * 4, wp[2], wp[3]);
+        f32x2 wp[NJP];
+        lds2x64(wrow + (RL_EPT * tx) * 4, wp[0], wp[1]);
 #pragma unroll
         for (int i = 0; i < TM; ++i) {
           const f32x2 xx = dup2(kk == 0 ? xv[i].x : kk == 1 ? xv[i].y : kk == 2 ? xv[i].z : xv[i].w);
 #pragma unroll
-          for (int jp = 0; jp < 4; ++jp) ffma2(acc[i][jp], xx, wp[jp]);
+          for (int jp = 0; jp < NJP; ++jp) ffma2(acc[i][jp], xx, wp[jp]);
         }
       }
     }
@@ -220,7 +224,7 @@ __global__ void __launch_bounds__(RL_THREADS, TM >= 7 ? 2 : 4) router_logits_ker
 #pragma unroll
       for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int jp = 0; jp < 4; ++jp) {
+        for (int jp = 0; jp < NJP; ++jp) {
           const float2 a = unpack2(acc[i][jp]);
           float& t0r = tot_ref(i, 2 * jp);
           float& t1r = tot_ref(i, 2 * jp + 1);
@@ -237,8 +241,8 @@ __global__ void __launch_bounds__(RL_THREADS, TM >= 7 ? 2 : 4) router_logits_ker
     const int64_t tok = t0 + TM * ty + i;
     if (tok >= n) continue;
 #pragma unroll
-    for (int j = 0; j < 8; j += 4) {
-      const int ee = e0 + (j == 0 ? 4 * tx : 32 + 4 * tx);
+    for (int j = 0; j < RL_EPT; j += 4) {
+      const int ee = e0 + RL_EPT * tx + j;
       if (ee >= e) continue;
       const float v0 = tot_ref(i, j), v1 = tot_ref(i, j + 1), v2 = tot_ref(i, j + 2), v3 = tot_ref(i, j + 3);
       if constexpr (SPLIT) {
