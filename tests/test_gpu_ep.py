@@ -179,3 +179,47 @@ def test_ep_hot_expert_replicas():
         # rows sent to the other rank: with the busiest experts local, fewer (token, rank) rows
         assert res["auto8"][2] < res["plain"][2], res
         assert res["none"][2] == res["plain"][2], res
+
+
+def empty_rank_worker(rank, nccl_id, ret):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        sp = layer_spec("tiny")
+        hp = sp.hparams()
+        t = synth.make_layer(sp)
+        n = 64 if rank == 0 else 0  # rank 1 has no tokens this forward
+        x = synth.make_input(max(n, 1), sp.H, 900)[:n]
+        L = dm.MoELayer(hp, t, dist=dm.dist_cfg(rank, WORLD, rank, nccl_id, timeout_ms=30000))
+        out = L.forward(x)
+        out2 = L.forward(x)
+        L.close()
+        if n:
+            r_out = oracle.layer(hp, t, x)[0]
+            errs = [float(np.linalg.norm(o.astype(np.float64) - r_out) / np.linalg.norm(r_out)) for o in (out, out2)]
+        else:
+            errs = [0.0, 0.0] if out.shape == (0, sp.H) else [1.0, 1.0]
+        ret[rank] = ("ok", errs)
+    except Exception as e:  # reported to the parent
+        ret[rank] = ("error", repr(e))
+
+
+@pytest.mark.gpu
+@needs2
+def test_ep_rank_without_tokens():
+    """A rank with no tokens still takes its part in the exchange (its experts receive the other
+    rank's rows), so the forward completes on every rank and the other rank's output is right."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    nccl_id = dm.nccl_unique_id()
+    procs = [ctx.Process(target=empty_rank_worker, args=(r, nccl_id, ret)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    for r in range(WORLD):
+        status, errs = ret[r]
+        assert status == "ok", (r, errs)
+        assert max(errs) <= 2e-3, (r, errs)
