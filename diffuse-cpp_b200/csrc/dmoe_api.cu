@@ -457,9 +457,11 @@ dmoe_status run_experts(dmoe_layer* L, cudaStream_t st, int64_t n_sh, int64_t ro
   gp.grp[1].present = rt ? 1 : 0;
   // persistent grid; with the chunked expert-parallel exchange a few SMs stay free for NCCL
   const int grid = L->sms - L->gemm_sm_reserve;
-  // dequant warpgroups per CTA: the largest of 4 / 3 / 2 the TMEM ring allows (measured 2-3 %
-  // faster than 2 at 1-8 blocks)
-  const int ndq = env_int("DMOE_NDQ", 4);
+  // dequant warpgroups per CTA: 4 (or the most the TMEM ring allows) on 32-64 token tiles,
+  // measured 2-3 % faster than 2 at 1-8 blocks; 2 on 128-token tiles, where each warpgroup then
+  // alternates between two A-ring slots instead of waiting on one (B200, c3 at 8192 tokens:
+  // gate/up 1371 -> 1287 us, down 1068 -> 1027 us, against 4)
+  const int ndq = env_int("DMOE_NDQ", nt >= 128 ? 2 : 4);
   // One launch for both GEMMs at small N (the persistent kernel runs all gate/up tiles, then the
   // down tiles, each as soon as its token tile's h rows are written): saves a launch, its ramp
   // and its tail imbalance. Measured on B200 (c3): 1 block 107 -> 95 us for the two GEMMs, even

@@ -68,7 +68,13 @@ struct GemmCfg {
     return PAIR ? 2 * kMTile : (tmode == MODE_GATEUP ? kMTile : MATS * kMTile);
   }
   static constexpr int STAGE_K = (WT == WT_Q4_K) ? 256 : 128;
-  static constexpr int KB_PER_STAGE = STAGE_K / 128;
+  // A block: the K range one dequant hand-off covers (TMEM columns ABK = AK / 2 per matrix).
+  // CTA pairs use 64-K blocks: their single-buffered 256-column accumulator leaves room for only
+  // two 128-K blocks, so each dequant warpgroup would own one buffer and strictly alternate with
+  // the MMA; four 64-K buffers let a warpgroup fill its next buffer while the MMA reads the last.
+  static constexpr int AK = (PAIR && QUANT) ? 64 : 128;
+  static constexpr int ABK = AK / 2;
+  static constexpr int KB_PER_STAGE = STAGE_K / AK;
   static constexpr int B_BYTES = STAGE_K * B_ROWS * 2;
   // per matrix per stage: q4_K 128 rows x one 144 B super-block; q8_0 128 x 128 int8 (SW128)
   // + 128 x 4 fp32 scales; f16 two SW128 boxes of 128 x 64.
@@ -88,7 +94,7 @@ struct GemmCfg {
   static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
   // TMEM: accumulators (double-buffered when they fit next to a 2+ deep A ring), A ring
   static constexpr int ACC_COLS = MATS * NT;
-  static constexpr int A_COLS = MATS * 64;
+  static constexpr int A_COLS = MATS * ABK;
   static constexpr int ACC_BUFS = (2 * ACC_COLS + (QUANT ? 2 * A_COLS : 0) <= 512) ? 2 : 1;
   static constexpr int NA_RAW = QUANT ? (512 - ACC_BUFS * ACC_COLS) / A_COLS : 0;
   static constexpr int NA = NA_RAW > 4 ? 4 : NA_RAW;
@@ -334,7 +340,9 @@ __device__ __forceinline__ bool warp_abort(volatile int* abort_flag) {
 // High nibbles: (q & 0x00F000F0) | 0x6400 -> 1024 + 16 q; minus 1024 -> 16 q (exact);
 // fma(16 q, d / 16, -m) with d / 16 an exact power-of-two rescaling of d (no shift needed).
 // Writes the row's 64 packed halves (TMEM columns 0..63 of the k-block's A block) into v.
-__device__ __forceinline__ void q4k_convert(uint32_t rowp, int kb, uint32_t (&v)[64]) {
+// NGL = 2: the whole 128-K half kb (64 columns); NGL = 1: its 64-K quarter gl0 (32 columns).
+template <int NGL>
+__device__ __forceinline__ void q4k_convert(uint32_t rowp, int kb, int gl0, uint32_t (&v)[32 * NGL]) {
   const uint4 hdr = lds128(rowp);
   const __half2 dd = as_h2(__byte_perm(hdr.x, 0, 0x1010));    // {d, d}
   const __half2 dmn = as_h2(__byte_perm(hdr.x, 0, 0x3232));   // {dmin, dmin}
@@ -356,18 +364,24 @@ __device__ __forceinline__ void q4k_convert(uint32_t rowp, int kb, uint32_t (&v)
   const __half2 dq01 = __hmul2(sc01, dd), dq23 = __hmul2(sc23, dd);
   const __half2 nm01 = __hneg2(__hmul2(mn01, dmn)), nm23 = __hneg2(__hmul2(mn23, dmn));
   // all of this K half's quants (64 bytes) are loaded before the first TMEM store
-  const uint32_t qp = rowp + 16 + 64 * kb;
-  const uint4 q0 = lds128(qp), q1 = lds128(qp + 16), q2 = lds128(qp + 32), q3 = lds128(qp + 48);
+  const uint32_t qp = rowp + 16 + 64 * kb + 32 * gl0;
+  const uint4 q0 = lds128(qp), q1 = lds128(qp + 16);
+  uint4 q2 = q0, q3 = q1;
+  if constexpr (NGL == 2) {
+    q2 = lds128(qp + 32);
+    q3 = lds128(qp + 48);
+  }
 #pragma unroll
-  for (int gl = 0; gl < 2; ++gl) {
+  for (int gi = 0; gi < NGL; ++gi) {
+    const int gl = gl0 + gi;
     // sub-blocks 2 gl (low nibbles) and 2 gl + 1 (high nibbles) of this K half
     const __half2 dlo = gl == 0 ? __low2half2(dq01) : __low2half2(dq23);
     const __half2 dhi = __hmul2(gl == 0 ? __high2half2(dq01) : __high2half2(dq23), k1_16);
     const __half2 mlo = gl == 0 ? __low2half2(nm01) : __low2half2(nm23);
     const __half2 mhi = gl == 0 ? __high2half2(nm01) : __high2half2(nm23);
-    const uint4 qa = gl == 0 ? q0 : q2, qb = gl == 0 ? q1 : q3;
+    const uint4 qa = gi == 0 ? q0 : q2, qb = gi == 0 ? q1 : q3;
     const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    // columns [32 gl, 32 gl + 16): low nibbles; [32 gl + 16, 32 gl + 32): high nibbles
+    // columns [32 gi, 32 gi + 16): low nibbles; [32 gi + 16, 32 gi + 32): high nibbles
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       const uint32_t q = qw[w], q8 = q >> 8;
@@ -375,52 +389,61 @@ __device__ __forceinline__ void q4k_convert(uint32_t rowp, int kb, uint32_t (&v)
       const uint32_t v13 = lop3_and_or(q8, 0x000F000Fu, 0x64006400u);
       const uint32_t h02 = lop3_and_or(q, 0x00F000F0u, 0x64006400u);
       const uint32_t h13 = lop3_and_or(q8, 0x00F000F0u, 0x64006400u);
-      v[32 * gl + 2 * w] = as_u32(__hfma2(__hsub2(as_h2(v02), k1024), dlo, mlo));
-      v[32 * gl + 2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(v13), k1024), dlo, mlo));
-      v[32 * gl + 16 + 2 * w] = as_u32(__hfma2(__hsub2(as_h2(h02), k1024), dhi, mhi));
-      v[32 * gl + 16 + 2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(h13), k1024), dhi, mhi));
+      v[32 * gi + 2 * w] = as_u32(__hfma2(__hsub2(as_h2(v02), k1024), dlo, mlo));
+      v[32 * gi + 2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(v13), k1024), dlo, mlo));
+      v[32 * gi + 16 + 2 * w] = as_u32(__hfma2(__hsub2(as_h2(h02), k1024), dhi, mhi));
+      v[32 * gi + 16 + 2 * w + 1] = as_u32(__hfma2(__hsub2(as_h2(h13), k1024), dhi, mhi));
     }
   }
 }
 
 // q8_0 (repacked): `qtile` = shared address of a 128 x 128 int8 tile (128B-swizzled), `stile` =
-// 128 x 4 fp32 scales.
-__device__ __forceinline__ void q80_convert(uint32_t qtile, uint32_t stile, int row, uint32_t (&v)[64]) {
+// 128 x 4 fp32 scales. NB 32-quant blocks from blk0 (NB = 4: the whole row, 64 columns).
+template <int NB>
+__device__ __forceinline__ void q80_convert(uint32_t qtile, uint32_t stile, int row, int blk0, uint32_t (&v)[16 * NB]) {
   const float4 sc = lds128f(stile + row * 16);
   const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
   const __half2 k1152 = __float2half2_rn(1152.0f);
   const uint32_t rp = qtile + row * 128;
-  uint4 qv8[8];  // the row's 128 quants, loaded before the first TMEM store
+  uint4 qv8[2 * NB];  // the blocks' quants, loaded before the first TMEM store
 #pragma unroll
-  for (int c = 0; c < 8; ++c) qv8[c] = lds128(rp + ((c ^ (row & 7)) << 4));
+  for (int c = 0; c < 2 * NB; ++c) qv8[c] = lds128(rp + (((2 * blk0 + c) ^ (row & 7)) << 4));
 #pragma unroll
-  for (int blk = 0; blk < 4; ++blk) {  // columns [16 blk, 16 blk + 16): 32-quant block blk
-    const __half2 d2 = __float2half2_rn(scv[blk]);
+  for (int bi = 0; bi < NB; ++bi) {  // columns [16 bi, 16 bi + 16): 32-quant block blk0 + bi
+    const __half2 d2 = __float2half2_rn(scv[blk0 + bi]);
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
-      const uint4 qv = qv8[2 * blk + cc];
+      const uint4 qv = qv8[2 * bi + cc];
       const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         const uint32_t xq = qw[w] ^ 0x80808080u;
         const uint32_t v0 = __byte_perm(xq, 0x64646464u, 0x5140);
         const uint32_t v1 = __byte_perm(xq, 0x64646464u, 0x5342);
-        v[16 * blk + 8 * cc + 2 * w] = as_u32(__hmul2(__hsub2(as_h2(v0), k1152), d2));
-        v[16 * blk + 8 * cc + 2 * w + 1] = as_u32(__hmul2(__hsub2(as_h2(v1), k1152), d2));
+        v[16 * bi + 8 * cc + 2 * w] = as_u32(__hmul2(__hsub2(as_h2(v0), k1152), d2));
+        v[16 * bi + 8 * cc + 2 * w + 1] = as_u32(__hmul2(__hsub2(as_h2(v1), k1152), d2));
       }
     }
   }
 }
 
-// one weight row's k-block of weight tile `wt` (q4_K super-block rows or a q8_0 tile) as 64 packed halves
-template <int WT>
-__device__ __forceinline__ void convert_kblock(uint32_t wt, int row, int kb, uint32_t (&v)[64]) {
-  if constexpr (WT == WT_Q4_K) q4k_convert(wt + row * 144, kb, v);
-  else q80_convert(wt, wt + 128 * 128, row, v);
+// one weight row's A block `ab` (ABK packed halves: 64 for 128 K, 32 for 64 K) of weight tile
+// `wt` (q4_K super-block rows or a q8_0 tile)
+template <int WT, int ABK>
+__device__ __forceinline__ void convert_ablock(uint32_t wt, int row, int ab, uint32_t (&v)[ABK]) {
+  static_assert(ABK == 64 || ABK == 32, "A blocks of 128 or 64 K");
+  if constexpr (WT == WT_Q4_K) {
+    if constexpr (ABK == 64) q4k_convert<2>(wt + row * 144, ab, 0, v);
+    else q4k_convert<1>(wt + row * 144, ab >> 1, ab & 1, v);
+  } else {
+    if constexpr (ABK == 64) q80_convert<4>(wt, wt + 128 * 128, row, 0, v);
+    else q80_convert<2>(wt, wt + 128 * 128, row, 2 * ab, v);
+  }
 }
-__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&v)[64]) {
+template <int NC>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&v)[NC]) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) tmem_st16(taddr + 16 * j, *reinterpret_cast<const uint32_t(*)[16]>(&v[16 * j]));
+  for (int j = 0; j < NC / 16; ++j) tmem_st16(taddr + 16 * j, *reinterpret_cast<const uint32_t(*)[16]>(&v[16 * j]));
 }
 
 // silu(g) = g * (1 / (1 + e^-g)); for g -> -inf the reciprocal of inf is 0 and the product -0
@@ -685,17 +708,21 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR, BRES>::THREA
             if (!wbwait(&afull[a], u & 1u, ERRBIT_TIMEOUT_TMEM)) { ok = false; break; }
             tc_fence_after();
             const uint32_t abuf = tbase + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
+            constexpr int JS = C::ABK / 8;  // 16-K steps per A block
+            static_assert(JS == 8 || JS == 4, "A block steps");
             if (elect_one()) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const uint64_t bdesc = bdesc0 + (uint64_t)(((kb * 2 + j / 4) * (C::B_ROWS * 128) + (j % 4) * 32) >> 4);
+              for (int j = 0; j < JS; ++j) {
+                // K offset kb AK + 16 j: its 64-K box, then 32 bytes per 16-K step inside it
+                const int kofs = kb * C::AK + 16 * j;
+                const uint64_t bdesc = bdesc0 + (uint64_t)(((kofs / 64) * (C::B_ROWS * 128) + (kofs % 64) * 2) >> 4);
                 const uint32_t acc = (kb == 0 && j == 0) ? acc_first : 1u;
 #pragma unroll
                 for (int m = 0; m < C::MATS; ++m) {
                   if constexpr (C::PAIR)
-                    mma_f16_ts_pair(dbase + m * NT, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
+                    mma_f16_ts_pair(dbase + m * NT, abuf + m * C::ABK + 8 * j, bdesc, idesc, acc);
                   else
-                    mma_f16_ts(dbase + m * NT, abuf + m * 64 + 8 * j, bdesc, idesc, acc);
+                    mma_f16_ts(dbase + m * NT, abuf + m * C::ABK + 8 * j, bdesc, idesc, acc);
                 }
               }
               if constexpr (C::PAIR) mma_commit_pair(&aempty[a]);
@@ -913,15 +940,15 @@ __global__ void __launch_bounds__(GemmCfg<WT, MODE, NT, NDQ_, PAIR, BRES>::THREA
           const uint32_t u = kbs / C::NA;
           // the first matrix is converted while the A buffer may still be in use (PRECONVERT),
           // so only its TMEM store waits for the buffer
-          uint32_t v[64];
-          if constexpr (C::PRECONVERT) convert_kblock<WT>(smem_u32(wtile_ptr(s, 0)), row, kb, v);
+          uint32_t v[C::ABK];
+          if constexpr (C::PRECONVERT) convert_ablock<WT, C::ABK>(smem_u32(wtile_ptr(s, 0)), row, kb, v);
           if (!bwait(&aempty[a], (u & 1u) ^ 1u, ERRBIT_TIMEOUT_TMEM)) { ok = false; break; }
           tc_fence_after();
           const uint32_t abuf = tbase + lane_off + C::ACC_BUFS * C::ACC_COLS + a * C::A_COLS;
 #pragma unroll
           for (int m = 0; m < C::MATS; ++m) {
-            if (!C::PRECONVERT || m > 0) convert_kblock<WT>(smem_u32(wtile_ptr(s, m)), row, kb, v);
-            tmem_st64(abuf + m * 64, v);
+            if (!C::PRECONVERT || m > 0) convert_ablock<WT, C::ABK>(smem_u32(wtile_ptr(s, m)), row, kb, v);
+            tmem_st_cols<C::ABK>(abuf + m * C::ABK, v);
           }
           tmem_wait_st();
           tc_fence_before();

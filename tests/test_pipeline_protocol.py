@@ -23,13 +23,14 @@ def gemm_cfg(wt, mode, nt, ndq, pair=False):
     quant = wt != F16
     mats = 2 if (mode == GATEUP or nt <= 64) else 1  # down at NT <= 64: two 128-row blocks
     stage_k = 256 if wt == Q4_K else 128
-    kb = stage_k // 128
+    ak = 64 if (pair and quant) else 128  # K per A block (dequant hand-off): 64 for CTA pairs
+    kb = stage_k // ak
     b_bytes = stage_k * (nt // 2 if pair else nt) * 2  # a pair's CTA loads half the token rows
     w_bytes = 128 * 144 if wt == Q4_K else (128 * 128 + 128 * 16 if wt == Q8_0 else 128 * 128 * 2)
     stage_bytes = b_bytes + mats * w_bytes
     stages = min(6, (227 * 1024 - 2048) // stage_bytes)
     acc_cols = mats * nt
-    a_cols = mats * 64
+    a_cols = mats * ak // 2
     acc_bufs = 2 if 2 * acc_cols + (2 * a_cols if quant else 0) <= 512 else 1
     na = min(4, (512 - acc_bufs * acc_cols) // a_cols) if quant else 0
     ndq = ndq if quant else 0
@@ -427,8 +428,8 @@ def gemm_cfg_bres_pair(wt, ndq):
     stage_k = 256 if wt == Q4_K else 128
     w_bytes = 128 * 144 if wt == Q4_K else 128 * 128 + 128 * 16
     stages = min(6, (227 * 1024 - 2048 - 1024 * 64 * 2) // w_bytes)
-    na = min(4, (512 - 2 * 128) // 64)
-    return dict(stages=stages, na=na, ndq=ndq, kb=stage_k // 128, acc_bufs=2, quant=True, ring_ok=na >= ndq)
+    na = min(4, (512 - 2 * 128) // 32)  # 64-K A blocks (pairs): 32 columns each
+    return dict(stages=stages, na=na, ndq=ndq, kb=stage_k // 64, acc_bufs=2, quant=True, ring_ok=na >= ndq)
 
 
 def roles_bres_pair(cfg, units):
