@@ -15,9 +15,9 @@
 //   idx  = top-k of sel, descending, ties to the lower expert id                   (:252)
 //   w    = p[idx] / (float)(sum_s (double) p[idx_s]) * scale                       (:253-262)
 //
-// Two launches: router_logits_kernel (the GEMM, either whole logits or per-segment partials
-// P_s summed by the tile's last CTA, then p = sigmoid(logit)) and route_kernel (bias, then the
-// routing of one block per CTA).
+// Two launches: the router GEMM (router_logits_wide_kernel: whole logits on 128-expert tiles at
+// large N; router_logits_split_kernel: per-segment partials P_s summed by the tile's last CTA),
+// then p = sigmoid(logit); and route_kernel (bias, then the routing of one block per CTA).
 #include "dmoe_internal.h"
 #include "sm100.cuh"
 
@@ -59,21 +59,14 @@ __device__ __forceinline__ float sigmoid_canonical(float l) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Router logits. CTA = 256 threads on a (16 TM) token x 64 expert tile; thread (ty, tx) =
-// (tid / 16, tid % 16) owns tokens TM ty .. TM ty + TM - 1 and experts 4 tx .. 4 tx + 3: TM x 4
-// independent fma chains (256 threads rather than 128 with 8 experts each: twice the warps per SM
-// to hide the shared-memory load latency at the same tile, shared-memory footprint and order). x [token][k] and the transposed
-// router weight wrt [k][expert] (transposed once at bind time) arrive in 32-k chunks through a
-// 3-deep cp.async ring.
-//   SPLIT = false: the CTA runs every 256-k segment and keeps tot = P_0 + P_1 + ...; writes
-//                  p = sigmoid(logit) to part[0].
-//   SPLIT = true:  one CTA per (tile, segment) writes its partial P_s to part[s]; the last CTA
-//                  of a tile to finish (per-tile arrival counter) adds P_0 .. P_{S-1} left to
-//                  right, writes p to part[0] and re-arms the counter (small N, where whole-K
-//                  tiles cannot fill the GPU).
-// TM = 8 (or 7, to balance the SMs) for large N (fewer shared-memory reads per fma, the router
-// weight re-read a quarter as often), split by segment while whole-K TM = 8 tiles cannot fill the
-// GPU; TM = 2 split for the smallest N (more CTAs).
+// Router logits split by segment (small and mid N, where whole-K tiles cannot fill the GPU).
+// CTA = 256 threads on a (16 TM) token x 64 expert tile and one 256-k segment s (blockIdx.z);
+// thread (ty, tx) = (tid / 16, tid % 16) owns tokens TM ty .. TM ty + TM - 1 and experts
+// 4 tx .. 4 tx + 3: TM x 4 independent fma chains. x [token][k] and the transposed router weight
+// wrt [k][expert] (transposed once at bind time) arrive in 32-k chunks by cp.async. Each CTA
+// writes its partial P_s to part[s]; the last CTA of a tile to finish (per-tile arrival counter)
+// adds P_0 .. P_{S-1} left to right, writes p = sigmoid(logit) to part[0] and re-arms the counter.
+// TM = 8 from ~1000 tokens (fewer shared-memory reads per fma), TM = 2 below (more CTAs).
 // ------------------------------------------------------------------------------------------
 constexpr int RL_EXP = 64, RL_KC = 32, RL_EPT = 4, RL_TX = RL_EXP / RL_EPT, RL_THREADS = 16 * RL_TX;
 static_assert(RL_EPT == 4, "a thread's experts are one 16-byte weight load and one float4 store per token");
@@ -83,19 +76,12 @@ template <int TM>
 constexpr int rl_tok() { return 16 * TM; }
 template <int TM>
 constexpr int rl_stage_floats() { return rl_tok<TM>() * RL_XP + RL_KC * RL_EXP; }
-// ring depth: the TM = 2 split path prefetches its whole 256-k segment at once (one memory
-// latency instead of eight); TM = 8 tiles (four times the shared memory per chunk) keep a 3-deep
-// ring, split or not
-template <int TM, bool SPLIT>
-constexpr int rl_stages() { return (SPLIT && TM <= 2) ? kRouterSeg / RL_KC : 3; }
-// TM >= 7 keeps the running segment sums tot in shared memory (expert-major: [TM x 8][thread],
-// conflict-free) instead of 56-64 more registers
+// ring depth: TM = 2 tiles prefetch their whole 256-k segment at once (one memory latency
+// instead of eight); TM = 8 tiles (four times the shared memory per chunk) keep a 3-deep ring
 template <int TM>
-constexpr bool rl_tot_smem() { return TM >= 7; }
-template <int TM, bool SPLIT>
-constexpr int rl_smem() {
-  return rl_stages<TM, SPLIT>() * rl_stage_floats<TM>() * 4 + (rl_tot_smem<TM>() ? TM * RL_EPT * RL_THREADS * 4 : 0);
-}
+constexpr int rl_stages() { return TM <= 2 ? kRouterSeg / RL_KC : 3; }
+template <int TM>
+constexpr int rl_smem() { return rl_stages<TM>() * rl_stage_floats<TM>() * 4; }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
@@ -127,29 +113,28 @@ __device__ __forceinline__ void lds2x64(uint32_t a, f32x2& lo, f32x2& hi) {
   asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "r"(a));
 }
 
-template <int TM, bool SPLIT>
-__global__ void __launch_bounds__(RL_THREADS, 2) router_logits_kernel(const float* __restrict__ x,
-                                                                   const float* __restrict__ wrt,
-                                                                   float* __restrict__ part, int64_t n, int h, int e,
-                                                                   int32_t* __restrict__ arrivals,
-                                                                   int32_t* __restrict__ zero_counts) {
+template <int TM>
+__global__ void __launch_bounds__(RL_THREADS, 2) router_logits_split_kernel(const float* __restrict__ x,
+                                                                          const float* __restrict__ wrt,
+                                                                          float* __restrict__ part, int64_t n, int h,
+                                                                          int e, int32_t* __restrict__ arrivals,
+                                                                          int32_t* __restrict__ zero_counts) {
   extern __shared__ __align__(16) float rl_smem_f[];
   pdl_wait();
   pdl_trigger();
   if (zero_counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)  // route_kernel's counters
     for (int i = threadIdx.x; i < e; i += RL_THREADS) zero_counts[i] = 0;
   constexpr int TT = rl_tok<TM>();
-  constexpr int RL_STAGES = rl_stages<TM, SPLIT>();
+  constexpr int RL_STAGES = rl_stages<TM>();
+  constexpr int NCHUNKS = kRouterSeg / RL_KC;
   const uint32_t sm0 = smem_u32(rl_smem_f);
   const int tid = threadIdx.x;
   const int ty = tid / RL_TX, tx = tid % RL_TX;
   const int64_t t0 = (int64_t)blockIdx.x * TT;
   const int e0 = blockIdx.y * RL_EXP;
   const int nseg = h / kRouterSeg;
-  const int s_begin = SPLIT ? (int)blockIdx.z : 0;
-  const int s_end = SPLIT ? s_begin + 1 : nseg;
-  constexpr int CH_PER_SEG = kRouterSeg / RL_KC;
-  const int kc0 = s_begin * kRouterSeg, nchunks = (s_end - s_begin) * CH_PER_SEG;
+  const int seg = (int)blockIdx.z;
+  const int kc0 = seg * kRouterSeg;
 
   auto xs_of = [&](int buf) { return sm0 + buf * rl_stage_floats<TM>() * 4; };
   auto ws_of = [&](int buf) { return xs_of(buf) + TT * RL_XP * 4; };
@@ -171,34 +156,23 @@ __global__ void __launch_bounds__(RL_THREADS, 2) router_logits_kernel(const floa
     }
   };
 
-  constexpr bool TOT_SMEM = rl_tot_smem<TM>();
   constexpr int NJP = RL_EPT / 2;
-  float tot[TOT_SMEM ? 1 : TM][RL_EPT];
-  float* tot_s = rl_smem_f + RL_STAGES * rl_stage_floats<TM>();  // TOT_SMEM: [TM * RL_EPT][RL_THREADS]
-  f32x2 acc[TM][NJP];  // experts (2 jp, 2 jp + 1) of the thread's RL_EPT, packed
+  f32x2 acc[TM][NJP];  // experts (2 jp, 2 jp + 1) of the thread's RL_EPT, packed: P_s
 #pragma unroll
-  for (int i = 0; i < TM; ++i) {
-#pragma unroll
-    for (int j = 0; j < RL_EPT; ++j)
-      if (!TOT_SMEM) tot[i][j] = 0.0f;
+  for (int i = 0; i < TM; ++i)
 #pragma unroll
     for (int jp = 0; jp < NJP; ++jp) acc[i][jp] = 0ull;  // (+0.0f, +0.0f)
-  }
-  // tot[i][j] lives in tot_s[(RL_EPT i + j) * RL_THREADS + tid] when TOT_SMEM
-  auto tot_ref = [&](int i, int j) -> float& {
-    return TOT_SMEM ? tot_s[(RL_EPT * i + j) * RL_THREADS + tid] : tot[TOT_SMEM ? 0 : i][j];
-  };
 
 #pragma unroll
   for (int c = 0; c < RL_STAGES - 1; ++c) {
-    if (c < nchunks) load_chunk(c, c);
+    if (c < NCHUNKS) load_chunk(c, c);
     cp_async_commit();
   }
-  for (int c = 0; c < nchunks; ++c) {
+  for (int c = 0; c < NCHUNKS; ++c) {
     const int buf = c % RL_STAGES;
     cp_async_wait<RL_STAGES - 2>();
     __syncthreads();  // chunk c landed for every thread; chunk c - 1's buffer is free
-    if (c + RL_STAGES - 1 < nchunks) load_chunk(c + RL_STAGES - 1, (c + RL_STAGES - 1) % RL_STAGES);
+    if (c + RL_STAGES - 1 < NCHUNKS) load_chunk(c + RL_STAGES - 1, (c + RL_STAGES - 1) % RL_STAGES);
     cp_async_commit();
     const uint32_t xs = xs_of(buf), ws = ws_of(buf);
 #pragma unroll 2
@@ -219,76 +193,184 @@ __global__ void __launch_bounds__(RL_THREADS, 2) router_logits_kernel(const floa
         }
       }
     }
+  }
+  cp_async_wait<0>();
+  float* dst = part + (int64_t)seg * n * e;
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int64_t tok = t0 + TM * ty + i;
+    const int ee = e0 + RL_EPT * tx;
+    if (tok >= n || ee >= e) continue;  // e is a multiple of 4: the thread's 4 experts are whole or absent
+    const float2 a = unpack2(acc[i][0]), b = unpack2(acc[i][1]);
+    *reinterpret_cast<float4*>(dst + tok * e + ee) = make_float4(a.x, a.y, b.x, b.y);
+  }
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  if (tid == 0) s_last = atomicAdd(&arrivals[tile], 1) == nseg - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // this tile's logits = P_0 + P_1 + ... in segment order; p = sigmoid(logit) into part[0]
+  const int64_t ps = n * e;
+  for (int q = tid; q < TT * (RL_EXP / 4); q += RL_THREADS) {
+    const int t = q / (RL_EXP / 4), e4 = q % (RL_EXP / 4);
+    const int64_t tok = t0 + t;
+    const int ee = e0 + 4 * e4;
+    if (tok >= n || ee >= e) continue;
+    const float4* src = reinterpret_cast<const float4*>(part + tok * e + ee);
+    float4 l = __ldcg(src);
+    for (int s0 = 1; s0 < nseg; s0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < nseg) v[u] = __ldcg(src + (int64_t)(s0 + u) * (ps / 4));
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < nseg) {
+          l.x = __fadd_rn(l.x, v[u].x);
+          l.y = __fadd_rn(l.y, v[u].y);
+          l.z = __fadd_rn(l.z, v[u].z);
+          l.w = __fadd_rn(l.w, v[u].w);
+        }
+    }
+    *reinterpret_cast<float4*>(part + tok * e + ee) =
+        make_float4(sigmoid_canonical(l.x), sigmoid_canonical(l.y), sigmoid_canonical(l.z), sigmoid_canonical(l.w));
+  }
+  if (tid == 0) arrivals[tile] = 0;  // re-armed for the next launch on this stream
+}
+
+// ------------------------------------------------------------------------------------------
+// Router logits on wide whole-K tiles (large N): CTA = 256 threads, one CTA per SM, on a (16 TM)
+// token x 128 expert tile. Warp w takes expert half w & 1 and token-row group w >> 1; lane =
+// (tyl, tx) = (lane / 8, lane % 8), token row ty = 4 (w >> 1) + tyl. A thread owns tokens ty + 16 i
+// (i < TM) and experts 4 tx .. 4 tx + 3 and 32 + 4 tx .. 32 + 4 tx + 3 of its half: TM x 8
+// independent fma chains, the segment sums in registers. Against the 64-expert tiles (measured
+// at 8192 tokens: 8.3 shared-memory wavefronts per warp and k, fma pipe 64 % active) each
+// half-warp (the unit a 16-byte shared load is served in) reads two adjacent token rows and 128
+// contiguous weight bytes per load, one wavefront each instead of one and two, for twice the fmas
+// per load; the 68-float x pitch puts adjacent rows 4 banks apart. x [token][k] and wrt
+// [k][expert] arrive in 64-k chunks through a 3-deep cp.async ring (198 KB at TM = 8). Same
+// canonical order as router_logits_split_kernel: per 256-k segment an fma chain from 0, the segment
+// sums added left to right, then p = sigmoid(logit) into probs [n][e].
+// ------------------------------------------------------------------------------------------
+constexpr int RW_EXP = 128, RW_KC = 64, RW_XP = RW_KC + 4, RW_THREADS = 256, RW_STAGES = 3;
+template <int TM>
+constexpr int rw_tok() { return 16 * TM; }
+template <int TM>
+constexpr int rw_stage_floats() { return rw_tok<TM>() * RW_XP + RW_KC * RW_EXP; }
+template <int TM>
+constexpr int rw_smem() { return RW_STAGES * rw_stage_floats<TM>() * 4; }
+static_assert(kRouterSeg % RW_KC == 0, "a chunk lies in one segment");
+
+template <int TM>
+__global__ void __launch_bounds__(RW_THREADS, 1) router_logits_wide_kernel(const float* __restrict__ x,
+                                                                         const float* __restrict__ wrt,
+                                                                         float* __restrict__ probs, int64_t n, int h,
+                                                                         int e, int32_t* __restrict__ zero_counts) {
+  extern __shared__ __align__(16) float rw_smem_f[];
+  pdl_wait();
+  pdl_trigger();
+  if (zero_counts && blockIdx.x == 0 && blockIdx.y == 0)  // route_kernel's counters
+    for (int i = threadIdx.x; i < e; i += RW_THREADS) zero_counts[i] = 0;
+  constexpr int TT = rw_tok<TM>();
+  constexpr int CH_PER_SEG = kRouterSeg / RW_KC;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tx = lane & 7, ty = 4 * (warp >> 1) + (lane >> 3), eh = warp & 1;
+  const int64_t t0 = (int64_t)blockIdx.x * TT;
+  const int e0 = blockIdx.y * RW_EXP;
+  const int nchunks = h / RW_KC;
+  const uint32_t sm0 = smem_u32(rw_smem_f);
+  auto xs_of = [&](int buf) { return sm0 + buf * rw_stage_floats<TM>() * 4; };
+  auto ws_of = [&](int buf) { return xs_of(buf) + TT * RW_XP * 4; };
+  auto load_chunk = [&](int c, int buf) {
+    const int kc = c * RW_KC;
+    const uint32_t xs = xs_of(buf), ws = ws_of(buf);
+#pragma unroll
+    for (int r = 0; r < TT * (RW_KC / 4) / RW_THREADS; ++r) {
+      const int q = tid + r * RW_THREADS, t = q / (RW_KC / 4), k4 = q % (RW_KC / 4);
+      const bool ok = t0 + t < n;
+      cp_async16(xs + (t * RW_XP + 4 * k4) * 4, ok ? x + (t0 + t) * h + kc + 4 * k4 : x, ok);
+    }
+#pragma unroll
+    for (int r = 0; r < (RW_KC * RW_EXP / 4) / RW_THREADS; ++r) {
+      const int q = tid + r * RW_THREADS, k = q / (RW_EXP / 4), e4 = q % (RW_EXP / 4);
+      const bool ok = e0 + 4 * e4 < e;
+      cp_async16(ws + (k * RW_EXP + 4 * e4) * 4, ok ? wrt + (int64_t)(kc + k) * e + e0 + 4 * e4 : wrt, ok);
+    }
+  };
+  static_assert(TT * (RW_KC / 4) % RW_THREADS == 0, "whole x loads per thread");
+
+  // acc[i][j]: experts (4 tx + 2 j, + 1) for j = 0, 1 and (32 + 4 tx + 2 (j - 2), + 1) for j = 2, 3
+  // of the half, packed; tot[i][2 j], tot[i][2 j + 1] their segment sums
+  f32x2 acc[TM][4];
+  float tot[TM][8];
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;  // (+0.0f, +0.0f)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tot[i][j] = 0.0f;
+  }
+#pragma unroll
+  for (int c = 0; c < RW_STAGES - 1; ++c) {
+    if (c < nchunks) load_chunk(c, c);
+    cp_async_commit();
+  }
+  for (int c = 0; c < nchunks; ++c) {
+    const int buf = c % RW_STAGES;
+    cp_async_wait<RW_STAGES - 2>();
+    __syncthreads();  // chunk c landed for every thread; chunk c - 1's buffer is free
+    if (c + RW_STAGES - 1 < nchunks) load_chunk(c + RW_STAGES - 1, (c + RW_STAGES - 1) % RW_STAGES);
+    cp_async_commit();
+    const uint32_t xrow = xs_of(buf) + ty * RW_XP * 4;              // token row ty + 16 i at + 16 i RW_XP floats
+    const uint32_t wcol = ws_of(buf) + (eh * (RW_EXP / 2) + 4 * tx) * 4;  // k row at + k RW_EXP floats
+#pragma unroll 2
+    for (int k4 = 0; k4 < RW_KC / 4; ++k4) {
+      float4 xv[TM];
+#pragma unroll
+      for (int i = 0; i < TM; ++i) xv[i] = lds128f(xrow + (16 * i * RW_XP + 4 * k4) * 4);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t wk = wcol + (4 * k4 + kk) * RW_EXP * 4;
+        f32x2 wp[4];
+        lds2x64(wk, wp[0], wp[1]);
+        lds2x64(wk + 32 * 4, wp[2], wp[3]);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+          const f32x2 xx = dup2(kk == 0 ? xv[i].x : kk == 1 ? xv[i].y : kk == 2 ? xv[i].z : xv[i].w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ffma2(acc[i][j], xx, wp[j]);
+        }
+      }
+    }
     if (((c + 1) % CH_PER_SEG) == 0) {  // end of a segment: fold its partial in order
       const bool first = (c + 1) == CH_PER_SEG;
 #pragma unroll
       for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int jp = 0; jp < NJP; ++jp) {
-          const float2 a = unpack2(acc[i][jp]);
-          float& t0r = tot_ref(i, 2 * jp);
-          float& t1r = tot_ref(i, 2 * jp + 1);
-          t0r = first ? a.x : __fadd_rn(t0r, a.x);
-          t1r = first ? a.y : __fadd_rn(t1r, a.y);
-          acc[i][jp] = 0ull;
+        for (int j = 0; j < 4; ++j) {
+          const float2 a = unpack2(acc[i][j]);
+          tot[i][2 * j] = first ? a.x : __fadd_rn(tot[i][2 * j], a.x);
+          tot[i][2 * j + 1] = first ? a.y : __fadd_rn(tot[i][2 * j + 1], a.y);
+          acc[i][j] = 0ull;
         }
     }
   }
   cp_async_wait<0>();
-  float* dst = part + (SPLIT ? (int64_t)s_begin * n * e : 0);
 #pragma unroll
   for (int i = 0; i < TM; ++i) {
-    const int64_t tok = t0 + TM * ty + i;
+    const int64_t tok = t0 + ty + 16 * i;
     if (tok >= n) continue;
 #pragma unroll
-    for (int j = 0; j < RL_EPT; j += 4) {
-      const int ee = e0 + RL_EPT * tx + j;
-      if (ee >= e) continue;
-      const float v0 = tot_ref(i, j), v1 = tot_ref(i, j + 1), v2 = tot_ref(i, j + 2), v3 = tot_ref(i, j + 3);
-      if constexpr (SPLIT) {
-        *reinterpret_cast<float4*>(dst + tok * e + ee) = make_float4(v0, v1, v2, v3);
-      } else {
-        *reinterpret_cast<float4*>(dst + tok * e + ee) =
-            make_float4(sigmoid_canonical(v0), sigmoid_canonical(v1), sigmoid_canonical(v2), sigmoid_canonical(v3));
-      }
+    for (int g = 0; g < 2; ++g) {
+      const int ee = e0 + eh * (RW_EXP / 2) + 32 * g + 4 * tx;
+      if (ee >= e) continue;  // e is a multiple of 4: the group is whole or absent
+      *reinterpret_cast<float4*>(probs + tok * e + ee) =
+          make_float4(sigmoid_canonical(tot[i][4 * g]), sigmoid_canonical(tot[i][4 * g + 1]),
+                      sigmoid_canonical(tot[i][4 * g + 2]), sigmoid_canonical(tot[i][4 * g + 3]));
     }
-  }
-  if constexpr (SPLIT) {
-    __shared__ int s_last;
-    __threadfence();
-    __syncthreads();
-    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-    if (tid == 0) s_last = atomicAdd(&arrivals[tile], 1) == nseg - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // this tile's logits = P_0 + P_1 + ... in segment order; p = sigmoid(logit) into part[0]
-    const int64_t ps = n * e;
-    for (int q = tid; q < TT * (RL_EXP / 4); q += RL_THREADS) {
-      const int t = q / (RL_EXP / 4), e4 = q % (RL_EXP / 4);
-      const int64_t tok = t0 + t;
-      const int ee = e0 + 4 * e4;
-      if (tok >= n || ee >= e) continue;
-      const float4* src = reinterpret_cast<const float4*>(part + tok * e + ee);
-      float4 l = __ldcg(src);
-      for (int s0 = 1; s0 < nseg; s0 += 8) {
-        float4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (s0 + u < nseg) v[u] = __ldcg(src + (int64_t)(s0 + u) * (ps / 4));
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          if (s0 + u < nseg) {
-            l.x = __fadd_rn(l.x, v[u].x);
-            l.y = __fadd_rn(l.y, v[u].y);
-            l.z = __fadd_rn(l.z, v[u].z);
-            l.w = __fadd_rn(l.w, v[u].w);
-          }
-      }
-      *reinterpret_cast<float4*>(part + tok * e + ee) =
-          make_float4(sigmoid_canonical(l.x), sigmoid_canonical(l.y), sigmoid_canonical(l.z), sigmoid_canonical(l.w));
-    }
-    if (tid == 0) arrivals[tile] = 0;  // re-armed for the next launch on this stream
   }
 }
 
@@ -472,56 +554,62 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
 
 // p = sigmoid(logit) into part[0] ([n][e]); the split path also uses part[1 .. h/256 - 1] for
 // partials and `arrivals` (router_arrivals(n, e) zeroed ints, left zeroed again).
-template <int TM, bool SPLIT>
-static cudaError_t launch_logits(dim3 grid, const float* x, const float* wrt, float* part, int64_t n, int h, int e,
-                                 int32_t* arrivals, int32_t* zero_counts, cudaStream_t st) {
-  auto kern = router_logits_kernel<TM, SPLIT>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rl_smem<TM, SPLIT>());
+template <int TM>
+static cudaError_t launch_logits_split(const float* x, const float* wrt, float* part, int64_t n, int h, int e,
+                                       int32_t* arrivals, int32_t* zero_counts, cudaStream_t st) {
+  auto kern = router_logits_split_kernel<TM>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rl_smem<TM>());
   if (err != cudaSuccess) return err;
-  return launch_pdl(kern, grid, dim3(RL_THREADS), rl_smem<TM, SPLIT>(), st, x, wrt, part, n, h, e, arrivals,
-                    zero_counts);
+  const dim3 grid((unsigned)((n + rl_tok<TM>() - 1) / rl_tok<TM>()), (unsigned)((e + RL_EXP - 1) / RL_EXP),
+                  (unsigned)(h / kRouterSeg));
+  return launch_pdl(kern, grid, dim3(RL_THREADS), rl_smem<TM>(), st, x, wrt, part, n, h, e, arrivals, zero_counts);
+}
+
+template <int TM>
+static cudaError_t launch_logits_wide(const float* x, const float* wrt, float* probs, int64_t n, int h, int e,
+                                      int32_t* zero_counts, cudaStream_t st) {
+  auto kern = router_logits_wide_kernel<TM>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rw_smem<TM>());
+  if (err != cudaSuccess) return err;
+  const dim3 grid((unsigned)((n + rw_tok<TM>() - 1) / rw_tok<TM>()), (unsigned)((e + RW_EXP - 1) / RW_EXP));
+  return launch_pdl(kern, grid, dim3(RW_THREADS), rw_smem<TM>(), st, x, wrt, probs, n, h, e, zero_counts);
 }
 
 cudaError_t launch_router(const float* x, const float* wrt, float* part, int64_t n, int h, int e, RouterPlan plan,
                           int32_t* arrivals, int32_t* zero_counts, cudaStream_t st) {
   if (h % kRouterSeg) return cudaErrorInvalidValue;
-  const unsigned nseg = (unsigned)(h / kRouterSeg);
-  const unsigned gy = (unsigned)((e + RL_EXP - 1) / RL_EXP);
   if ((plan == ROUTER_SPLIT2 || plan == ROUTER_SPLIT8) && !arrivals) return cudaErrorInvalidValue;
   switch (plan) {
     case ROUTER_WHOLE:
-      return launch_logits<8, false>(dim3((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, 1u), x, wrt, part, n, h,
-                                     e, nullptr, zero_counts, st);
+      return launch_logits_wide<8>(x, wrt, part, n, h, e, zero_counts, st);
     case ROUTER_WHOLE7:
-      return launch_logits<7, false>(dim3((unsigned)((n + rl_tok<7>() - 1) / rl_tok<7>()), gy, 1u), x, wrt, part, n, h,
-                                     e, nullptr, zero_counts, st);
+      return launch_logits_wide<7>(x, wrt, part, n, h, e, zero_counts, st);
     case ROUTER_SPLIT8:
-      return launch_logits<8, true>(dim3((unsigned)((n + rl_tok<8>() - 1) / rl_tok<8>()), gy, nseg), x, wrt, part, n, h,
-                                    e, arrivals, zero_counts, st);
+      return launch_logits_split<8>(x, wrt, part, n, h, e, arrivals, zero_counts, st);
     case ROUTER_SPLIT2:
-      return launch_logits<2, true>(dim3((unsigned)((n + rl_tok<2>() - 1) / rl_tok<2>()), gy, nseg), x, wrt, part, n, h,
-                                    e, arrivals, zero_counts, st);
+      return launch_logits_split<2>(x, wrt, part, n, h, e, arrivals, zero_counts, st);
   }
   return cudaErrorInvalidValue;
 }
 
-// Whole-K TM = 8 tiles once they load every SM 1.4 times (a whole-K tile runs ~300 us alone on an
-// SM, ~490 us two to an SM, against ~2.4 us per 32 tokens split by segment); below that, the same
-// tiles split by 256-k segment while those give every SM one; below that, TM = 2 tiles split by
-// segment. Measured on B200 (E = 256, H = 4096; router stage, logits + routing), whole / split
-// 128 / split 32 tokens:
+// Wide whole-K tiles once they give at least every other SM one (a wide tile takes the same time
+// whatever the grid: one per SM); below that, 128-token tiles split by 256-k segment while those
+// give every SM one; below that, 32-token tiles split by segment. Measured on B200 with the
+// 64-expert whole-K tiles (E = 256, H = 4096; router stage, logits + routing), whole / split 128 /
+// split 32 tokens:
 //   256 tokens   293 /  71 /  59 us        2048 tokens  307 / 175 / 220 us
 //   512 tokens   303 /  82 /  86 us        3072 tokens  307 / 230 / 321 us
 //   1024 tokens  304 / 117 / 130 us       4096 tokens  310 / 302 / 436 us
-//   5120 tokens (whole) 515 us, 8192 tokens (whole) 490 us
-// Whole-K tiles of 112 tokens (TM = 7) where they put less work on the busiest SM than 128-token
-// tiles: at 8192 tokens 296 tiles run two per SM, where 256 tiles leave 40 SMs with one.
+// 112-token wide tiles (TM = 7) where they put less work on the busiest SM than 128-token tiles:
+// at 8192 tokens 148 tiles of 112 tokens, one per SM, where 128 of 128 tokens leave 20 SMs idle.
 RouterPlan router_plan(int64_t n, int e, int h, int sms) {
   const int64_t etiles = (e + RL_EXP - 1) / RL_EXP;
+  const int64_t wtiles = (e + RW_EXP - 1) / RW_EXP;
   const int64_t tiles8 = ((n + rl_tok<8>() - 1) / rl_tok<8>()) * etiles;
-  const int64_t tiles7 = ((n + rl_tok<7>() - 1) / rl_tok<7>()) * etiles;
-  if (10 * tiles8 >= 14 * (int64_t)sms)
-    return 7 * ((tiles7 + sms - 1) / sms) < 8 * ((tiles8 + sms - 1) / sms) ? ROUTER_WHOLE7 : ROUTER_WHOLE;
+  const int64_t wide8 = ((n + rw_tok<8>() - 1) / rw_tok<8>()) * wtiles;
+  const int64_t wide7 = ((n + rw_tok<7>() - 1) / rw_tok<7>()) * wtiles;
+  if (2 * wide7 >= (int64_t)sms)
+    return 7 * ((wide7 + sms - 1) / sms) < 8 * ((wide8 + sms - 1) / sms) ? ROUTER_WHOLE7 : ROUTER_WHOLE;
   if (tiles8 * (h / kRouterSeg) >= sms) return ROUTER_SPLIT8;
   return ROUTER_SPLIT2;
 }
