@@ -995,7 +995,11 @@ size_t dmoe_last_error(char* buf, size_t len) {
   return g_last_error.size();
 }
 
-dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmoe_layer** out) {
+// dmoe_create; with `parent` (an expert-parallel layer of the same ranks) the new layer's
+// communicator is split from the parent's instead of initialised from dist->nccl_id, so that
+// one unique id serves every layer of a model.
+static dmoe_status create_layer(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, const dmoe_layer* parent,
+                                dmoe_layer** out) {
   if (!out) return fail(DMOE_ERR_INVALID_ARG, "null output handle");
   *out = nullptr;
   dmoe_status st = validate(d);
@@ -1006,7 +1010,9 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
     if (dist->rank < 0 || dist->rank >= world) return fail(DMOE_ERR_INVALID_ARG, "rank %d of %d", dist->rank, world);
     if (d->n_expert % world) return fail(DMOE_ERR_UNSUPPORTED, "n_expert %lld not divisible by world_size %d",
                                          (long long)d->n_expert, world);
-    if (!dist->nccl_id) return fail(DMOE_ERR_INVALID_ARG, "expert parallelism needs dist->nccl_id");
+    if (!dist->nccl_id && !parent) return fail(DMOE_ERR_INVALID_ARG, "expert parallelism needs dist->nccl_id");
+    if (parent && (!parent->comm || parent->world != world || parent->rank != dist->rank))
+      return fail(DMOE_ERR_INVALID_ARG, "parent layer is not an expert-parallel layer of the same ranks");
     if (!nccl().ok) return fail(DMOE_ERR_NCCL, "NCCL unavailable: %s", nccl().why);
   }
   int ndev = 0;
@@ -1118,19 +1124,35 @@ dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmo
           cudaEventCreateWithFlags(&L->ev_comb[c], cudaEventDisableTiming) != cudaSuccess)
         return bail(fail(DMOE_ERR_CUDA, "event create"));
     // non-blocking communicator: init and every group are polled against the layer's deadline
-    ncclUniqueId id;
-    std::memcpy(&id, dist->nccl_id, sizeof(id));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
-    const ncclResult_t r = nccl().CommInitRankConfig(&L->comm, world, id, L->rank, &cfg);
+    ncclResult_t r;
+    if (parent) {
+      r = nccl().CommSplit(parent->comm, 0, L->rank, &L->comm, &cfg);
+    } else {
+      ncclUniqueId id;
+      std::memcpy(&id, dist->nccl_id, sizeof(id));
+      r = nccl().CommInitRankConfig(&L->comm, world, id, L->rank, &cfg);
+    }
     if (r != ncclSuccess && r != ncclInProgress) {
       L->comm = nullptr;
-      return bail(fail(DMOE_ERR_NCCL, "ncclCommInitRankConfig: %s", nccl().GetErrorString(r)));
+      return bail(fail(DMOE_ERR_NCCL, "%s: %s", parent ? "ncclCommSplit" : "ncclCommInitRankConfig",
+                       nccl().GetErrorString(r)));
     }
     if ((st = nccl_settle(L, r, "communicator init (all ranks must call dmoe_create)")) != DMOE_OK) return bail(st);
   }
   *out = L;
   return DMOE_OK;
+}
+
+dmoe_status dmoe_create(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, dmoe_layer** out) {
+  return create_layer(d, dist, nullptr, out);
+}
+
+dmoe_status dmoe_create_split(const dmoe_layer_desc* d, const dmoe_dist_cfg* dist, const dmoe_layer* parent,
+                              dmoe_layer** out) {
+  if (!parent) return fail(DMOE_ERR_INVALID_ARG, "null parent layer");
+  return create_layer(d, dist, parent, out);
 }
 
 dmoe_status dmoe_nccl_unique_id(void* id128) {

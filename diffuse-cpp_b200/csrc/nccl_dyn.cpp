@@ -24,6 +24,7 @@ const NcclApi& nccl() {
     };
     sym(api.GetUniqueId, "ncclGetUniqueId");
     sym(api.CommInitRankConfig, "ncclCommInitRankConfig");
+    sym(api.CommSplit, "ncclCommSplit");
     sym(api.CommDestroy, "ncclCommDestroy");
     sym(api.CommAbort, "ncclCommAbort");
     sym(api.CommGetAsyncError, "ncclCommGetAsyncError");

@@ -105,6 +105,29 @@ class Stats(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class ModelInfo(ctypes.Structure):
+    _fields_ = [
+        ("n_layer", ctypes.c_int32),
+        ("first_k_dense", ctypes.c_int32),
+        ("n_moe_layers", ctypes.c_int32),
+        ("expert_type", ctypes.c_int32),
+        ("shared_type", ctypes.c_int32),
+        ("norm_topk_prob", ctypes.c_int32),
+        ("routed_scaling", ctypes.c_float),
+        ("n_embd", ctypes.c_int64),
+        ("n_ff_exp", ctypes.c_int64),
+        ("n_ff_shexp", ctypes.c_int64),
+        ("n_expert", ctypes.c_int64),
+        ("n_expert_used", ctypes.c_int64),
+        ("expert_capacity", ctypes.c_int64),
+        ("moe_block_size", ctypes.c_int64),
+        ("moe_bytes", ctypes.c_int64),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
 class DmoeError(RuntimeError):
     def __init__(self, status: int, message: str):
         super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
@@ -151,6 +174,18 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.dmoe_sample_step.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int32, ctypes.c_int32,
                                      ctypes.c_float, P, P, P, P]
     lib.dmoe_sample_step.restype = ctypes.c_int
+    lib.dmoe_create_split.argtypes = [ctypes.POINTER(LayerDesc), ctypes.POINTER(DistCfg), P, ctypes.POINTER(P)]
+    lib.dmoe_create_split.restype = ctypes.c_int
+    lib.dmoe_model_load.argtypes = [ctypes.c_char_p, ctypes.POINTER(DistCfg), ctypes.POINTER(P)]
+    lib.dmoe_model_load.restype = ctypes.c_int
+    lib.dmoe_model_inspect.argtypes = [ctypes.c_char_p, ctypes.POINTER(ModelInfo)]
+    lib.dmoe_model_inspect.restype = ctypes.c_int
+    lib.dmoe_model_get_info.argtypes = [P, ctypes.POINTER(ModelInfo)]
+    lib.dmoe_model_get_info.restype = ctypes.c_int
+    lib.dmoe_model_layer.argtypes = [P, ctypes.c_int32]
+    lib.dmoe_model_layer.restype = P
+    lib.dmoe_model_free.argtypes = [P]
+    lib.dmoe_model_free.restype = None
     _lib = lib
     return lib
 
@@ -217,8 +252,11 @@ class MoELayer:
     """One bound MoE layer (dmoe_create). `tensors` holds the GGUF tensors:
     w_gate/w_up/w_down (uint8 bytes or float16 arrays), sw_*, w_router [E, H] f32, b_router [E] f32 or None."""
 
-    def __init__(self, hp: dict, tensors: dict, dist: Optional[DistCfg] = None):
+    def __init__(self, hp: dict, tensors: dict, dist: Optional[DistCfg] = None, parent: Optional["MoELayer"] = None):
+        """parent: an expert-parallel layer of the same ranks whose communicator this layer's is
+        split from (dmoe_create_split); dist.nccl_id is then not needed."""
         lib = load()
+        self._owner = None
         self._keep = {}
         d = LayerDesc()
         d.n_embd = hp["n_embd"]
@@ -243,9 +281,23 @@ class MoELayer:
         self.hp = dict(hp)
         self.desc = d
         h = ctypes.c_void_p()
-        _check(lib.dmoe_create(ctypes.byref(d), ctypes.byref(dist) if dist is not None else None, ctypes.byref(h)))
+        dp = ctypes.byref(dist) if dist is not None else None
+        if parent is not None:
+            _check(lib.dmoe_create_split(ctypes.byref(d), dp, parent._h, ctypes.byref(h)))
+        else:
+            _check(lib.dmoe_create(ctypes.byref(d), dp, ctypes.byref(h)))
         self._h = h
         self._keep.clear()  # weights are on the device now
+
+    @classmethod
+    def _borrowed(cls, handle: int, hp: dict, owner) -> "MoELayer":
+        """A view of a layer owned by a MoEModel (freed with the model, not by close())."""
+        self = cls.__new__(cls)
+        self._h = ctypes.c_void_p(handle)
+        self.hp = dict(hp)
+        self._keep = {}
+        self._owner = owner
+        return self
 
     def forward(self, x, out=None, route: bool = False, route_only: bool = False, profile: bool = False,
                 stream: Optional[int] = None, deterministic: bool = False):
@@ -309,8 +361,60 @@ class MoELayer:
         return s.as_dict()
 
     def close(self) -> None:
+        if getattr(self, "_owner", None) is not None:  # borrowed from a model
+            self._h = None
+            return
         if getattr(self, "_h", None):
             load().dmoe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def model_inspect(path: str) -> dict:
+    """dmoe_model_inspect: the hyper-parameters and MoE tensor checks of a GGUF model, no device."""
+    info = ModelInfo()
+    _check(load().dmoe_model_inspect(os.fsencode(path), ctypes.byref(info)))
+    return info.as_dict()
+
+
+class MoEModel:
+    """Every MoE layer of a GGUF model bound once (dmoe_model_load; replaces
+    diffuse_model_load_impl, src/diffuse-model.cpp:67-224, for the MoE blocks). `layer(il)` is the
+    MoELayer of block il (None for a dense block); the layers live as long as the model."""
+
+    def __init__(self, path: str, dist: Optional[DistCfg] = None):
+        lib = load()
+        h = ctypes.c_void_p()
+        _check(lib.dmoe_model_load(os.fsencode(path), ctypes.byref(dist) if dist is not None else None,
+                                   ctypes.byref(h)))
+        self._h = h
+        info = ModelInfo()
+        _check(lib.dmoe_model_get_info(self._h, ctypes.byref(info)))
+        self.info = info.as_dict()
+        hp = {k: self.info[k] for k in ("n_embd", "n_ff_exp", "n_ff_shexp", "n_expert", "n_expert_used",
+                                        "expert_capacity", "moe_block_size", "routed_scaling", "norm_topk_prob",
+                                        "expert_type", "shared_type")}
+        self._layers = {}
+        for il in range(self.info["first_k_dense"], self.info["n_layer"]):
+            lh = lib.dmoe_model_layer(self._h, il)
+            if not lh:
+                raise DmoeError(1, f"dmoe_model_layer({il}) returned NULL")
+            self._layers[il] = MoELayer._borrowed(lh, hp, self)
+
+    def layer(self, il: int) -> Optional[MoELayer]:
+        return self._layers.get(il)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            for L in self._layers.values():
+                L._h = None
+            self._layers = {}
+            load().dmoe_model_free(self._h)
             self._h = None
 
     def __del__(self):

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define DMOE_ABI_VERSION 4
+#define DMOE_ABI_VERSION 5
 
 /* Replaces the reference's bool returns + DIFFUSE_DIE/exit(1) (src/diffuse-common.h:22-27,
  * src/diffuse-moe-graph.cpp:325-329). */
@@ -144,6 +144,55 @@ dmoe_status dmoe_create(const dmoe_layer_desc* desc, const dmoe_dist_cfg* dist, 
 /* Writes a fresh 128-byte NCCL unique id for dmoe_dist_cfg.nccl_id (create it on one rank and
  * share it with the others). No counterpart in the reference, which runs on one device. */
 dmoe_status dmoe_nccl_unique_id(void* id128);
+
+/* dmoe_create for a further expert-parallel layer of the same ranks: its communicator is split
+ * from `parent`'s (ncclCommSplit) instead of initialised from dist->nccl_id (which may be NULL),
+ * so one unique id serves all layers of a model. Collective over the parent's ranks; dist gives
+ * this rank's rank / world_size / device / timeout_ms, which must match the parent's. */
+dmoe_status dmoe_create_split(const dmoe_layer_desc* desc, const dmoe_dist_cfg* dist,
+                              const struct dmoe_layer* parent, struct dmoe_layer** out);
+
+/* ---- Whole-model upload from GGUF (replaces diffuse_model_load_impl,
+ * src/diffuse-model.cpp:67-224, for the MoE layers, and the weight offload that
+ * src/diffuse-backend.h:104-118 leaves undone). dmoe_model_load maps the file, reads the
+ * hyper-parameters as the reference does (keys "<prefix>.<name>" with prefix "diffuse", "qwen2"
+ * or "llama": block_count, embedding_length, expert_count, expert_used_count,
+ * expert_shared_count, expert_feed_forward_length, first_k_dense_replace, routed_scaling_factor
+ * (default 1), norm_topk_prob (1), expert_capacity (48), moe_block_size (block_length, else 32)),
+ * and binds every MoE layer il >= first_k_dense_replace from its tensors blk.<il>.moe_gate.weight,
+ * moe_gate_bias.weight (optional), moe_experts_{gate,up,down}.weight and, with shared experts,
+ * moe_shared_{gate,up,down}.weight: each is copied to the device once and the file is unmapped
+ * before the call returns. The model must be "llada2_moe" (diffuse.model_type; the reference's
+ * default without that key unless the architecture is qwen2 or llama). dist: as for dmoe_create
+ * (collective); the first MoE layer's communicator comes from dist->nccl_id and the others are
+ * split from it. */
+typedef struct dmoe_model_info {
+  int32_t n_layer;          /* block_count */
+  int32_t first_k_dense;    /* layers [0, first_k_dense) are dense: no MoE layer */
+  int32_t n_moe_layers;     /* n_layer - first_k_dense */
+  int32_t expert_type;      /* DMOE_TYPE_* of the expert stacks, and of the shared expert */
+  int32_t shared_type;
+  int32_t norm_topk_prob;
+  float routed_scaling;
+  int64_t n_embd;
+  int64_t n_ff_exp;
+  int64_t n_ff_shexp;       /* 0 without shared experts */
+  int64_t n_expert;
+  int64_t n_expert_used;
+  int64_t expert_capacity;
+  int64_t moe_block_size;
+  int64_t moe_bytes;        /* bytes of MoE tensors read from the file, over all layers */
+} dmoe_model_info;
+
+struct dmoe_model;
+dmoe_status dmoe_model_load(const char* path, const dmoe_dist_cfg* dist, struct dmoe_model** out);
+/* The checks of dmoe_model_load without a device: reads the file's hyper-parameters and every MoE
+ * tensor's name, shape and type into info; nothing is copied. */
+dmoe_status dmoe_model_inspect(const char* path, dmoe_model_info* info);
+dmoe_status dmoe_model_get_info(const struct dmoe_model* model, dmoe_model_info* info);
+/* The bound layer of block il, or NULL for a dense block or il out of range; owned by the model. */
+struct dmoe_layer* dmoe_model_layer(struct dmoe_model* model, int32_t il);
+void dmoe_model_free(struct dmoe_model* model);
 
 /* Hot-expert replication for skewed expert-parallel loads. No counterpart in the reference,
  * which runs on one device. Collective: every rank calls it with the same arguments, between

@@ -31,7 +31,24 @@ def test_every_declared_symbol_is_exported():
 
 
 def test_abi_version():
-    assert dm.load().dmoe_abi_version() == 4
+    assert dm.load().dmoe_abi_version() == 5
+
+
+def test_model_and_split_argument_errors(tmp_path):
+    """dmoe_model_load / dmoe_create_split refuse null arguments and unreadable files with status
+    codes; the model accessors tolerate a null model."""
+    lib = dm.load()
+    h = ctypes.c_void_p()
+    assert lib.dmoe_model_load(None, None, ctypes.byref(h)) == 1
+    assert lib.dmoe_model_load(os.fsencode(str(tmp_path / "missing.gguf")), None, ctypes.byref(h)) == 1
+    assert "cannot open" in dm.last_error() and not h.value
+    assert lib.dmoe_model_load(b"x", None, None) == 1
+    assert lib.dmoe_model_get_info(None, None) == 1
+    assert lib.dmoe_model_layer(None, 0) is None
+    lib.dmoe_model_free(None)
+    d = dm.LayerDesc()
+    assert lib.dmoe_create_split(ctypes.byref(d), None, None, ctypes.byref(h)) == 1
+    assert "null parent" in dm.last_error()
 
 
 def test_replicate_experts_argument_errors():

@@ -223,3 +223,55 @@ def test_ep_rank_without_tokens():
         status, errs = ret[r]
         assert status == "ok", (r, errs)
         assert max(errs) <= 2e-3, (r, errs)
+
+
+def model_worker(rank, path, nccl_id, ret):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        from model_gguf import ModelSpec
+
+        ms = ModelSpec(n_layer=3, first_k=1)
+        model = dm.MoEModel(path, dist=dm.dist_cfg(rank, WORLD, rank, nccl_id, timeout_ms=60000))
+        x = synth.make_input(64, ms.H, 600 + rank)
+        res = {}
+        for il in range(ms.first_k, ms.n_layer):
+            hp = ms.layer_spec(il).hparams()
+            t = synth.make_layer(ms.layer_spec(il))
+            out, (idx, w, _) = model.layer(il).forward(x, route=True)
+            r_out, r_idx, r_w, _, _ = oracle.layer(hp, t, x)
+            err = float(np.linalg.norm(out.astype(np.float64) - r_out) / np.linalg.norm(r_out))
+            res[il] = (bool(np.array_equal(idx, r_idx)), err, int(model.layer(il).stats()["ep_rows_sent"]))
+        model.close()
+        ret[rank] = res
+    except Exception as e:  # reported to the parent
+        ret[rank] = ("error", repr(e))
+
+
+@pytest.mark.gpu
+@needs2
+def test_ep_model_load(tmp_path):
+    """A GGUF model loaded on both ranks (dmoe_model_load with dist): the first MoE layer's
+    communicator from the unique id, the next one's split from it; every layer exchanges rows
+    and matches the oracle."""
+    import torch.multiprocessing as mp
+
+    from model_gguf import ModelSpec, write_model
+
+    path = str(tmp_path / "m.gguf")
+    write_model(path, ModelSpec(n_layer=3, first_k=1))
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    nccl_id = dm.nccl_unique_id()
+    procs = [ctx.Process(target=model_worker, args=(r, path, nccl_id, ret)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(600)
+        assert p.exitcode == 0
+    for r in range(WORLD):
+        res = ret[r]
+        assert isinstance(res, dict), res
+        for il, (ok, err, sent) in res.items():
+            assert ok, (r, il)
+            assert err <= 2e-3, (r, il, err)
+            assert sent > 0, (r, il)
