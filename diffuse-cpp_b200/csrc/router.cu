@@ -385,6 +385,12 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
 }
 
+// monotonic map of a float onto unsigned order (-0 below +0; every non-NaN float above 0)
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 constexpr int RT_THREADS = 1024;
 
 __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
@@ -440,31 +446,42 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
   }
   __syncthreads();
   if (a.use_block) {
-    // block max by the fold m = s_t + relu(m - s_t), t = 1 .. blk-1 in order (:223-229)
+    // block max by the fold m = s_t + relu(m - s_t), t = 1 .. blk-1 in order (:223-229); the
+    // scores are loaded 8 tokens ahead of the dependent chain
+    auto fold = [](float m, float st) {
+      const float d = __fsub_rn(m, st);
+      return __fadd_rn(st, d > 0.0f ? d : 0.0f);
+    };
     for (int ee = tid; ee < E; ee += RT_THREADS) {
       float m = ss[ee];
-      for (int t = 1; t < tpb; ++t) {
-        const float st = ss[t * E + ee];
-        const float d = __fsub_rn(m, st);
-        const float rl = d > 0.0f ? d : 0.0f;
-        m = __fadd_rn(st, rl);
+      int t = 1;
+      for (; t + 8 <= tpb; t += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = ss[(t + u) * E + ee];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) m = fold(m, v[u]);
       }
+      for (; t < tpb; ++t) m = fold(m, ss[t * E + ee]);
       bmax[ee] = m;
     }
     __syncthreads();
     // thr = value at position cap-1 of bmax sorted descending (:231-236): rank counts split
     // over `nsp` threads per expert
+    // (chunks of whole float4s: E is a multiple of 4, so a float4 below E lies inside)
     const int nsp = max(1, RT_THREADS / E);
-    const int chunk = (E + nsp - 1) / nsp;
+    const int chunk = ((E + nsp - 1) / nsp + 3) & ~3;
     if (tid < nsp * E) {
       const int ee = tid % E, q = tid / E;
       const float v = bmax[ee];
       int gt = 0, eq = 0;
       const int j1 = min(E, (q + 1) * chunk);
-      for (int j = q * chunk; j < j1; ++j) {
-        const float u = bmax[j];
-        gt += u > v;
-        eq += u == v;
+      const float4* b4 = reinterpret_cast<const float4*>(bmax);
+#pragma unroll 4
+      for (int j = q * chunk; j < j1; j += 4) {
+        const float4 u = b4[j >> 2];
+        gt += (u.x > v) + (u.y > v) + (u.z > v) + (u.w > v);
+        eq += (u.x == v) + (u.y == v) + (u.z == v) + (u.w == v);
       }
       atomicAdd(&gt_s[ee], gt);
       atomicAdd(&eq_s[ee], eq);
@@ -484,14 +501,22 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
       addv[ee] = keep ? 0.0f : -1e30f;
     }
     __syncthreads();
-    for (int i = tid; i < cnt; i += RT_THREADS) ss[i] = __fadd_rn(ss[i], addv[i % E]);
+    if (RT_THREADS % E == 0) {  // a thread's scores are all of one expert
+      const float av = addv[tid % E];
+      for (int i = tid; i < cnt; i += RT_THREADS) ss[i] = __fadd_rn(ss[i], av);
+    } else {
+      for (int i = tid; i < cnt; i += RT_THREADS) ss[i] = __fadd_rn(ss[i], addv[i % E]);
+    }
     __syncthreads();
   }
   // per-token top-k (:252): one warp per token, ties to the lower expert id. Each lane keeps
   // the best of its candidates (experts lane, lane + 32, ...); every round the warp reduces the
-  // lanes' bests, and only the winning lane marks its candidate taken and rescans.
+  // lanes' bests, and only the winning lane marks its candidate taken and rescans. With E <= 256
+  // a lane's (at most 8) candidates sit in registers, so a rescan reads no shared memory.
+  constexpr int RC = 8;
   const int warp = tid >> 5, lane = tid & 31;
   const int ncand = (E - lane + 31) / 32;  // this lane's candidates (<= 32)
+  const bool regs = E <= 32 * RC;
   const int per = (tpb + a.tok_split - 1) / a.tok_split;
   const int tb = part * per, te = min(ntok, tb + per);
   for (int t = tb + warp; t < te; t += RT_THREADS / 32) {
@@ -499,9 +524,23 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
     uint32_t taken = 0;
     float hv = 0.0f;
     int hi = -1;
+    float cv[RC];
+#pragma unroll
+    for (int j = 0; j < RC; ++j) cv[j] = (regs && j < ncand) ? st[j * 32 + lane] : 0.0f;
     auto rescan = [&]() {
       hv = 0.0f;
       hi = -1;
+      if (regs) {
+#pragma unroll
+        for (int j = 0; j < RC; ++j) {
+          const int ee = j * 32 + lane;
+          if (j < ncand && !(taken & (1u << j)) && (hi < 0 || better(cv[j], ee, hv, hi))) {
+            hv = cv[j];
+            hi = ee;
+          }
+        }
+        return;
+      }
       for (int j = 0; j < ncand; ++j) {
         if (taken & (1u << j)) continue;
         const int ee = j * 32 + lane;
@@ -515,17 +554,13 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(RouteArgs a) {
     rescan();
     int sel_idx = -1;  // lane s < top_k keeps slot s
     for (int s = 0; s < a.top_k; ++s) {
-      float bv = hv;
-      int bi = hi;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi >= 0 && (bi < 0 || better(ov, oi, bv, bi))) {
-          bv = ov;
-          bi = oi;
-        }
-      }
+      // the warp's best (value, then lowest id): the largest order key (keys order floats as the
+      // comparisons do; NaN scores, whose routing the reference leaves unspecified too, aside),
+      // then the lowest id among the lanes holding it; 0 = no candidate left
+      const uint32_t key = hi >= 0 ? order_key(hv) : 0u;
+      const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+      const uint32_t bu = __reduce_min_sync(0xffffffffu, (hi >= 0 && key == kmax) ? (uint32_t)hi : 0xffffffffu);
+      const int bi = kmax ? (int)bu : -1;
       if (lane == s) sel_idx = bi;
       if (bi >= 0 && (bi & 31) == lane) {
         taken |= 1u << (bi >> 5);

@@ -91,12 +91,13 @@ def test_c3_q4k_1_and_8_blocks():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("plan", [0, 1, 2, 3])
-@pytest.mark.parametrize("E", [64, 160])
+@pytest.mark.parametrize("E", [64, 160, 320])
 def test_router_plans_bit_exact(plan, E, monkeypatch):
     """Each router logits plan (whole-K 128- or 112-token tiles of 128 experts; per-segment
     partials of 32- or 128-token tiles of 64 experts summed in segment order) gives the oracle's
     routing bit for bit, on a ragged last token tile; E = 64 leaves the upper half of a 128-expert
-    tile empty, E = 160 fills the second tile a quarter."""
+    tile empty, E = 160 fills the second tile a quarter; E = 320 takes the routing kernel's
+    shared-memory top-k (more than 8 candidates per lane)."""
     monkeypatch.setenv("DMOE_ROUTER_SPLIT", str(plan))
     spec = tiny(dm.TYPE_Q8_0, H=1024, E=E, top_k=6, cap=20, seed=23)
     check_layer(spec, 608)  # 19 routing blocks: the last 128-token tile holds 96 tokens
