@@ -218,6 +218,51 @@ def bench_sampler(dev, stream, peaks_hbm: float, no_cpu: bool) -> dict:
     return sampler
 
 
+def bench_c5(layer_tensors: dict, spec, steps: int = 8) -> dict:
+    """a LLaDA2.2-flash-shaped 32-block model (block 0 dense SwiGLU I = 9216,
+    blocks 1-31 the c3 MoE layer, hidden 4096, 32 / 4 heads of 128, vocab 157184) with random
+    weights generates 256 tokens after a 480-token random prompt in 32-token blocks, 8 denoising
+    steps per block committing the 4 most confident positions (and any at >= 0.95). The MoE layers
+    and the sampler step are this library's kernels; attention, dense projections and lm_head
+    are torch library calls on bf16 weights. The 31 MoE layers are 31 device copies of one
+    synthetic q4_K weight set. `value` = generated tokens / wall time of the generation (the
+    model's forwards, sampler steps and the per-step host read of the commit count) with the
+    key/value cache and each step's forward replayed from a CUDA graph; the cache without graphs
+    and the reference's whole-window recompute at every step are timed beside it."""
+    import torch
+
+    import diffuse_moe as dm
+    import llada2
+
+    cfg = llada2.LLaDA2Config()
+    moe = {il: dm.MoELayer(spec.hparams(), layer_tensors) for il in range(cfg.first_k_dense, cfg.n_layer)}
+    w = llada2.LLaDA2Model.random_weights(cfg, seed=11)
+    w["output"][cfg.mask_token_id] = 0.0
+    model = llada2.LLaDA2Model(cfg, w, moe, dtype=torch.bfloat16)
+    del w
+    prompt = np.random.default_rng(5).integers(0, cfg.mask_token_id, size=480)
+    out = {"workload": "config 5: 32 blocks (1 dense + 31 MoE c3 q4_K), 480-token prompt + 256 generated, "
+                       "32-token blocks, 8 steps committing top-4 (threshold 0.95)", "generated": 256}
+    model.reserve(480 + 256)
+    for name, cache, graphs in (("kv_cache_graphs", True, True), ("kv_cache", True, False),
+                                ("recompute_window", False, False)):
+        # warm-up on the same prompt (the same prefill; the graphs are captured here)
+        llada2.generate(model, prompt, 64, steps=steps, threshold=0.95, use_cache=cache, graphs=graphs)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        seq, nf = llada2.generate(model, prompt, 256, steps=steps, threshold=0.95, use_cache=cache, graphs=graphs)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        out[name] = {"seconds": dt, "tokens_per_s": 256 / dt, "forwards": nf, "ms_per_forward": dt / nf * 1e3,
+                     "masked_left": int(np.sum(seq == cfg.mask_token_id))}
+    out["value"] = out["kv_cache_graphs"]["tokens_per_s"]
+    out["unit"] = "generated tokens/s"
+    model.drop_graphs()
+    for L in moe.values():
+        L.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -228,6 +273,7 @@ def main():
     ap.add_argument("--config", default="c3")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-c5", action="store_true", help="skip the full-model (config 5) generation leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -470,6 +516,14 @@ def main():
         except Exception as ex:  # noqa: BLE001
             sampler = {"error": f"{type(ex).__name__}: {ex}"}
 
+    # ---- config 5: the whole model's generation around these layers (secondary, like the sampler)
+    c5 = None
+    if rank == 0 and world == 1 and not args.no_c5 and args.config == "c3":
+        try:
+            c5 = bench_c5(t, spec)
+        except Exception as ex:  # noqa: BLE001
+            c5 = {"error": f"{type(ex).__name__}: {ex}"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, sample, _, _ = run_cpu_reference(spec, t, n_tok, 3, 1, budget_s=20.0)
@@ -490,6 +544,8 @@ def main():
             line["configs"] = configs
         if sampler is not None:
             line["sampler"] = sampler
+        if c5 is not None:
+            line["c5"] = c5
         print(json.dumps(line))
     layer.close()
     if world > 1:
