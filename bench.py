@@ -1,5 +1,5 @@
-"""Benchmark of the block-routed MoE layer (BASELINE metric: MoE-layer tokens/s and HBM GB/s,
-256 experts, top-8, q4_K, at 1/2/4/8 B200).
+"""Benchmark of the block-routed MoE layer (the metric of BASELINE.json: MoE-layer tokens/s and
+HBM GB/s, 256 experts, top-8, q4_K, at 1/2/4/8 B200).
 
 Workload: the LLaDA2.2-flash-shaped layer (hidden 4096, 256 routed SwiGLU experts of width 1024,
 one shared expert of width 1024, fp32 router, capacity 48 per 32-token block, top-8, x2.5) with
@@ -12,7 +12,7 @@ One step = one dmoe_forward over the GPU's 8192 tokens. `value` is device-reside
 D2H of out inside the timed region). With N > 1 (torchrun) the layer is expert-parallel: rank r
 holds experts [256 r / N, 256 (r + 1) / N), routes its own 256 blocks and exchanges token rows and
 partial outputs with the other ranks over NCCL inside every step (weak scaling: 8192 tokens per
-GPU); the timing is the max over ranks. N > 1 also reports `c4`: the BASELINE c4 workload
+GPU); the timing is the max over ranks. N > 1 also reports `c4`: the c4 workload of BASELINE.json
 (16384 tokens in total, Zipf-skewed expert bias, expert-parallel over the N GPUs), as a strong-
 scaling measurement with per-rank expert loads.
 
@@ -22,9 +22,10 @@ restatement (weights in their GGUF blocks, activations rounded to Q8_K, AVX2 int
 OpenMP on every host thread), each step a sample of the workload's blocks sized to fit a few
 minutes (the whole step when it fits).
 
-Besides the headline, the line carries `configs`: device-resident lines for BASELINE configs c1
-(small layer, F16 weights, 1 block) and c2 (small layer, q8_0 weights, 64 blocks), each with its
-HBM GB/s and fraction of the layer roofline.
+Besides the headline, the line carries `configs`: device-resident lines for the configs c1
+(small layer, F16 weights, 1 block) and c2 (small layer, q8_0 weights, 64 blocks) of BASELINE.json,
+each with its HBM GB/s and fraction of the layer roofline; and `c5`: the whole-model generation of
+config 5 around these layers (bench_c5).
 """
 from __future__ import annotations
 
@@ -219,7 +220,7 @@ def bench_sampler(dev, stream, peaks_hbm: float, no_cpu: bool) -> dict:
 
 
 def bench_c5(layer_tensors: dict, spec, steps: int = 8) -> dict:
-    """BASELINE config 5: a LLaDA2.2-flash-shaped 32-block model (block 0 dense SwiGLU I = 9216,
+    """Config 5 of BASELINE.json: a LLaDA2.2-flash-shaped 32-block model (block 0 dense SwiGLU I = 9216,
     blocks 1-31 the c3 MoE layer, hidden 4096, 32 / 4 heads of 128, vocab 157184) with random
     weights generates 256 tokens after a 480-token random prompt in 32-token blocks, 8 denoising
     steps per block committing the 4 most confident positions (and any at >= 0.95). The MoE layers
@@ -405,7 +406,7 @@ def main():
                           "stages_ms": prof, "token_tile": st["token_tile"], "ksplit": [st["ksplit_gateup"],
                                                                                         st["ksplit_down"]]})
 
-    # ---- BASELINE configs c1 (F16, 1 block) and c2 (q8_0, 64 blocks) of the small layer shape
+    # ---- configs c1 (F16, 1 block) and c2 (q8_0, 64 blocks) of the small layer shape
     configs = None
     if not args.no_sweep and world == 1:
         configs = {}
