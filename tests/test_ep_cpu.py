@@ -1,5 +1,5 @@
 """Expert parallelism on CPU: the decomposition the library's EP path implements (ep.cu), run
-with real collectives (torch.distributed gloo, world size 2) around the oracle.
+with real collectives (torch.distributed gloo, world size 2 and 4) around the oracle.
 
 Each rank routes its own whole token blocks, sends one row per (token, owning rank) with its
 slot list (rank-local expert id or -1, gate weight), computes the weighted partial rows of its
@@ -19,9 +19,6 @@ import torch.multiprocessing as mp
 import diffuse_moe as dm
 import oracle
 import synth
-
-WORLD = 2
-
 
 def free_port() -> int:
     s = socket.socket()
@@ -51,21 +48,22 @@ def local_tensors(t, hp, rank, world, hot=()):
 
 def exchange(objs_by_dest):
     """all-to-all of python objects over gloo: returns the list received from each source."""
-    gathered = [None] * WORLD
+    world = dist.get_world_size()
+    gathered = [None] * world
     dist.all_gather_object(gathered, objs_by_dest)
     me = dist.get_rank()
-    return [gathered[src][me] for src in range(WORLD)]
+    return [gathered[src][me] for src in range(world)]
 
 
-def worker(rank, port, ret, chunks=1, hot=()):
+def worker(rank, world, port, ret, chunks=1, hot=()):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         sp = spec()
         hp = sp.hparams()
         t = synth.make_layer(sp)
-        E, K, el = hp["n_expert"], hp["n_expert_used"], hp["n_expert"] // WORLD
+        E, K, el = hp["n_expert"], hp["n_expert_used"], hp["n_expert"] // world
         x = synth.make_input(64, sp.H, 100 + rank)  # this rank's 2 blocks
         # local routing (no communication)
         lg = oracle.logits(x, t["w_router"])
@@ -79,7 +77,7 @@ def worker(rank, port, ret, chunks=1, hot=()):
         def dest(e):
             return (rank, el + hot.index(e)) if e in hot else (e // el, e - (e // el) * el)
 
-        sends = [[] for _ in range(WORLD)]
+        sends = [[] for _ in range(world)]
         for tok in range(x.shape[0]):
             ds = [dest(int(e)) for e in idx[tok]]
             for d in sorted({r for r, _ in ds}):
@@ -87,18 +85,18 @@ def worker(rank, port, ret, chunks=1, hot=()):
                 sends[d].append((tok, x[tok], slots))
         # the exchange pipelined over chunks of this rank's tokens (the library's ep_chunks): every
         # chunk's dispatch, then every chunk's partials and combine, in chunk order on all ranks
-        lt = local_tensors(t, hp, rank, WORLD, hot)
+        lt = local_tensors(t, hp, rank, world, hot)
         hp_l = dict(hp, n_expert=el + len(hot), n_ff_shexp=0)
         n = x.shape[0]
         bounds = [(n * c // chunks, n * (c + 1) // chunks) for c in range(chunks)]
-        in_chunk = [[[(tok, xr_, sl) for tok, xr_, sl in sends[d] if lo <= tok < hi] for d in range(WORLD)]
+        in_chunk = [[[(tok, xr_, sl) for tok, xr_, sl in sends[d] if lo <= tok < hi] for d in range(world)]
                     for lo, hi in bounds]
-        recvs = [exchange([[(x_row, slots) for _, x_row, slots in cs[d]] for d in range(WORLD)]) for cs in in_chunk]
+        recvs = [exchange([[(x_row, slots) for _, x_row, slots in cs[d]] for d in range(world)]) for cs in in_chunk]
         shared = oracle.experts(hp, t, x, np.zeros_like(idx), np.zeros_like(w), mode=0)
         acc = np.zeros_like(shared)
         for c, recv in enumerate(recvs):
             parts = []  # partial rows with only this rank's experts
-            for src in range(WORLD):
+            for src in range(world):
                 rows = recv[src]
                 if not rows:
                     parts.append(np.zeros((0, sp.H), np.float32))
@@ -109,7 +107,7 @@ def worker(rank, port, ret, chunks=1, hot=()):
                 parts.append(oracle.experts(hp_l, lt, xr, li, lw, mode=0))
             back = exchange(parts)
             # owner: partials of the chunk's tokens in rank order
-            for d in range(WORLD):
+            for d in range(world):
                 for j, (tok, _, _) in enumerate(in_chunk[c][d]):
                     acc[tok] += back[d][j]
         out = acc + shared
@@ -121,13 +119,14 @@ def worker(rank, port, ret, chunks=1, hot=()):
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("chunks,hot", [(1, ()), (3, ()), (2, (0, 5, 6))])
-def test_expert_parallel_decomposition_gloo(chunks, hot):
+@pytest.mark.parametrize("world,chunks,hot", [(2, 1, ()), (2, 3, ()), (2, 2, (0, 5, 6)), (4, 1, ()),
+                                              (4, 2, (1, 2, 7))])
+def test_expert_parallel_decomposition_gloo(world, chunks, hot):
     """chunks: the exchange pipelined over chunks of each rank's tokens; hot: experts replicated
-    on every rank (one owned by each rank and one more), whose slots are computed locally."""
+    on every rank (owned by different ranks), whose slots are computed locally."""
     ctx = mp.get_context("spawn")
     ret = ctx.Manager().dict()
-    mp.start_processes(worker, args=(free_port(), ret, chunks, hot), nprocs=WORLD, start_method="spawn")
-    assert sorted(ret.keys()) == list(range(WORLD))
-    for r in range(WORLD):
+    mp.start_processes(worker, args=(world, free_port(), ret, chunks, hot), nprocs=world, start_method="spawn")
+    assert sorted(ret.keys()) == list(range(world))
+    for r in range(world):
         assert ret[r] < 1e-5, (r, ret[r])
