@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <exception>
 #include <string>
 #include <vector>
 
@@ -100,6 +101,10 @@ dmoe_status read_info(const GgufFile& f, dmoe_model_info& in) {
   if ((s = get_f32(f, "routed_scaling_factor", 1.0f, scale)) != DMOE_OK) return s;
   if (n_exp == 0 || n_used == 0) return mfail(DMOE_ERR_INVALID_ARG, "expert_count / expert_used_count missing or 0");
   if (first_k > n_layer) return mfail(DMOE_ERR_INVALID_ARG, "first_k_dense_replace %u > block_count %u", first_k, n_layer);
+  // every MoE block needs at least four tensors of its own: a block count beyond the file's
+  // tensor count is corrupt (and would size the layer table from garbage)
+  if ((uint64_t)(n_layer - first_k) * 4 > f.n_tensors())
+    return mfail(DMOE_ERR_INVALID_ARG, "block_count %u with %zu tensors in the file", n_layer, f.n_tensors());
   in = dmoe_model_info{};
   in.n_layer = (int32_t)n_layer;
   in.first_k_dense = (int32_t)first_k;
@@ -230,12 +235,16 @@ extern "C" {
 
 dmoe_status dmoe_model_inspect(const char* path, dmoe_model_info* info) {
   if (!info) return mfail(DMOE_ERR_INVALID_ARG, "null info");
-  GgufFile f;
-  dmoe_model_info in{};
-  std::vector<dmoe_layer_desc> descs;
-  const dmoe_status s = open_and_scan(path, f, in, descs);
-  if (s == DMOE_OK) *info = in;
-  return s;
+  try {
+    GgufFile f;
+    dmoe_model_info in{};
+    std::vector<dmoe_layer_desc> descs;
+    const dmoe_status s = open_and_scan(path, f, in, descs);
+    if (s == DMOE_OK) *info = in;
+    return s;
+  } catch (const std::exception& e) {  // host allocation failure while reading the file
+    return mfail(DMOE_ERR_OOM, "reading %s: %s", path, e.what());
+  }
 }
 
 dmoe_status dmoe_model_load(const char* path, const dmoe_dist_cfg* dist, dmoe_model** out) {
@@ -244,7 +253,12 @@ dmoe_status dmoe_model_load(const char* path, const dmoe_dist_cfg* dist, dmoe_mo
   GgufFile f;
   dmoe_model_info in{};
   std::vector<dmoe_layer_desc> descs;
-  dmoe_status s = open_and_scan(path, f, in, descs);
+  dmoe_status s;
+  try {
+    s = open_and_scan(path, f, in, descs);
+  } catch (const std::exception& e) {  // host allocation failure while reading the file
+    return mfail(DMOE_ERR_OOM, "reading %s: %s", path, e.what());
+  }
   if (s != DMOE_OK) return s;
   dmoe_model* m = new dmoe_model();
   m->info = in;

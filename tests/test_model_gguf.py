@@ -115,3 +115,10 @@ def test_corrupt_files(tmp_path):
     expect_error(q, 1, "implausible")
     expect_error(str(tmp_path / "none.gguf"), 1, "cannot open")
     assert not os.path.exists(str(tmp_path / "none.gguf"))
+
+
+def test_implausible_block_count(tmp_path):
+    """A block count the file's tensors cannot hold is refused before any table is sized from it."""
+    p = str(tmp_path / "m.gguf")
+    write_model(p, ModelSpec(n_layer=2), keys={"block_count": 4000000})
+    expect_error(p, 1, "block_count 4000000 with")
