@@ -450,7 +450,9 @@ def main():
                 "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms}
     t_roof = max(B / (peaks_hbm * 1e9), F / (peaks["bf16_tflops"] * 1e12))
     layer_roof = {"bytes": B, "flops": F, "hbm_gbs": B / (ms / 1e3) / 1e9, "tflops": F / (ms / 1e3) / 1e12,
-                  "frac": t_roof / (ms / 1e3), "peak_source": peaks["source"]}
+                  "frac": t_roof / (ms / 1e3), "peak_source": peaks["source"],
+                  # the same bound with the 8 TB/s HBM3e specification instead of the measured copy rate
+                  "frac_hbm_spec_8tbs": max(B / 8.0e12, F / (peaks["bf16_tflops"] * 1e12)) / (ms / 1e3)}
 
     # ---- c4 (N > 1): 16384 tokens in total, Zipf-skewed bias, expert-parallel (strong scaling)
     c4 = None
@@ -487,9 +489,15 @@ def main():
             dist.all_gather(allv, loads)
             return [int(v.item()) for v in allv]
 
+        rows4 = rows_per_rank(st4)
+        # NVLink term of the expert-parallel roofline: every received row arrives as fp16 (2 B per
+        # hidden unit) and returns as an fp32 partial (4 B), against the measured 770 GB/s peer copy
+        # per direction (the busiest rank bounds the step; its own rows are included)
+        nvl = max(rows4) * sp4.H * 6
         c4 = {"tokens": 16384, "ms_per_step": ms4, "tokens_per_s": 16384 / (ms4 / 1e3),
-              "rows_received_per_rank": rows_per_rank(st4), "scaling": "strong",
-              "bias": "0.5 log Zipf(1.1) over a random expert permutation"}
+              "rows_received_per_rank": rows4, "scaling": "strong",
+              "bias": "0.5 log Zipf(1.1) over a random expert permutation",
+              "nvlink_bytes_busiest_rank": nvl, "nvlink_bound_ms": nvl / 770e9 * 1e3}
         # the same workload with the busiest experts of the last forward replicated on every rank
         # (dmoe_replicate_experts): their (token, slot) pairs stay on the token's rank
         n_hot = 16
