@@ -29,3 +29,51 @@ def test_transfer_schedule():
     assert llada2.transfer_schedule(32, 0) == []
     for L, s in ((32, 3), (32, 7), (30, 4)):
         assert sum(llada2.transfer_schedule(L, s)) == L
+
+
+class OracleMoE:
+    """Stand-in for a diffuse_moe.MoELayer on the CPU: the layer oracle (float64 accumulation) on
+    the same tensors, written into `out` like dmoe_forward."""
+
+    def __init__(self, hp, t):
+        self.hp, self.t = hp, t
+
+    def forward(self, h, out=None, stream=None):
+        import oracle
+
+        out.copy_(torch.from_numpy(oracle.layer(self.hp, self.t, h.numpy())[0].astype(np.float32)))
+        return out
+
+
+def cpu_model():
+    import diffuse_moe as dm
+    import synth
+
+    cfg = llada2.LLaDA2Config(n_layer=3, n_embd=256, n_head=4, n_head_kv=2, head_dim=64, rotary_dim=32, n_ff=512,
+                              first_k_dense=1, n_vocab=300, rope_base=10000.0, mask_token_id=299)
+    w = llada2.LLaDA2Model.random_weights(cfg, seed=5, device="cpu")
+    moe, specs = {}, {}
+    for il in range(cfg.first_k_dense, cfg.n_layer):
+        sp = synth.LayerSpec(H=256, I=256, Is=256, E=16, top_k=4, cap=6, blk=32, expert_type=dm.TYPE_Q8_0,
+                             seed=60 + il)
+        t = synth.make_layer(sp)
+        moe[il] = OracleMoE(sp.hparams(), t)
+        specs[il] = (sp.hparams(), t)
+    return cfg, w, llada2.LLaDA2Model(cfg, w, moe, dtype=torch.float32, device="cpu"), specs
+
+
+def test_model_forward_on_cpu_matches_restatement():
+    """The model's host code (block-causal mask over the cache, GQA head mapping, RoPE positions,
+    QK norm, residuals) on the CPU with the MoE layers replaced by the oracle: the logits of a
+    3-block window match the float64 restatement; the last block's logits from the cache match
+    the whole window."""
+    cfg, w, model, specs = cpu_model()
+    tokens = np.random.default_rng(1).integers(0, cfg.n_vocab - 1, size=96)
+    got = model.forward(torch.as_tensor(tokens), 0).numpy()
+    wn = {k: v.float().numpy() for k, v in w.items()}
+    ref = llada2_ref.forward(cfg, wn, specs, tokens)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-4
+    cache = model.new_cache(96)
+    model.forward(torch.as_tensor(tokens[:64]), 0, cache, commit=64)
+    part = model.forward(torch.as_tensor(tokens[64:]), 64, cache).numpy()
+    assert np.linalg.norm(part - got[64:]) / np.linalg.norm(got[64:]) <= 1e-5
