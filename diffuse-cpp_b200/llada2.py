@@ -264,7 +264,7 @@ def transfer_schedule(block_length: int, steps: int) -> list:
 
 
 def generate(model: LLaDA2Model, prompt: np.ndarray, n_generate: int, steps: int = 8, threshold: float = 0.95,
-             use_cache: bool = True, graphs: bool = False) -> tuple:
+             use_cache: bool = True, graphs: bool = False, sampler=None) -> tuple:
     """Greedy low-confidence block diffusion (generate_block_diffusion, diffuse-sampler.cpp:100-258):
     blocks tile from position 0; the prompt's whole blocks are prefilled; each later block runs up
     to `steps` denoising steps, each committing the schedule's count of its most confident masked
@@ -272,7 +272,9 @@ def generate(model: LLaDA2Model, prompt: np.ndarray, n_generate: int, steps: int
     sequence (int32 numpy) and the number of forwards. use_cache=False recomputes the whole window
     at every step, as the reference does. graphs=True (with the cache) replays each step's forward
     from a CUDA graph, one per window size, kept by the model over the cache of model.reserve()
-    (captured at first use, after the prefill)."""
+    (captured at first use, after the prefill). sampler: the step function with the signature of
+    diffuse_moe.sample_step (default: this library's GPU kernel)."""
+    sample = dm.sample_step if sampler is None else sampler
     c = model.cfg
     L = c.block_length
     prompt_len = len(prompt)
@@ -312,6 +314,6 @@ def generate(model: LLaDA2Model, prompt: np.ndarray, n_generate: int, steps: int
                 logits = model.forward(seq[: b0 + L].long(), 0)[b0:]
             forwards += 1
             blk_seq = seq[b0: b0 + L]
-            dm.sample_step(logits.contiguous(), blk_seq, c.mask_token_id, sched[step], threshold, token, prob, ncom)
+            sample(logits.contiguous(), blk_seq, c.mask_token_id, sched[step], threshold, token, prob, ncom)
             remaining -= int(ncom.item())
     return seq.cpu().numpy(), forwards

@@ -77,3 +77,29 @@ def test_model_forward_on_cpu_matches_restatement():
     model.forward(torch.as_tensor(tokens[:64]), 0, cache, commit=64)
     part = model.forward(torch.as_tensor(tokens[64:]), 64, cache).numpy()
     assert np.linalg.norm(part - got[64:]) / np.linalg.norm(got[64:]) <= 1e-5
+
+
+def oracle_sampler(logits, seq, mask_id, n_transfer, threshold, token, prob, n_committed):
+    """diffuse_moe.sample_step's contract on CPU tensors, through the oracle's restatement."""
+    import oracle
+
+    tok, pr, s, nc = oracle.sample_step(logits.numpy(), seq.numpy(), mask_id, n_transfer, threshold)
+    seq.copy_(torch.from_numpy(s))
+    token.copy_(torch.from_numpy(tok))
+    prob.copy_(torch.from_numpy(pr))
+    n_committed.fill_(nc)
+
+
+def test_generation_loop_on_cpu_cache_equals_recompute():
+    """The block-diffusion loop (prefill, per-block steps, the previous block entering the cache in
+    the next block's first step, the remaining-mask count) on the CPU with the oracle's MoE layers
+    and sampler: the cached run commits the same tokens as the whole-window recompute, one forward
+    more (the prefill)."""
+    cfg, w, model, _ = cpu_model()
+    w["output"][cfg.mask_token_id] = 0.0
+    model.w["output"][cfg.mask_token_id] = 0.0
+    prompt = np.random.default_rng(3).integers(0, cfg.n_vocab - 1, size=70)
+    seq_c, nf_c = llada2.generate(model, prompt, 40, steps=4, threshold=0.95, use_cache=True, sampler=oracle_sampler)
+    seq_r, nf_r = llada2.generate(model, prompt, 40, steps=4, threshold=0.95, use_cache=False, sampler=oracle_sampler)
+    assert np.array_equal(seq_c, seq_r) and nf_c == nf_r + 1
+    assert np.array_equal(seq_c[:70], prompt) and not np.any(seq_c == cfg.mask_token_id)
