@@ -44,10 +44,10 @@ def _stack(t: np.ndarray, E: int) -> np.ndarray:
 
 
 def write_model(path: str, ms: ModelSpec, *, drop=(), override=None, keys=None, model_type="llada2_moe",
-                alignment=None, omit=()) -> dict:
+                alignment=None, omit=(), extra=None) -> dict:
     """Writes the model; returns {il: tensors} of its MoE blocks. drop: tensor names to leave out;
     override: {tensor name: array (and raw type)} to replace; keys: extra / replaced u32 keys;
-    omit: key names (without the prefix) to leave out."""
+    omit: key names (without the prefix) to leave out; extra(writer): adds further metadata."""
     override = override or {}
     w = GGUFWriter(path, "diffuse")
     if alignment is not None:
@@ -66,6 +66,8 @@ def write_model(path: str, ms: ModelSpec, *, drop=(), override=None, keys=None, 
     w.add_float32("diffuse.attention.layer_norm_rms_epsilon", 1e-6)
     if model_type is not None:
         w.add_string("diffuse.model_type", model_type)
+    if extra is not None:
+        extra(w)
     rng = np.random.default_rng(ms.seed)
 
     def put(name, arr, raw=None):

@@ -122,3 +122,25 @@ def test_implausible_block_count(tmp_path):
     p = str(tmp_path / "m.gguf")
     write_model(p, ModelSpec(n_layer=2), keys={"block_count": 4000000})
     expect_error(p, 1, "block_count 4000000 with")
+
+
+def test_real_file_metadata(tmp_path):
+    """A file carrying what the reference converter writes besides the layers
+    (tools/convert-llada2-fast.py:144-173): string, bool, string-array and int-array keys (the
+    tokenizer's token list, types and merges), plus u64 / f64 / i32 keys; the reader skips them."""
+    p = str(tmp_path / "m.gguf")
+
+    def tokenizer(w):
+        w.add_string("tokenizer.ggml.model", "gpt2")
+        w.add_token_list([f"tok{i}" for i in range(3000)] + ["", "éè", "x" * 300])
+        w.add_token_types([1] * 3003)
+        w.add_token_merges(["a b", "c d"])
+        w.add_bool("tokenizer.ggml.add_bos_token", False)
+        w.add_uint64("diffuse.some_u64", 1 << 40)
+        w.add_float64("diffuse.some_f64", 0.5)
+        w.add_int32("diffuse.some_i32", -7)
+        w.add_string("tokenizer.chat_template", "{{ messages }}")
+
+    layers = write_model(p, ModelSpec(n_layer=2), extra=tokenizer)
+    info = dm.model_inspect(p)
+    assert info["n_moe_layers"] == 1 and info["moe_bytes"] == moe_bytes(layers)
