@@ -1005,6 +1005,8 @@ static dmoe_status create_layer(const dmoe_layer_desc* d, const dmoe_dist_cfg* d
   dmoe_status st = validate(d);
   if (st != DMOE_OK) return st;
   const int world = dist ? std::max(1, dist->world_size) : 1;
+  if (parent && world <= 1)
+    return fail(DMOE_ERR_INVALID_ARG, "a split communicator needs an expert-parallel dist (world_size > 1)");
   if (world > 1) {
     if (world > kMaxRanks) return fail(DMOE_ERR_UNSUPPORTED, "world_size %d > %d", world, kMaxRanks);
     if (dist->rank < 0 || dist->rank >= world) return fail(DMOE_ERR_INVALID_ARG, "rank %d of %d", dist->rank, world);

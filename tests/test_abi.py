@@ -5,6 +5,7 @@ import glob
 import os
 import re
 
+import numpy as np
 import pytest
 
 import diffuse_moe as dm
@@ -49,6 +50,19 @@ def test_model_and_split_argument_errors(tmp_path):
     d = dm.LayerDesc()
     assert lib.dmoe_create_split(ctypes.byref(d), None, None, ctypes.byref(h)) == 1
     assert "null parent" in dm.last_error()
+    # a valid descriptor but no expert-parallel config: refused before the parent is touched
+    import synth
+
+    sp = synth.LayerSpec(H=256, I=256, Is=256, E=16, top_k=4, cap=6, blk=32, expert_type=dm.TYPE_Q8_0, seed=1)
+    t = synth.make_layer(sp)
+    keep = {k: np.ascontiguousarray(v) for k, v in t.items() if v is not None}
+    d = dm.LayerDesc(n_embd=256, n_ff_exp=256, n_ff_shexp=256, n_expert=16, n_expert_used=4, expert_capacity=6,
+                     moe_block_size=32, routed_scaling=2.5, norm_topk_prob=1, expert_type=dm.TYPE_Q8_0,
+                     shared_type=dm.TYPE_Q8_0)
+    for k, v in keep.items():
+        setattr(d, k, v.ctypes.data)
+    assert lib.dmoe_create_split(ctypes.byref(d), None, ctypes.c_void_p(8), ctypes.byref(h)) == 1
+    assert "needs an expert-parallel dist" in dm.last_error()
 
 
 def test_replicate_experts_argument_errors():
